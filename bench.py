@@ -1,0 +1,518 @@
+#!/usr/bin/env python3
+"""Benchmark of the int4-dequant GEMM/GEMV (+ fused LoRA) hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|prefill|lora|mlp70b|tiny]
+
+Prints ONE JSON line on rank 0.
+
+Default workload = BASELINE configs[1], the decode GEMV sweep: X[M x 4096]
+fp32 ~ N(0,1) for M in {1, 2, 4, 8}, W int4 [4096 x 4096] group 32, scales
+U[0.005, 0.02].  One step = the sweep over L = 24 distinct device copies of W
+(a 24-layer decode pass, 1.02 GB of algorithmic bytes, > 2x the 126 MB L2, so
+every launch streams its weights from HBM).  Steps are CUDA-graph replays of
+the library's own launches.  Metric: algorithmic HBM bytes (packed W + scales
++ X + Y) per second, whole job.  N > 1 runs N independent replicas (the decode
+path is "replicas only"; scaling "weak").
+
+Other workloads (secondary figures, also attached to the default line at N=1):
+prefill = configs[2] (2048 x 4096 x 11008), lora = configs[3] (512 x 4096 x
+4096, r=16, alpha=32), tiny = configs[0]; mlp70b = configs[4] N-sharded over
+the ranks with an NCCL all-gather of Y (run it under torchrun).
+
+--impl reference times the reference's own CPU implementation
+(cpu_reference of vulkan-runtime/tests/test_q4gemm.cpp:102-119, compiled from
+the reference sources into oracle/_ref/) on the host cores, same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import math
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "int4 GEMV HBM GB/s (decode), GEMM TFLOP/s (prefill), % roofline, 1–8 GPU"
+DECODE_LAYERS = 24
+DECODE_SWEEP = (1, 2, 4, 8)
+
+# ncu DRAM traffic (read + write bytes per launch) of the dominant kernel,
+# from the capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC_PER_LAUNCH = {
+    "decode": None,
+}
+
+
+def load_package():
+    if "spaceslug_b200" in sys.modules:
+        return sys.modules["spaceslug_b200"]
+    root = ROOT / "spaceslug-main_b200"
+    spec = importlib.util.spec_from_file_location("spaceslug_b200", root / "__init__.py",
+                                                  submodule_search_locations=[str(root)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["spaceslug_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def decode_bytes(m: int, k: int = 4096, n: int = 4096) -> int:
+    """Algorithmic bytes of one GEMV launch: packed W + scales + X + Y."""
+    return k * n // 2 + n * (k // 32) * 4 + m * k * 4 + m * n * 4
+
+
+# ------------------------------------------------------------- distributed --
+class Dist:
+    def __init__(self, gpus: int) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if gpus > 1 and self.world == 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+
+    def init(self, backend: str = "nccl") -> None:
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local) if backend == "nccl" else None)
+            self.pg = dist
+
+    def barrier(self) -> None:
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.proc = None
+        self.gpu = gpu_index
+        self.path = None
+
+    def start(self) -> None:
+        exe = shutil.which("nvidia-smi")
+        if not exe:
+            return
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.fh = open(self.path, "w")
+        self.proc = subprocess.Popen([exe, f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits", "-lms", "200"],
+                                     stdout=self.fh, stderr=subprocess.DEVNULL)
+
+    def stop(self) -> dict | None:
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------- CPU baselines --
+def cpu_reference_decode(seconds: float, threads: int) -> dict:
+    """Time the reference's cpu_reference on the decode sweep (one weight matrix)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle.oracle import Oracle, PreparedReference, Reference, cpu_count  # test-infra: CPU baseline only
+    pkg = load_package()
+    from spaceslug_b200 import synth
+    cfg = synth.CONFIGS["decode"]
+    w_kn, _, scales = synth.make_weights(cfg.k, cfg.n, cfg.scale_lo, cfg.scale_hi, 0)
+    threads = max(1, min(threads, cpu_count()))
+    parts = threads
+    while cfg.n % parts:
+        parts -= 1
+    kind = "reference" if Reference.available() else "port"
+    probs = []
+    if kind == "reference":
+        ref = Reference()
+        for m in DECODE_SWEEP:
+            probs.append(PreparedReference(ref, synth.make_x(m, cfg.k, m), w_kn, scales, parts))
+        run = lambda: [p.run(parts) for p in probs]  # noqa: E731
+    else:
+        orc = Oracle()
+        xs = [synth.make_x(m, cfg.k, m) for m in DECODE_SWEEP]
+        run = lambda: [orc.gemm(x, w_kn, scales) for x in xs]  # noqa: E731
+    per_sweep = sum(decode_bytes(m) for m in DECODE_SWEEP)
+    run()  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    for p in probs:
+        p.close()
+    return {"value": per_sweep * reps / el / 1e9, "unit": "GB/s", "cores": parts if kind == "reference" else 1,
+            "kind": kind, "sample": f"{reps} full decode sweeps (M=1,2,4,8; K=N=4096) on one weight matrix, "
+                                    f"{el:.1f} s, N split into {parts} column shard(s)"}
+
+
+def run_reference_arm(args, dist: Dist) -> None:
+    if dist.rank != 0:
+        return
+    sys.path.insert(0, str(ROOT))
+    from oracle.oracle import PreparedReference, Reference, cpu_count  # reference arm: CPU only
+    pkg = load_package()
+    from spaceslug_b200 import synth
+    if args.workload != "decode":
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the decode workload"}))
+        return
+    if not Reference.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libq4ref.so was not built"}))
+        return
+    cfg = synth.CONFIGS["decode"]
+    w_kn, _, scales = synth.make_weights(cfg.k, cfg.n, cfg.scale_lo, cfg.scale_hi, 0)
+    threads = cpu_count()
+    parts = threads
+    while cfg.n % parts:
+        parts -= 1
+    ref = Reference()
+    probs = [PreparedReference(ref, synth.make_x(m, cfg.k, m), w_kn, scales, parts) for m in DECODE_SWEEP]
+    step = lambda: [p.run(parts) for p in probs]  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    per_step = sum(decode_bytes(m) for m in DECODE_SWEEP)
+    value = per_step * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "decode GEMV sweep M=1,2,4,8; K=N=4096 (BASELINE configs[1])",
+                   "step": "one sweep on one weight matrix", "parallelism": f"{parts} host threads"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": parts, "kind": "reference",
+                         "sample": f"{args.steps} sweeps, N split into {parts} column shards"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    for p in probs:
+        p.close()
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------ GPU helpers --
+def l2_flush_buffer(torch, dev):
+    return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+
+def time_graph_replays(torch, stream, graphs, steps: int, flush=None):
+    """Replays `graphs` (list) `steps` times; returns per-graph total ms."""
+    starts = [[torch.cuda.Event(enable_timing=True) for _ in graphs] for _ in range(steps)]
+    ends = [[torch.cuda.Event(enable_timing=True) for _ in graphs] for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for s in range(steps):
+            for i, g in enumerate(graphs):
+                if flush is not None:
+                    flush.zero_()
+                starts[s][i].record(stream)
+                g.replay()
+                ends[s][i].record(stream)
+    stream.synchronize()
+    return [sum(starts[s][i].elapsed_time(ends[s][i]) for s in range(steps)) for i in range(len(graphs))]
+
+
+def capture(torch, stream, fn):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+# ------------------------------------------------------------ GPU workloads --
+def decode_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
+    dev = torch.device("cuda", dist.local)
+    cfg = synth.CONFIGS["decode"]
+    w_kn, packed, scales = synth.make_weights(cfg.k, cfg.n, cfg.scale_lo, cfg.scale_hi, seed=dist.rank)
+    layers = [session.weights(packed, scales, cfg.k, cfg.n, device=dist.local) for _ in range(DECODE_LAYERS)]
+    xs = {m: torch.from_numpy(synth.make_x(m, cfg.k, seed=m)).to(dev) for m in DECODE_SWEEP}
+    ys = {m: torch.empty((m, cfg.n), dtype=torch.float32, device=dev) for m in DECODE_SWEEP}
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+
+    def sweep_m(m):
+        def f():
+            for w in layers:
+                w.run(xs[m].data_ptr(), ys[m].data_ptr(), m, sp)
+        return f
+
+    for m in DECODE_SWEEP:  # eager warm-up (context, attributes)
+        sweep_m(m)()
+    stream.synchronize()
+    n0 = session.launch_count()
+    graphs = [capture(torch, stream, sweep_m(m)) for m in DECODE_SWEEP]
+    launches_per_step = session.launch_count() - n0
+    for _ in range(args.warmup):
+        time_graph_replays(torch, stream, graphs, 1)
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dist.local)).split(",")[0])
+                          if os.environ.get("CUDA_VISIBLE_DEVICES", "").isdigit() else dist.local)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    per_graph = time_graph_replays(torch, stream, graphs, args.steps)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    clk = clocks.stop()
+    total_ms = dist.max(sum(per_graph))
+    per_step_bytes = DECODE_LAYERS * sum(decode_bytes(m) for m in DECODE_SWEEP)
+    value = per_step_bytes * args.steps * dist.world / (total_ms * 1e-3) / 1e9
+    per_m = {}
+    for m, ms in zip(DECODE_SWEEP, per_graph):
+        gbs = DECODE_LAYERS * decode_bytes(m) * args.steps / (ms * 1e-3) / 1e9
+        per_m[str(m)] = {"GB/s": round(gbs, 1), "us_per_launch": round(ms * 1e3 / args.steps / DECODE_LAYERS, 3),
+                         "frac": round(gbs / peaks["hbm_gbs"], 4)}
+    achieved = per_step_bytes * args.steps / (sum(per_graph) * 1e-3) / 1e9
+    avg_launch_bytes = per_step_bytes / (DECODE_LAYERS * len(DECODE_SWEEP))
+
+    # e2e through the C-ABI with host buffers (pinned): per step, every layer
+    # call copies X in and Y out (spaceslug_q4_weights_run_host, synchronous).
+    xh = {m: torch.from_numpy(synth.make_x(m, cfg.k, seed=m)).pin_memory() for m in DECODE_SWEEP}
+    yh = {m: torch.empty((m, cfg.n), dtype=torch.float32).pin_memory() for m in DECODE_SWEEP}
+    run_host = session.raw("spaceslug_q4_weights_run_host")
+    import ctypes
+    fp = ctypes.POINTER(ctypes.c_float)
+
+    def e2e_step():
+        for m in DECODE_SWEEP:
+            xp = ctypes.cast(xh[m].data_ptr(), fp)
+            yp = ctypes.cast(yh[m].data_ptr(), fp)
+            for w in layers:
+                if run_host(w.handle, xp, yp, m) != 0:
+                    raise RuntimeError("run_host failed")
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_step()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = dist.max(time.perf_counter() - t0)
+    e2e_value = per_step_bytes * e2e_steps * dist.world / e2e_s / 1e9
+    h2d = DECODE_LAYERS * sum(m * cfg.k * 4 for m in DECODE_SWEEP)
+    d2h = DECODE_LAYERS * sum(m * cfg.n * 4 for m in DECODE_SWEEP)
+    for w in layers:
+        w.close()
+    traffic = NCU_TRAFFIC_PER_LAUNCH.get("decode")
+    return {
+        "value": value, "ms_per_step": total_ms / args.steps, "clocks": clk, "per_m": per_m,
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": avg_launch_bytes,
+                     "peak_source": peaks["source"], "kernel": "q4_gemv_kernel"},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "spaceslug_q4_weights_run_host (pinned host X/Y, resident weights)"},
+    }
+
+
+def gemm_gpu(args, dist: Dist, torch, session, synth, peaks, name: str, steps: int | None = None) -> dict:
+    """prefill / lora / tiny: one handle run per step, L2 flushed between steps."""
+    dev = torch.device("cuda", dist.local)
+    cfg = synth.CONFIGS[name]
+    inp = synth.make_inputs(cfg)
+    h = session.weights(inp.packed, inp.scales, cfg.k, cfg.n, device=dist.local)
+    if cfg.rank:
+        h.set_lora(inp.lora_a, inp.lora_b, cfg.alpha)
+    x = torch.from_numpy(inp.x).to(dev)
+    y = torch.empty((cfg.m, cfg.n), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    fn = lambda: h.run(x.data_ptr(), y.data_ptr(), cfg.m, stream.cuda_stream)  # noqa: E731
+    fn()
+    stream.synchronize()
+    n0 = session.launch_count()
+    g = capture(torch, stream, fn)
+    launches = session.launch_count() - n0
+    flush = l2_flush_buffer(torch, dev)
+    steps = steps or args.steps
+    time_graph_replays(torch, stream, [g], max(3, args.warmup), flush)
+    ms = time_graph_replays(torch, stream, [g], steps, flush)[0] / steps
+    flops = 2.0 * cfg.m * cfg.n * cfg.k
+    tflops = flops / (ms * 1e-3) / 1e12
+    out = {"TFLOP/s": round(tflops, 1), "ms": round(ms, 4), "frac_of_bf16_peak": round(tflops / peaks["bf16_tflops"], 4),
+           "flops": flops, "launches_per_step": launches, "shape": [cfg.m, cfg.k, cfg.n]}
+    if cfg.rank:
+        out["lora_flops_excluded"] = 2.0 * cfg.m * cfg.k * cfg.rank + 2.0 * cfg.m * cfg.rank * cfg.n
+    h.close()
+    del flush
+    return out
+
+
+def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
+    """columns of W sharded over the ranks, NCCL all-gather of Y."""
+    from spaceslug_b200 import sharding
+    dev = torch.device("cuda", dist.local)
+    cfg = synth.CONFIGS["mlp70b"]
+    w_kn, packed, scales = synth.make_weights(cfg.k, cfg.n, cfg.scale_lo, cfg.scale_hi, 0)
+    del w_kn
+    c0, c1 = sharding.shard_columns(cfg.n, dist.world, dist.rank)
+    h = session.weights(packed, scales, cfg.k, cfg.n, c0, c1, device=dist.local)
+    x = torch.from_numpy(synth.make_x(cfg.m, cfg.k, 0)).to(dev)
+    ys = torch.empty((cfg.m, c1 - c0), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    gemm = lambda: h.run(x.data_ptr(), ys.data_ptr(), cfg.m, stream.cuda_stream)  # noqa: E731
+    gemm()
+    stream.synchronize()
+    flush = l2_flush_buffer(torch, dev)
+    steps = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(steps + args.warmup)]
+    dist.barrier()
+    for i in range(steps + args.warmup):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            ev[i][0].record(stream)
+            gemm()
+            ev[i][1].record(stream)
+            y = sharding.allgather_columns(ys, cfg.n, dist.pg, stream=stream) if dist.world > 1 else ys
+            ev[i][2].record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    g_ms = sum(ev[i][0].elapsed_time(ev[i][1]) for i in range(args.warmup, steps + args.warmup)) / steps
+    t_ms = sum(ev[i][0].elapsed_time(ev[i][2]) for i in range(args.warmup, steps + args.warmup)) / steps
+    g_ms, t_ms = dist.max(g_ms), dist.max(t_ms)
+    flops = 2.0 * cfg.m * cfg.n * cfg.k
+    h.close()
+    return {"value": flops / (t_ms * 1e-3) / 1e12, "gemm_only_tflops": flops / (g_ms * 1e-3) / 1e12,
+            "ms_per_step": t_ms, "gemm_ms": g_ms, "allgather_ms": t_ms - g_ms,
+            "per_gpu_frac_gemm": flops / dist.world / (g_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+            "y_shape": list(y.shape)}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill", "lora", "tiny", "mlp70b"], default="decode")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the prefill/lora figures")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        run_reference_arm(args, dist)
+        return
+
+    import torch
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dist.init("nccl")
+    torch.cuda.set_device(dist.local)
+    load_package()
+    from spaceslug_b200 import backend, synth
+    session = backend.BackendSession()
+    session._native()  # fail loudly when the library is missing
+    peaks = measured_peaks()
+    line = {"metric": METRIC, "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "vs_baseline": None, "data": "synthetic"}
+
+    if args.workload == "decode":
+        r = decode_gpu(args, dist, torch, session, synth, peaks)
+        line.update({"value": r["value"], "unit": "GB/s", "ms_per_step": r["ms_per_step"], "scaling": "weak",
+                     "dtype": "f32",
+                     "config": {"workload": "decode GEMV sweep M=1,2,4,8; K=N=4096 int4 g32 (BASELINE configs[1])",
+                                "layers_per_step": DECODE_LAYERS, "global_batch": list(DECODE_SWEEP),
+                                "l2": "inputs larger than L2: 24 distinct weight copies, "
+                                      f"{DECODE_LAYERS * sum(decode_bytes(m) for m in DECODE_SWEEP) / 1e9:.2f} GB per step",
+                                "parallelism": f"{dist.world} replica(s)"},
+                     "per_m": r["per_m"], "roofline": r["roofline"], "e2e": r["e2e"],
+                     "gpu_launches": r["gpu_launches"], "clocks": r["clocks"]})
+        if dist.world == 1 and not args.no_secondary:
+            sec = {}
+            for name in ("prefill", "lora"):
+                try:
+                    sec[name] = gemm_gpu(args, dist, torch, session, synth, peaks, name, steps=10)
+                except Exception as exc:  # report, do not hide
+                    sec[name] = {"error": str(exc)}
+            line["secondary"] = sec
+        if dist.rank == 0 and dist.world == 1:
+            line["cpu_baseline"] = cpu_reference_decode(args.cpu_seconds, threads=1)
+    elif args.workload == "mlp70b":
+        r = mlp70b_gpu(args, dist, torch, session, synth, peaks)
+        line.update({"value": r["value"], "unit": "TFLOP/s", "ms_per_step": r["ms_per_step"], "scaling": "strong",
+                     "dtype": "f16 MMA / f32 accumulate",
+                     "config": {"workload": "70B MLP int4 GEMM 4096x8192x28672, N-sharded + NCCL all-gather "
+                                            "(BASELINE configs[4])", "parallelism": f"N-shard x{dist.world}",
+                                "l2": "L2 flushed (256 MB write) before every step"},
+                     "detail": r})
+    else:
+        r = gemm_gpu(args, dist, torch, session, synth, peaks, args.workload)
+        line.update({"value": r["TFLOP/s"], "unit": "TFLOP/s", "ms_per_step": r["ms"], "scaling": "weak",
+                     "dtype": "f16 MMA / f32 accumulate",
+                     "config": {"workload": args.workload, "l2": "L2 flushed (256 MB write) before every step",
+                                "parallelism": "single GPU"},
+                     "detail": r})
+    if dist.rank == 0:
+        print(json.dumps(line))
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

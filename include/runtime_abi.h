@@ -1,0 +1,137 @@
+/*
+ * Spaceslug native runtime C-ABI, B200 (sm_100a) build.
+ *
+ * Extends the reference's native/runtime_abi.h (which declares only
+ * spaceslug_vector_add) with the int4-dequant GEMM/GEMV + LoRA hot path.  All
+ * entry points follow the reference ABI conventions of
+ * vulkan-runtime/src/api/lora_delta_api.h:5-13 and sgemm_api.h:5-9:
+ *   - extern "C", int return code:
+ *       0 ok,
+ *       1 invalid arguments (checked before any device work),
+ *       2 runtime failure (CUDA error; the reference returns 2 for Vulkan
+ *         failures, lora_delta_api.cpp:84),
+ *       3 a kernel wait exceeded its time limit (new: the kernels bound every
+ *         spin-wait and report instead of hanging);
+ *   - plain pointers and sizes, row-major fp32 activations;
+ *   - host-pointer entry points are synchronous (they return after the result
+ *     is back in host memory), like the reference's;
+ *   - no exception ever crosses the ABI.
+ * Entry points ending in _device take device pointers and a cudaStream_t
+ * passed as void* (NULL = legacy default stream) and are asynchronous.
+ *
+ * Weight layout ("reference layout", vulkan-runtime/shaders/q4gemm.comp:7-19):
+ *   int4 v in [-8, 7] stored as the nibble (v & 0xF); the byte for (k, n) is
+ *   pb = n*(K/2) + k/2, even k in the low nibble; bytes are packed 4 per
+ *   little-endian uint32 word (K*N/8 words); one fp32 scale per (32-k group,
+ *   column) at scales[n*(K/32) + k/32]; w(k, n) = float(v) * scale.
+ *
+ * Shapes: any M >= 1 and N >= 1; K must be a positive multiple of 32.
+ * Device pointers for x, packed and y must be 16-byte aligned.
+ *
+ * Thread safety: distinct calls may run concurrently from different host
+ * threads; one weights handle must not be used by two threads at once.
+ */
+#ifndef SPACESLUG_RUNTIME_ABI_H
+#define SPACESLUG_RUNTIME_ABI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPACESLUG_OK 0
+#define SPACESLUG_INVALID_ARGUMENT 1
+#define SPACESLUG_RUNTIME_FAILURE 2
+#define SPACESLUG_TIMEOUT 3
+
+/* Unchanged from the reference: native/runtime_abi.h:6 / runtime_abi.cpp:3-7
+ * (host CPU; returns 1 on a null pointer). */
+int spaceslug_vector_add(const float* left, const float* right, float* output, size_t count);
+
+/* Replaces vulkan-runtime/src/api/lora_delta_api.h:8-13 with the same
+ * signature, limits and semantics: Y[M,64] = X[M,64] * A[64,R] * B[R,64],
+ * fp32 row-major host buffers, 1 <= m <= 128, 1 <= rank <= 8, no alpha/rank
+ * scale inside (callers pre-scale B, python/spaceslug/backend.py:666). */
+int spaceslug_lora_delta(const float* x, const float* a, const float* b, float* y, uint32_t m, uint32_t rank);
+
+/* Host packer: logical int4 w_kn[k*N + n] in [-8, 7] -> reference layout
+ * (K*N/8 words).  Replaces pack_q4 of vulkan-runtime/tests/test_q4gemm.cpp:84-99
+ * (and bench/bench_q4gemm.cpp:118-133).  Runs on the host CPU, no GPU needed.
+ * Returns 1 for null pointers, k % 32 != 0 or n == 0.  Values outside [-8, 7]
+ * are stored as (v & 0xF), exactly like the reference. */
+int spaceslug_q4_pack(const int8_t* w_kn, uint32_t k, uint32_t n, uint32_t* packed_out);
+
+/* Device packer (same contract, device pointers, asynchronous on `stream`). */
+int spaceslug_q4_pack_device(const int8_t* w_kn, uint32_t k, uint32_t n, uint32_t* packed_out, void* stream);
+
+/* Dequantised weights w_kn[k*N + n] = float(v) * scale in fp32 (one rounding),
+ * bit-exact with the reference's dequant (vulkan-runtime/shaders/q4gemm.comp:104-122).
+ * Host pointers, synchronous; a debug/check export. */
+int spaceslug_q4_dequant(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n, float* w_kn_out);
+int spaceslug_q4_dequant_device(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n, float* w_kn_out,
+                                void* stream);
+
+/* Y[M x N] = X[M x K] * dequant(W), fp32 in and out, host pointers,
+ * synchronous.  The int4 GEMM of vulkan-runtime/shaders/q4gemm.comp (driven by
+ * tests/test_q4gemm.cpp:159-425 and bench/bench_q4gemm.cpp:142-396; the
+ * reference exports no C symbol for it).  M <= 8 runs the fp32 GEMV, larger M
+ * the tcgen05 tensor-core GEMM. */
+int spaceslug_q4gemm(const float* x, const uint32_t* packed, const float* scales, float* y, uint32_t m, uint32_t n,
+                     uint32_t k);
+
+/* As spaceslug_q4gemm plus the fused LoRA term:
+ *   Y = X * dequant(W) + (alpha / rank) * (X * A) * B,
+ * A [K x rank], B [rank x N] fp32 row-major (python/spaceslug/lora.py:21-23
+ * defines delta = (alpha/rank) * A @ B; the composition replaces
+ * python/spaceslug/backend.py:663-667).  1 <= rank <= 64. */
+int spaceslug_q4gemm_lora(const float* x, const uint32_t* packed, const float* scales, const float* lora_a,
+                          const float* lora_b, uint32_t rank, float alpha, float* y, uint32_t m, uint32_t n,
+                          uint32_t k);
+
+/* Device-pointer variant of both of the above (lora_a / lora_b may be NULL
+ * with rank 0).  Scratch memory comes from the device's stream-ordered pool. */
+int spaceslug_q4gemm_device(const float* x, const uint32_t* packed, const float* scales, const float* lora_a,
+                            const float* lora_b, uint32_t rank, float alpha, float* y, uint32_t m, uint32_t n,
+                            uint32_t k, void* stream);
+
+/* Device-resident weights (model-load time upload, then many calls), after
+ * the persistent-session pattern of vulkan-runtime/src/api/lora_session_api.h:6-14.
+ * The handle keeps columns [col_begin, col_end) of a K x N weight matrix given
+ * in the reference layout (host pointers), so a column shard of an N-sharded
+ * multi-GPU layer is one contiguous byte range with no repacking.
+ * col_begin = 0, col_end = n keeps the whole matrix. */
+typedef struct spaceslug_q4_weights spaceslug_q4_weights;
+int spaceslug_q4_weights_create(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n,
+                                uint32_t col_begin, uint32_t col_end, int device, spaceslug_q4_weights** out);
+/* Attach (or, with rank 0, detach) a LoRA adapter; lora_b is the full
+ * [rank x n] host matrix, the handle keeps its own columns. */
+int spaceslug_q4_weights_set_lora(spaceslug_q4_weights* w, const float* lora_a, const float* lora_b, uint32_t rank,
+                                  float alpha);
+/* Y[m x (col_end-col_begin)] for device pointers, asynchronous on `stream`. */
+int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, void* stream);
+/* Same with host pointers: copies X in, Y out, synchronous. */
+int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m);
+int spaceslug_q4_weights_destroy(spaceslug_q4_weights* w);
+
+/* Operand type of the tensor-core path: 0 = f16 with exact power-of-two
+ * row/column exponents (default), 1 = bf16.  Returns the previous value, or
+ * -1 for an invalid type. */
+int spaceslug_q4_set_operand_type(int type);
+
+/* Reads and clears the kernel status word of `device` (0 = no kernel wait
+ * has timed out since the last call).  Synchronises the device. */
+int spaceslug_q4_device_status(int device);
+
+/* Number of kernels this library has launched since load (all devices). */
+uint64_t spaceslug_q4_launch_count(void);
+
+/* Human-readable description of the last non-zero return code on this thread. */
+const char* spaceslug_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPACESLUG_RUNTIME_ABI_H */

@@ -1,0 +1,244 @@
+"""ctypes binding of libspaceslug_b200.so, in the style of the reference host.
+
+Mirrors python/spaceslug/backend.py of the reference: the native library is
+loaded lazily with ``ctypes.CDLL`` (backend.py:53-62), each symbol's argtypes
+/ restype are declared only ``if hasattr(...)`` (backend.py:64-200), the bound
+symbols become capabilities (backend.py:369-400), and a non-zero return code
+raises ``BackendError`` (backend.py:1689).  There is no CPU fallback: a
+missing library or a failing call raises.
+
+Host-pointer entry points take numpy arrays (float32 / int8 / uint32, C
+contiguous); device entry points take raw device addresses (ints, e.g.
+``tensor.data_ptr()``) and a CUDA stream handle (int, 0 = default stream).
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+DEFAULT_LIBRARY = PKG / "lib" / "libspaceslug_b200.so"
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_vp = ctypes.c_void_p
+_u32 = ctypes.c_uint32
+
+# name -> (argtypes, restype); mirrors include/runtime_abi.h
+_SIGNATURES = {
+    "spaceslug_vector_add": ([_f32p, _f32p, _f32p, ctypes.c_size_t], ctypes.c_int),
+    "spaceslug_lora_delta": ([_f32p, _f32p, _f32p, _f32p, _u32, _u32], ctypes.c_int),
+    "spaceslug_q4_pack": ([_i8p, _u32, _u32, _u32p], ctypes.c_int),
+    "spaceslug_q4_pack_device": ([_vp, _u32, _u32, _vp, _vp], ctypes.c_int),
+    "spaceslug_q4_dequant": ([_u32p, _f32p, _u32, _u32, _f32p], ctypes.c_int),
+    "spaceslug_q4_dequant_device": ([_vp, _vp, _u32, _u32, _vp, _vp], ctypes.c_int),
+    "spaceslug_q4gemm": ([_f32p, _u32p, _f32p, _f32p, _u32, _u32, _u32], ctypes.c_int),
+    "spaceslug_q4gemm_lora": ([_f32p, _u32p, _f32p, _f32p, _f32p, _u32, ctypes.c_float, _f32p, _u32, _u32, _u32],
+                              ctypes.c_int),
+    "spaceslug_q4gemm_device": ([_vp, _vp, _vp, _vp, _vp, _u32, ctypes.c_float, _vp, _u32, _u32, _u32, _vp],
+                                ctypes.c_int),
+    "spaceslug_q4_weights_create": ([_u32p, _f32p, _u32, _u32, _u32, _u32, ctypes.c_int, ctypes.POINTER(_vp)],
+                                    ctypes.c_int),
+    "spaceslug_q4_weights_set_lora": ([_vp, _f32p, _f32p, _u32, ctypes.c_float], ctypes.c_int),
+    "spaceslug_q4_weights_run": ([_vp, _vp, _vp, _u32, _vp], ctypes.c_int),
+    "spaceslug_q4_weights_run_host": ([_vp, _f32p, _f32p, _u32], ctypes.c_int),
+    "spaceslug_q4_weights_destroy": ([_vp], ctypes.c_int),
+    "spaceslug_q4_set_operand_type": ([ctypes.c_int], ctypes.c_int),
+    "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
+    "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
+    "spaceslug_last_error": ([], ctypes.c_char_p),
+}
+
+# symbol -> capability name reported by capabilities()
+_CAPABILITIES = {
+    "spaceslug_vector_add": "vector_add",
+    "spaceslug_lora_delta": "lora_delta_abi",
+    "spaceslug_q4_pack": "q4_pack",
+    "spaceslug_q4_dequant": "q4_dequant",
+    "spaceslug_q4gemm": "q4gemm",
+    "spaceslug_q4gemm_lora": "q4gemm_lora_fused",
+    "spaceslug_q4gemm_device": "q4gemm_device",
+    "spaceslug_q4_weights_create": "q4_weights_resident",
+}
+
+
+class BackendError(RuntimeError):
+    """A structured backend invocation failure."""
+
+    def __init__(self, message: str, code: int | None = None) -> None:
+        super().__init__(message)
+        self.code = code
+
+
+def _arr(a, dtype) -> np.ndarray:
+    out = np.ascontiguousarray(a, dtype=dtype)
+    return out
+
+
+def _p(a: np.ndarray, typ):
+    return a.ctypes.data_as(typ)
+
+
+class BackendSession:
+    """Session over the native library (no CPU fallback)."""
+
+    def __init__(self, library_path: str | Path | None = None) -> None:
+        self._library_path = Path(library_path) if library_path else DEFAULT_LIBRARY
+        self._library: ctypes.CDLL | None = None
+
+    # ------------------------------------------------------------ loading --
+    def _native(self) -> ctypes.CDLL:
+        if self._library is None:
+            if not self._library_path.is_file():
+                raise BackendError(f"runtime shared library is missing: {self._library_path}")
+            try:
+                lib = ctypes.CDLL(str(self._library_path))
+            except OSError as exc:
+                raise BackendError(f"failed to load {self._library_path}: {exc}") from exc
+            for name, (argtypes, restype) in _SIGNATURES.items():
+                if hasattr(lib, name):
+                    fn = getattr(lib, name)
+                    fn.argtypes = argtypes
+                    fn.restype = restype
+            self._library = lib
+        return self._library
+
+    @property
+    def library_path(self) -> Path:
+        return self._library_path
+
+    def capabilities(self) -> list[str]:
+        lib = self._native()
+        return [cap for sym, cap in _CAPABILITIES.items() if hasattr(lib, sym)]
+
+    def exported_symbols(self) -> list[str]:
+        lib = self._native()
+        return [s for s in _SIGNATURES if hasattr(lib, s)]
+
+    def _call(self, name: str, *args) -> int:
+        lib = self._native()
+        if not hasattr(lib, name):
+            raise BackendError(f"native symbol {name} is unavailable")
+        code = getattr(lib, name)(*args)
+        if code != 0:
+            msg = lib.spaceslug_last_error().decode(errors="replace") if hasattr(lib, "spaceslug_last_error") else ""
+            raise BackendError(f"native {name} returned {code}: {msg}", code)
+        return code
+
+    def raw(self, name: str):
+        """The bound ctypes function (returns codes instead of raising)."""
+        return getattr(self._native(), name)
+
+    # -------------------------------------------------------------- ops --
+    def vector_add(self, left, right) -> np.ndarray:
+        l, r = _arr(left, np.float32), _arr(right, np.float32)
+        if l.shape != r.shape:
+            raise BackendError("tensor shape mismatch")
+        out = np.empty_like(l)
+        self._call("spaceslug_vector_add", _p(l, _f32p), _p(r, _f32p), _p(out, _f32p), l.size)
+        return out
+
+    def lora_delta(self, x, a, b, m: int, rank: int) -> np.ndarray:
+        """Legacy Y[M,64] = X A B (reference backend.py:1678-1690)."""
+        xx, aa, bb = _arr(x, np.float32), _arr(a, np.float32), _arr(b, np.float32)
+        y = np.empty(m * 64, np.float32)
+        self._call("spaceslug_lora_delta", _p(xx, _f32p), _p(aa, _f32p), _p(bb, _f32p), _p(y, _f32p), m, rank)
+        return y
+
+    def q4_pack(self, w_kn) -> np.ndarray:
+        w = _arr(w_kn, np.int8)
+        k, n = w.shape
+        out = np.empty(k * n // 8, np.uint32)
+        self._call("spaceslug_q4_pack", _p(w, _i8p), k, n, _p(out, _u32p))
+        return out
+
+    def q4_dequant(self, packed, scales, k: int, n: int) -> np.ndarray:
+        pk, sc = _arr(packed, np.uint32), _arr(scales, np.float32)
+        out = np.empty((k, n), np.float32)
+        self._call("spaceslug_q4_dequant", _p(pk, _u32p), _p(sc, _f32p), k, n, _p(out, _f32p))
+        return out
+
+    def q4gemm(self, x, packed, scales, n: int, lora_a=None, lora_b=None, alpha: float = 0.0) -> np.ndarray:
+        xx, pk, sc = _arr(x, np.float32), _arr(packed, np.uint32), _arr(scales, np.float32)
+        m, k = xx.shape
+        y = np.empty((m, n), np.float32)
+        if lora_a is None:
+            self._call("spaceslug_q4gemm", _p(xx, _f32p), _p(pk, _u32p), _p(sc, _f32p), _p(y, _f32p), m, n, k)
+        else:
+            la, lb = _arr(lora_a, np.float32), _arr(lora_b, np.float32)
+            rank = la.shape[1]
+            self._call("spaceslug_q4gemm_lora", _p(xx, _f32p), _p(pk, _u32p), _p(sc, _f32p), _p(la, _f32p),
+                       _p(lb, _f32p), rank, float(alpha), _p(y, _f32p), m, n, k)
+        return y
+
+    def q4gemm_device(self, x: int, packed: int, scales: int, y: int, m: int, n: int, k: int, stream: int = 0,
+                      lora_a: int = 0, lora_b: int = 0, rank: int = 0, alpha: float = 0.0) -> None:
+        self._call("spaceslug_q4gemm_device", x, packed, scales, lora_a or None, lora_b or None, rank, float(alpha),
+                   y, m, n, k, stream or None)
+
+    def q4_dequant_device(self, packed: int, scales: int, k: int, n: int, out: int, stream: int = 0) -> None:
+        self._call("spaceslug_q4_dequant_device", packed, scales, k, n, out, stream or None)
+
+    def q4_pack_device(self, w_kn: int, k: int, n: int, packed: int, stream: int = 0) -> None:
+        self._call("spaceslug_q4_pack_device", w_kn, k, n, packed, stream or None)
+
+    def set_operand_type(self, kind: str) -> str:
+        prev = self.raw("spaceslug_q4_set_operand_type")({"f16": 0, "bf16": 1}[kind])
+        return {0: "f16", 1: "bf16"}.get(prev, "?")
+
+    def device_status(self, device: int = 0) -> int:
+        return int(self.raw("spaceslug_q4_device_status")(device))
+
+    def launch_count(self) -> int:
+        return int(self.raw("spaceslug_q4_launch_count")())
+
+    def weights(self, packed, scales, k: int, n: int, col_begin: int = 0, col_end: int | None = None,
+                device: int = 0) -> "Q4Weights":
+        return Q4Weights(self, packed, scales, k, n, col_begin, n if col_end is None else col_end, device)
+
+
+class Q4Weights:
+    """Device-resident int4 weights (a handle of the C-ABI)."""
+
+    def __init__(self, session: BackendSession, packed, scales, k: int, n: int, col_begin: int, col_end: int,
+                 device: int) -> None:
+        self.session = session
+        pk, sc = _arr(packed, np.uint32), _arr(scales, np.float32)
+        self.k, self.n_total, self.col_begin, self.col_end = k, n, col_begin, col_end
+        self.n = col_end - col_begin
+        h = _vp()
+        session._call("spaceslug_q4_weights_create", _p(pk, _u32p), _p(sc, _f32p), k, n, col_begin, col_end,
+                      device, ctypes.byref(h))
+        self.handle = h
+
+    def set_lora(self, lora_a, lora_b, alpha: float) -> None:
+        if lora_a is None:
+            self.session._call("spaceslug_q4_weights_set_lora", self.handle, None, None, 0, 0.0)
+            return
+        la, lb = _arr(lora_a, np.float32), _arr(lora_b, np.float32)
+        self.session._call("spaceslug_q4_weights_set_lora", self.handle, _p(la, _f32p), _p(lb, _f32p),
+                           la.shape[1], float(alpha))
+
+    def run(self, x: int, y: int, m: int, stream: int = 0) -> None:
+        self.session._call("spaceslug_q4_weights_run", self.handle, x, y, m, stream or None)
+
+    def run_host(self, x) -> np.ndarray:
+        xx = _arr(x, np.float32)
+        m = xx.shape[0]
+        y = np.empty((m, self.n), np.float32)
+        self.session._call("spaceslug_q4_weights_run_host", self.handle, _p(xx, _f32p), _p(y, _f32p), m)
+        return y
+
+    def close(self) -> None:
+        if self.handle:
+            self.session._call("spaceslug_q4_weights_destroy", self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -1,0 +1,67 @@
+// Launch interfaces of the sm_100a kernels (internal to libspaceslug_b200.so;
+// the public C-ABI is include/runtime_abi.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace q4 {
+
+// 16-bit operand type of the tensor-core (prefill) path.
+enum class Operand16 : int { kF16 = 0, kBF16 = 1 };
+
+struct GemvArgs {
+    const float* x;          // [M][K] fp32, device
+    const uint32_t* packed;  // reference layout, K*N/8 words, device
+    const float* scales;     // [N][K/32], device
+    float* y;                // [M][N] fp32, device
+    int M, N, K;
+    int cluster_k;           // CTAs per cluster = number of K slices
+    int clusters;            // grid = cluster_k * clusters CTAs
+    int cols_per_cluster;
+    const float* lora_t;     // [M][rank] = X*A (fp32) or nullptr
+    const float* lora_b;     // [rank][N] or nullptr
+    int rank;
+    float lora_scale;        // alpha / rank
+};
+int launch_gemv(const GemvArgs& a, cudaStream_t stream);
+size_t gemv_smem_bytes(int M, int K, int cluster_k, int cols_per_cluster);
+
+struct GemmArgs {
+    CUtensorMap tmap_x16;     // [M][K] 16-bit, box 64 x 128, 128B swizzle
+    CUtensorMap tmap_w;       // packed as uint32 [N][K/8], box 8 x BN, no swizzle
+    const float* scales;      // [N][K/32]
+    const int* col_exp;       // [N] power-of-two exponent applied to the column's scales, or nullptr
+    const int* row_exp;       // [M] power-of-two exponent applied to X rows, or nullptr
+    float* y;                 // [M][N]
+    int M, N, K;
+    Operand16 op;
+    int bn;                   // 128 or 256
+    const float* lora_t;      // [M][rank] fp32 or nullptr
+    const float* lora_b;      // [rank][N] fp32
+    int rank;
+    float lora_scale;
+    int* status;              // kernel status word (0 = ok)
+};
+int launch_gemm(const GemmArgs& a, cudaStream_t stream);
+size_t gemm_smem_bytes(int bn);
+
+// fp32 -> 16-bit cast of X with per-row power-of-two exponents (row_exp may be
+// nullptr: plain round-to-nearest cast).
+int launch_cast_x(const float* x, void* x16, int* row_exp, int M, int K, Operand16 op, cudaStream_t stream);
+// Per-column exponent f_n so that 8 * max_g |scale[n][g]| * 2^f_n lies in [2^13, 2^14).
+int launch_col_exp(const float* scales, int* col_exp, int N, int K, cudaStream_t stream);
+// Bit-exact dequant w[k*N + n] = float(v) * scale (fp32).
+int launch_dequant(const uint32_t* packed, const float* scales, float* w_kn, int K, int N, cudaStream_t stream);
+// Device packer: logical int8 b[k*N + n] in [-8,7] -> reference layout.
+int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t stream);
+// T[M][rank] = X[M][K] * A[K][rank] in fp32.
+int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream);
+// Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
+int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
+                        cudaStream_t stream);
+
+}  // namespace q4

@@ -1,0 +1,579 @@
+// Host runtime behind include/runtime_abi.h: argument validation, per-device
+// context (status word, stream for synchronous calls, stream-ordered scratch
+// pool), TMA descriptor encoding, kernel dispatch (GEMV for M <= 8, tcgen05
+// GEMM above), device-resident weight handles.
+//
+// Error behaviour mirrors vulkan-runtime/src/api/lora_delta_api.cpp:42-85:
+// arguments are checked first (return 1), every device failure returns 2, and
+// nothing throws across the ABI (catch (...) -> 2).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/runtime_abi.h"
+#include "q4_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_operand{static_cast<int>(q4::Operand16::kF16)};
+std::once_flag g_operand_env_once;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+struct CudaError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+void check_launch(int e, const char* what) {
+    if (e != 0) throw CudaError(std::string(what) + ": " + cudaGetErrorString(static_cast<cudaError_t>(e)));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// ------------------------------------------------------------ device ctx --
+struct DeviceCtx {
+    std::once_flag once;
+    bool ok = false;
+    std::string init_error;
+    int sm_count = 0;
+    int* status = nullptr;  // device int, kernels record wait timeouts here
+    cudaStream_t stream = nullptr;  // for the synchronous host-pointer entry points
+    std::mutex host_mu;             // serialises use of `stream` by host entry points
+};
+
+constexpr int kMaxDevices = 64;
+DeviceCtx g_ctx[kMaxDevices];
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+EncodeTiledFn encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    });
+    if (!g_encode) throw CudaError("cuTensorMapEncodeTiled is unavailable");
+    return g_encode;
+}
+
+DeviceCtx& ctx_for(int device) {
+    if (device < 0 || device >= kMaxDevices) throw CudaError("device ordinal out of range");
+    DeviceCtx& c = g_ctx[device];
+    std::call_once(c.once, [&] {
+        try {
+            check(cudaSetDevice(device), "cudaSetDevice");
+            check(cudaDeviceGetAttribute(&c.sm_count, cudaDevAttrMultiProcessorCount, device), "sm count");
+            int major = 0, minor = 0;
+            check(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "cc major");
+            check(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device), "cc minor");
+            if (major != 10) throw CudaError("this library is built for sm_100a (B200); device is sm_" +
+                                             std::to_string(major) + std::to_string(minor));
+            check(cudaMalloc(&c.status, sizeof(int)), "cudaMalloc status");
+            check(cudaMemset(c.status, 0, sizeof(int)), "cudaMemset status");
+            check(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            cudaMemPool_t pool;
+            check(cudaDeviceGetDefaultMemPool(&pool, device), "default mem pool");
+            uint64_t keep = UINT64_MAX;
+            check(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep), "pool threshold");
+            c.ok = true;
+        } catch (const std::exception& e) {
+            c.init_error = e.what();
+        }
+    });
+    if (!c.ok) throw CudaError(c.init_error.empty() ? "device init failed" : c.init_error);
+    return c;
+}
+
+int current_device() {
+    int d = 0;
+    check(cudaGetDevice(&d), "cudaGetDevice");
+    return d;
+}
+
+q4::Operand16 operand_type() {
+    std::call_once(g_operand_env_once, [] {
+        const char* e = std::getenv("SPACESLUG_Q4_OPERAND");
+        if (e && std::strcmp(e, "bf16") == 0) g_operand.store(static_cast<int>(q4::Operand16::kBF16));
+        if (e && std::strcmp(e, "f16") == 0) g_operand.store(static_cast<int>(q4::Operand16::kF16));
+    });
+    return static_cast<q4::Operand16>(g_operand.load());
+}
+
+// Stream-ordered scratch buffer released on the same stream at scope exit.
+struct Scratch {
+    void* p = nullptr;
+    cudaStream_t s = nullptr;
+    Scratch(size_t bytes, cudaStream_t stream) : s(stream) {
+        if (bytes) check(cudaMallocAsync(&p, bytes, stream), "cudaMallocAsync");
+    }
+    ~Scratch() {
+        if (p) cudaFreeAsync(p, s);
+    }
+    Scratch(const Scratch&) = delete;
+    Scratch& operator=(const Scratch&) = delete;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Argument check shared by all GEMM entry points (reference convention:
+// before any device work, return 1).
+const char* shape_error(const void* x, const void* packed, const void* scales, const void* y, uint32_t m, uint32_t n,
+                        uint32_t k, uint32_t rank, const void* la, const void* lb, float alpha) {
+    if (!x || !packed || !scales || !y) return "null pointer";
+    if (m == 0 || n == 0 || k == 0) return "zero dimension";
+    if (k % 32u) return "k must be a multiple of 32 (the scale group size)";
+    if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return "dimension too large";
+    if (rank > 64) return "LoRA rank must be <= 64";
+    if (rank > 0 && (!la || !lb)) return "LoRA rank > 0 needs both A and B";
+    if (rank > 0 && !std::isfinite(alpha)) return "LoRA alpha must be finite";
+    return nullptr;
+}
+
+// --------------------------------------------------------------- dispatch --
+struct Problem {
+    const float* x;
+    const uint32_t* packed;
+    const float* scales;
+    const int* col_exp;  // precomputed per-column exponents (handles) or nullptr
+    const float* lora_a;
+    const float* lora_b;
+    int rank;
+    float alpha;
+    float* y;
+    int M, N, K;
+};
+
+void choose_gemv(const DeviceCtx& c, int M, int N, int K, q4::GemvArgs& a) {
+    const int G = K / 32;
+    int S = 1;
+    while (S < 8 && G % (2 * S) == 0 && G / (2 * S) >= 32) S *= 2;
+    const int target = std::max(1, (2 * c.sm_count) / S);
+    int cols = (N + target - 1) / target;
+    cols = (cols + 3) / 4 * 4;
+    a.cluster_k = S;
+    a.cols_per_cluster = cols;
+    a.clusters = (N + cols - 1) / cols;
+    (void)M;
+}
+
+void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encoder()(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+}
+
+void run_problem(const Problem& p, cudaStream_t stream) {
+    DeviceCtx& c = ctx_for(current_device());
+    Scratch t_buf(p.rank > 0 ? static_cast<size_t>(p.M) * p.rank * sizeof(float) : 0, stream);
+    float* lora_t = static_cast<float*>(t_buf.p);
+    if (p.rank > 0) check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream), "lora_xa");
+    const float lscale = p.rank > 0 ? p.alpha / static_cast<float>(p.rank) : 0.0f;
+
+    if (p.M <= 8) {
+        q4::GemvArgs a{};
+        a.x = p.x; a.packed = p.packed; a.scales = p.scales; a.y = p.y;
+        a.M = p.M; a.N = p.N; a.K = p.K;
+        choose_gemv(c, p.M, p.N, p.K, a);
+        a.lora_t = lora_t; a.lora_b = p.rank > 0 ? p.lora_b : nullptr; a.rank = p.rank; a.lora_scale = lscale;
+        check_launch(q4::launch_gemv(a, stream), "gemv launch");
+        return;
+    }
+
+    const q4::Operand16 op = operand_type();
+    const bool f16 = op == q4::Operand16::kF16;
+    Scratch x16(static_cast<size_t>(p.M) * p.K * 2, stream);
+    Scratch rexp(f16 ? static_cast<size_t>(p.M) * sizeof(int) : 0, stream);
+    Scratch cexp(f16 && p.col_exp == nullptr ? static_cast<size_t>(p.N) * sizeof(int) : 0, stream);
+    int* row_exp = static_cast<int*>(rexp.p);
+    const int* col_exp = f16 ? (p.col_exp ? p.col_exp : static_cast<int*>(cexp.p)) : nullptr;
+    check_launch(q4::launch_cast_x(p.x, x16.p, row_exp, p.M, p.K, op, stream), "cast_x");
+    if (f16 && p.col_exp == nullptr)
+        check_launch(q4::launch_col_exp(p.scales, static_cast<int*>(cexp.p), p.N, p.K, stream), "col_exp");
+
+    q4::GemmArgs g{};
+    const long tiles256 = static_cast<long>((p.M + 127) / 128) * ((p.N + 255) / 256);
+    g.bn = tiles256 >= c.sm_count ? 256 : 128;
+    encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
+              static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) * 2, 64, 128,
+              CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
+              static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8, static_cast<uint32_t>(g.bn),
+              CU_TENSOR_MAP_SWIZZLE_NONE);
+    g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
+    g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
+    g.lora_t = lora_t; g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
+    g.status = c.status;
+    check_launch(q4::launch_gemm(g, stream), "gemm launch");
+}
+
+// Reads and clears the status word (synchronises `stream` first).
+int take_status(DeviceCtx& c, cudaStream_t stream) {
+    check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    int st = 0;
+    check(cudaMemcpy(&st, c.status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
+    if (st) check(cudaMemset(c.status, 0, sizeof(int)), "clear status");
+    return st;
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        return f();
+    } catch (const CudaError& e) {
+        return fail(SPACESLUG_RUNTIME_FAILURE, e.what());
+    } catch (const std::bad_alloc&) {
+        return fail(SPACESLUG_RUNTIME_FAILURE, "host allocation failed");
+    } catch (const std::exception& e) {
+        return fail(SPACESLUG_RUNTIME_FAILURE, e.what());
+    } catch (...) {
+        return fail(SPACESLUG_RUNTIME_FAILURE, "unknown failure");
+    }
+}
+
+void h2d(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+    if (bytes) check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync H2D");
+}
+void d2h(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+    if (bytes) check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync D2H");
+}
+
+}  // namespace
+
+struct spaceslug_q4_weights {
+    int device = 0;
+    int K = 0, N = 0;  // N = number of kept columns
+    uint32_t col_begin = 0, n_total = 0;
+    uint32_t* packed = nullptr;
+    float* scales = nullptr;
+    int* col_exp = nullptr;
+    float* lora_a = nullptr;
+    float* lora_b = nullptr;
+    int rank = 0;
+    float alpha = 0.0f;
+};
+
+extern "C" {
+
+int spaceslug_vector_add(const float* left, const float* right, float* output, size_t count) {
+    if (!left || !right || !output) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    for (size_t i = 0; i < count; ++i) output[i] = left[i] + right[i];
+    return SPACESLUG_OK;
+}
+
+int spaceslug_q4_pack(const int8_t* w_kn, uint32_t k, uint32_t n, uint32_t* packed_out) {
+    if (!w_kn || !packed_out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
+    return guarded([&] {
+        // Column-major output: for each column n, K/8 words of 8 nibbles each.
+        // Walk k in blocks of 8 rows so each output word is assembled in a
+        // register; the int8 source is read row-block by row-block.
+        const size_t words_per_col = k / 8u;
+        std::vector<uint32_t> acc(n);
+        for (uint32_t c = 0; c < k / 8u; ++c) {
+            std::fill(acc.begin(), acc.end(), 0u);
+            for (uint32_t i = 0; i < 8u; ++i) {
+                const int8_t* row = w_kn + static_cast<size_t>(8u * c + i) * n;
+                const uint32_t shift = 4u * i;
+                for (uint32_t col = 0; col < n; ++col)
+                    acc[col] |= (static_cast<uint32_t>(static_cast<uint8_t>(row[col])) & 0xFu) << shift;
+            }
+            for (uint32_t col = 0; col < n; ++col) packed_out[static_cast<size_t>(col) * words_per_col + c] = acc[col];
+        }
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_pack_device(const int8_t* w_kn, uint32_t k, uint32_t n, uint32_t* packed_out, void* stream) {
+    if (!w_kn || !packed_out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
+    return guarded([&] {
+        ctx_for(current_device());
+        check_launch(q4::launch_pack(w_kn, packed_out, static_cast<int>(k), static_cast<int>(n),
+                                     static_cast<cudaStream_t>(stream)),
+                     "pack launch");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_dequant_device(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n, float* w_kn_out,
+                                void* stream) {
+    if (!packed || !scales || !w_kn_out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
+    if (!aligned16(packed)) return fail(SPACESLUG_INVALID_ARGUMENT, "packed must be 16-byte aligned");
+    return guarded([&] {
+        ctx_for(current_device());
+        check_launch(q4::launch_dequant(packed, scales, w_kn_out, static_cast<int>(k), static_cast<int>(n),
+                                        static_cast<cudaStream_t>(stream)),
+                     "dequant launch");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_dequant(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n, float* w_kn_out) {
+    if (!packed || !scales || !w_kn_out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const size_t pw = static_cast<size_t>(k) * n / 2, sb = static_cast<size_t>(n) * (k / 32) * 4,
+                     wb = static_cast<size_t>(k) * n * 4;
+        Scratch dp(pw, c.stream), ds(sb, c.stream), dw(wb, c.stream);
+        h2d(dp.p, packed, pw, c.stream);
+        h2d(ds.p, scales, sb, c.stream);
+        check_launch(q4::launch_dequant(static_cast<uint32_t*>(dp.p), static_cast<float*>(ds.p),
+                                        static_cast<float*>(dw.p), static_cast<int>(k), static_cast<int>(n), c.stream),
+                     "dequant launch");
+        d2h(w_kn_out, dw.p, wb, c.stream);
+        check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4gemm_device(const float* x, const uint32_t* packed, const float* scales, const float* lora_a,
+                            const float* lora_b, uint32_t rank, float alpha, float* y, uint32_t m, uint32_t n,
+                            uint32_t k, void* stream) {
+    if (const char* err = shape_error(x, packed, scales, y, m, n, k, rank, lora_a, lora_b, alpha))
+        return fail(SPACESLUG_INVALID_ARGUMENT, err);
+    if (!aligned16(x) || !aligned16(packed) || !aligned16(y))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "x, packed and y must be 16-byte aligned");
+    return guarded([&] {
+        Problem p{x, packed, scales, nullptr, lora_a, lora_b, static_cast<int>(rank), alpha, y,
+                  static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)};
+        run_problem(p, static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4gemm_lora(const float* x, const uint32_t* packed, const float* scales, const float* lora_a,
+                          const float* lora_b, uint32_t rank, float alpha, float* y, uint32_t m, uint32_t n,
+                          uint32_t k) {
+    if (const char* err = shape_error(x, packed, scales, y, m, n, k, rank, lora_a, lora_b, alpha))
+        return fail(SPACESLUG_INVALID_ARGUMENT, err);
+    if (rank == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "LoRA rank must be >= 1");
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const size_t xb = static_cast<size_t>(m) * k * 4, pb = static_cast<size_t>(k) * n / 2,
+                     sb = static_cast<size_t>(n) * (k / 32) * 4, yb = static_cast<size_t>(m) * n * 4,
+                     ab = static_cast<size_t>(k) * rank * 4, bb = static_cast<size_t>(rank) * n * 4;
+        Scratch dx(xb, c.stream), dp(pb, c.stream), ds(sb, c.stream), dy(yb, c.stream), da(ab, c.stream),
+            db(bb, c.stream);
+        h2d(dx.p, x, xb, c.stream);
+        h2d(dp.p, packed, pb, c.stream);
+        h2d(ds.p, scales, sb, c.stream);
+        h2d(da.p, lora_a, ab, c.stream);
+        h2d(db.p, lora_b, bb, c.stream);
+        Problem p{static_cast<float*>(dx.p), static_cast<uint32_t*>(dp.p), static_cast<float*>(ds.p), nullptr,
+                  static_cast<float*>(da.p), static_cast<float*>(db.p), static_cast<int>(rank), alpha,
+                  static_cast<float*>(dy.p), static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)};
+        run_problem(p, c.stream);
+        d2h(y, dy.p, yb, c.stream);
+        if (take_status(c, c.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4gemm(const float* x, const uint32_t* packed, const float* scales, float* y, uint32_t m, uint32_t n,
+                     uint32_t k) {
+    if (const char* err = shape_error(x, packed, scales, y, m, n, k, 0, nullptr, nullptr, 0.0f))
+        return fail(SPACESLUG_INVALID_ARGUMENT, err);
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const size_t xb = static_cast<size_t>(m) * k * 4, pb = static_cast<size_t>(k) * n / 2,
+                     sb = static_cast<size_t>(n) * (k / 32) * 4, yb = static_cast<size_t>(m) * n * 4;
+        Scratch dx(xb, c.stream), dp(pb, c.stream), ds(sb, c.stream), dy(yb, c.stream);
+        h2d(dx.p, x, xb, c.stream);
+        h2d(dp.p, packed, pb, c.stream);
+        h2d(ds.p, scales, sb, c.stream);
+        Problem p{static_cast<float*>(dx.p), static_cast<uint32_t*>(dp.p), static_cast<float*>(ds.p), nullptr,
+                  nullptr, nullptr, 0, 0.0f, static_cast<float*>(dy.p), static_cast<int>(m), static_cast<int>(n),
+                  static_cast<int>(k)};
+        run_problem(p, c.stream);
+        d2h(y, dy.p, yb, c.stream);
+        if (take_status(c, c.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_lora_delta(const float* x, const float* a, const float* b, float* y, uint32_t m, uint32_t rank) {
+    // Same checks as vulkan-runtime/src/api/lora_delta_api.cpp:44.
+    if (x == nullptr || a == nullptr || b == nullptr || y == nullptr || m == 0 || m > 128 || rank == 0 || rank > 8)
+        return fail(SPACESLUG_INVALID_ARGUMENT, "invalid arguments (need 1<=m<=128, 1<=rank<=8, non-null)");
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const size_t xb = static_cast<size_t>(m) * 64 * 4, ab = 64u * rank * 4, bb = rank * 64u * 4;
+        Scratch dx(xb, c.stream), da(ab, c.stream), db(bb, c.stream), dy(xb, c.stream);
+        h2d(dx.p, x, xb, c.stream);
+        h2d(da.p, a, ab, c.stream);
+        h2d(db.p, b, bb, c.stream);
+        check_launch(q4::launch_lora_delta64(static_cast<float*>(dx.p), static_cast<float*>(da.p),
+                                             static_cast<float*>(db.p), static_cast<float*>(dy.p),
+                                             static_cast<int>(m), static_cast<int>(rank), c.stream),
+                     "lora_delta launch");
+        d2h(y, dy.p, xb, c.stream);
+        check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_create(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n,
+                                uint32_t col_begin, uint32_t col_end, int device, spaceslug_q4_weights** out) {
+    if (!packed || !scales || !out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
+    if (col_begin >= col_end || col_end > n) return fail(SPACESLUG_INVALID_ARGUMENT, "bad column range");
+    *out = nullptr;
+    return guarded([&] {
+        check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceCtx& c = ctx_for(device);
+        auto* w = new spaceslug_q4_weights();
+        w->device = device;
+        w->K = static_cast<int>(k);
+        w->N = static_cast<int>(col_end - col_begin);
+        w->col_begin = col_begin;
+        w->n_total = n;
+        const size_t G = k / 32u;
+        const size_t pb = static_cast<size_t>(w->N) * k / 2, sb = static_cast<size_t>(w->N) * G * 4;
+        try {
+            check(cudaMalloc(&w->packed, pb), "cudaMalloc packed");
+            check(cudaMalloc(&w->scales, sb), "cudaMalloc scales");
+            check(cudaMalloc(&w->col_exp, static_cast<size_t>(w->N) * sizeof(int)), "cudaMalloc col_exp");
+            std::lock_guard<std::mutex> lk(c.host_mu);
+            h2d(w->packed, packed + static_cast<size_t>(col_begin) * (k / 8u), pb, c.stream);
+            h2d(w->scales, scales + static_cast<size_t>(col_begin) * G, sb, c.stream);
+            check_launch(q4::launch_col_exp(w->scales, w->col_exp, w->N, w->K, c.stream), "col_exp");
+            check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        } catch (...) {
+            spaceslug_q4_weights_destroy(w);
+            throw;
+        }
+        *out = w;
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_set_lora(spaceslug_q4_weights* w, const float* lora_a, const float* lora_b, uint32_t rank,
+                                  float alpha) {
+    if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
+    if (rank > 64) return fail(SPACESLUG_INVALID_ARGUMENT, "LoRA rank must be <= 64");
+    if (rank > 0 && (!lora_a || !lora_b || !std::isfinite(alpha)))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "LoRA needs A, B and a finite alpha");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        cudaFree(w->lora_a);
+        cudaFree(w->lora_b);
+        w->lora_a = w->lora_b = nullptr;
+        w->rank = 0;
+        if (rank == 0) return SPACESLUG_OK;
+        // lora_b is the full [rank x n_total] matrix; keep the handle's columns.
+        check(cudaMalloc(&w->lora_a, static_cast<size_t>(w->K) * rank * 4), "cudaMalloc lora_a");
+        check(cudaMalloc(&w->lora_b, static_cast<size_t>(rank) * w->N * 4), "cudaMalloc lora_b");
+        check(cudaMemcpy(w->lora_a, lora_a, static_cast<size_t>(w->K) * rank * 4, cudaMemcpyHostToDevice), "H2D A");
+        check(cudaMemcpy2D(w->lora_b, static_cast<size_t>(w->N) * 4, lora_b + w->col_begin,
+                           static_cast<size_t>(w->n_total) * 4, static_cast<size_t>(w->N) * 4, rank,
+                           cudaMemcpyHostToDevice),
+              "H2D B");
+        w->rank = static_cast<int>(rank);
+        w->alpha = alpha;
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, void* stream) {
+    if (!w || !x || !y) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (m == 0 || m > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "bad m");
+    if (!aligned16(x) || !aligned16(y)) return fail(SPACESLUG_INVALID_ARGUMENT, "x and y must be 16-byte aligned");
+    return guarded([&] {
+        if (current_device() != w->device) check(cudaSetDevice(w->device), "cudaSetDevice");
+        Problem p{x, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, y,
+                  static_cast<int>(m), w->N, w->K};
+        run_problem(p, static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m) {
+    if (!w || !x || !y) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (m == 0 || m > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "bad m");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        DeviceCtx& c = ctx_for(w->device);
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const size_t xb = static_cast<size_t>(m) * w->K * 4, yb = static_cast<size_t>(m) * w->N * 4;
+        Scratch dx(xb, c.stream), dy(yb, c.stream);
+        h2d(dx.p, x, xb, c.stream);
+        Problem p{static_cast<float*>(dx.p), w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank,
+                  w->alpha, static_cast<float*>(dy.p), static_cast<int>(m), w->N, w->K};
+        run_problem(p, c.stream);
+        d2h(y, dy.p, yb, c.stream);
+        if (take_status(c, c.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_destroy(spaceslug_q4_weights* w) {
+    if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
+    cudaSetDevice(w->device);
+    cudaFree(w->packed);
+    cudaFree(w->scales);
+    cudaFree(w->col_exp);
+    cudaFree(w->lora_a);
+    cudaFree(w->lora_b);
+    delete w;
+    return SPACESLUG_OK;
+}
+
+int spaceslug_q4_set_operand_type(int type) {
+    if (type != 0 && type != 1) return -1;
+    operand_type();  // apply the environment default first
+    return g_operand.exchange(type);
+}
+
+int spaceslug_q4_device_status(int device) {
+    return guarded([&] {
+        check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceCtx& c = ctx_for(device);
+        check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        int st = 0;
+        check(cudaMemcpy(&st, c.status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
+        if (st) check(cudaMemset(c.status, 0, sizeof(int)), "clear status");
+        return st;
+    });
+}
+
+uint64_t spaceslug_q4_launch_count(void) { return g_launches.load(); }
+
+const char* spaceslug_last_error(void) { return g_last_error.c_str(); }
+
+}  // extern "C"
