@@ -89,6 +89,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Bounded wait that ignores the abort flag: used on the abort path to let
+// copies already in flight land before the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+    const unsigned long long t0 = globaltimer_ns();
+#pragma unroll 1
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+}
+
+// 4-byte asynchronous global -> shared copy; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// Arrive on `bar` once all of this thread's prior cp.async copies completed
+// (the arrival counts against the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // --------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

@@ -1,20 +1,29 @@
 // Prefill GEMM (M > 8):  Y[M x N] = X[M x K] . dequant(W)  (+ LoRA term).
 //
 // Replaces vulkan-runtime/shaders/q4gemm.comp:61-175 (fp32 FMA tiles with the
-// int4 B operand dequantised into an fp32 LDS tile) with a Blackwell tensor
-// core pipeline:
+// int4 B operand dequantised into an fp32 LDS tile) with a persistent
+// Blackwell tensor-core pipeline.  One CTA per SM walks output tiles of
+// (128*H) x 128; per tile and 64-wide k-step:
 //
-//   warp 0        TMA producer: X tile (16-bit, 128 x 64, 128B swizzle) and
-//                 the raw packed W tile (BN columns x 32 bytes) per k-step;
-//   warp 1        allocates TMEM, one elected thread issues tcgen05.mma
-//                 (kind::f16, M=128, N=BN, K=16 x 4 per k-step) into an fp32
-//                 TMEM accumulator, commits each stage back to the producer;
-//   warps 2..9    dequantise: nibbles -> float(v) (exact) * scale (fp32, RN,
-//                 the reference's w = float(v) * scale of q4gemm.comp:116-122)
-//                 -> 16-bit RN, written straight into the canonical K-major
-//                 128B-swizzled UMMA B tile; then warps 2..5 run the epilogue
-//                 (tcgen05.ld 32 lanes x 16 columns, undo the power-of-two
-//                 operand exponents, add the fused LoRA term, store fp32 Y).
+//   warp 0        TMA producer: X tile (16-bit, 64 x 128H, 128B swizzle) and
+//                 the raw packed W tile (128 columns x 32 bytes);
+//   warp 1        allocates TMEM (2 accumulator buffers x H x 128 columns);
+//                 one elected thread issues tcgen05.mma kind::f16 (M=128,
+//                 N=128, K=16; H row halves share one B tile), commits each
+//                 stage back to the producer and each finished accumulator
+//                 to the epilogue;
+//   warps 2..9    dequantise one (column, 32-k group) unit each per k-step:
+//                 nibbles -> float(v) exactly -> * scale in fp32 (the
+//                 reference's w = float(v) * scale, q4gemm.comp:116-122) ->
+//                 16-bit RN, written straight into the canonical K-major
+//                 128B-swizzled UMMA B tile (packed f32x2 arithmetic);
+//   warps 10..13  epilogue: tcgen05.ld 32 lanes x 16 columns, undo the
+//                 power-of-two operand exponents, add the fused LoRA term
+//                 (alpha/r) * T[m,:] . B[:, n], store fp32 Y; overlaps the
+//                 next tile's main loop through the second TMEM buffer.
+//
+// With H = 2 every dequantised weight feeds 256 rows of MMA, which keeps the
+// CUDA-core dequant work well under the tensor-core time per k-step.
 //
 // Operand precision: f16 operands carry a per-row power-of-two exponent for X
 // and a per-column one for W (chosen so no element can overflow f16); the
@@ -34,36 +43,38 @@ namespace q4 {
 
 namespace {
 
-constexpr int kBM = 128;
+constexpr int kBN = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 320;  // 10 warps
+constexpr int kThreads = 448;  // 14 warps
 constexpr int kDequantWarps = 8;
-constexpr int kDequantThreads = kDequantWarps * 32;
+constexpr int kEpiWarp0 = 10;
+constexpr int kEpiWarps = 4;
 
-template <int BN>
+template <int H>
 struct Cfg {
-    static constexpr int kStages = BN == 256 ? 4 : 6;
-    static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-    static constexpr int kBBytes = BN * kBK * 2;   // BN x 128 B
-    static constexpr int kRBytes = BN * kBK / 2;   // BN x 32 B (packed nibbles)
+    static constexpr int kBM = 128 * H;
+    static constexpr int kStages = H == 2 ? 4 : 6;
+    static constexpr int kABytes = kBM * kBK * 2;  // 16 KB per 128-row half
+    static constexpr int kBBytes = kBN * kBK * 2;  // 16 KB
+    static constexpr int kRBytes = kBN * kBK / 2;  // 4 KB (packed nibbles)
     static constexpr int kAOff = 0;
     static constexpr int kBOff = kAOff + kStages * kABytes;
     static constexpr int kROff = kBOff + kStages * kBBytes;
     static constexpr int kBarOff = kROff + kStages * kRBytes;
-    static constexpr int kNumBars = 4 * kStages + 1;
+    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 1;  // ring, acc_full[2], acc_empty[2], done
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kBytes = kMiscOff + 16;
     static constexpr int kSmemAlloc = kBytes + 1024;  // slack for 1024-byte alignment
-    static constexpr int kUnitsPerThread = (BN * 2) / kDequantThreads;  // (column, group) units
+    static constexpr int kTmemCols = 2 * H * kBN;     // 256 or 512
     static_assert(kSmemAlloc <= 232448, "shared memory budget");
-    static_assert(kUnitsPerThread * kDequantThreads == BN * 2, "dequant mapping");
+    static_assert(kDequantWarps * 32 == kBN * 2, "one (column, group) unit per dequant thread");
 };
 
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
 
 template <typename T16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-    if constexpr (sizeof(T16) == 2 && std::is_same<T16, __half>::value) {
+    if constexpr (std::is_same<T16, __half>::value) {
         __half2 h = __floats2half2_rn(lo, hi);
         return *reinterpret_cast<uint32_t*>(&h);
     } else {
@@ -72,32 +83,33 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     }
 }
 
-// Dequantise one packed word (8 consecutive k of one column) times `s` into
-// four 16-bit pairs.  Same magic-number unpack as the GEMV: v exact, then one
-// fp32 multiply by the (power-of-two adjusted) scale, then 16-bit RN.
+// Dequantise one packed word (8 consecutive k of one column) times s into
+// four 16-bit pairs: magic-number unpack (exact), one fp32 multiply (RN),
+// 16-bit RN; pairs (k, k+1) are processed as packed f32x2.
 template <typename T16>
-__device__ __forceinline__ uint4 dequant_word(uint32_t q, float s) {
+__device__ __forceinline__ uint4 dequant_word(uint32_t q, float2 s2) {
     const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;
     const uint32_t hi = ((q >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;
-    const float bias = 8388616.0f;
+    const float2 nbias = make_float2(-8388616.0f, -8388616.0f);
     uint32_t out[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-        const float ve = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))) - bias;
-        const float vo = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))) - bias;
-        out[b] = pack2<T16>(ve * s, vo * s);
+        const float2 mg = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))),
+                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))));
+        const float2 w = __fmul2_rn(__fadd2_rn(mg, nbias), s2);
+        out[b] = pack2<T16>(w.x, w.y);
     }
     return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
-template <int BN, typename T16>
+template <int H, typename T16>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                    const float* __restrict__ scales, const int* __restrict__ col_exp,
                    const int* __restrict__ row_exp, float* __restrict__ y, int M, int N, int K,
                    const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank, float lora_scale,
                    int* __restrict__ status) {
-    using C = Cfg<BN>;
+    using C = Cfg<H>;
     constexpr int ST = C::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
@@ -112,12 +124,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto full_r = [&](int s) { return bar + 8u * (ST + s); };
     auto full_b = [&](int s) { return bar + 8u * (2 * ST + s); };
     auto empty = [&](int s) { return bar + 8u * (3 * ST + s); };
-    const uint32_t acc_full = bar + 8u * (4 * ST);
+    auto acc_full = [&](int b) { return bar + 8u * (4 * ST + b); };
+    auto acc_empty = [&](int b) { return bar + 8u * (4 * ST + 2 + b); };
+    const uint32_t done_bar = bar + 8u * (4 * ST + 4);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+    const int MT = (M + C::kBM - 1) / C::kBM;
+    const int NT = (N + kBN - 1) / kBN;
+    const int tiles = MT * NT;
     const int KT = (K + kBK - 1) / kBK;
     const int G = K / 32;
 
@@ -128,156 +144,203 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(full_b(s), kDequantWarps);
             mbar_init(empty(s), 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full(b), 1);
+            mbar_init(acc_empty(b), kEpiWarps);
+        }
+        mbar_init(done_bar, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
         tma_prefetch_desc(&tmap_x);
         tma_prefetch_desc(&tmap_w);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), BN);
+        tmem_alloc(smem_u32(tmem_holder), C::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before_sync();
     __syncthreads();
     tc_fence_after_sync();
-    const uint32_t tmem_d = *tmem_holder;
+    const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
-            for (int kt = 0; kt < KT; ++kt) {
-                const int s = kt % ST;
-                const uint32_t ph = (kt / ST) & 1u;
-                if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) break;
-                mbar_arrive_expect_tx(full_a(s), C::kABytes);
-                tma_load_2d(a_s + s * C::kABytes, &tmap_x, full_a(s), kt * kBK, m0);
-                mbar_arrive_expect_tx(full_r(s), C::kRBytes);
-                tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST;
+                    const uint32_t ph = (it / ST) & 1u;
+                    if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_a(s), C::kABytes);
+                    tma_load_2d(a_s + s * C::kABytes, &tmap_x, full_a(s), kt * kBK, m0);
+                    mbar_arrive_expect_tx(full_r(s), C::kRBytes);
+                    tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
+                }
+            }
+            if (*abort_flag) {  // let the copies in flight land before exit
+                for (int j = (it > ST ? it - ST : 0); j < it; ++j) {
+                    mbar_drain(full_a(j % ST), (j / ST) & 1u);
+                    mbar_drain(full_r(j % ST), (j / ST) & 1u);
+                }
             }
         }
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
         if (elect_one()) {
-            const uint32_t idesc =
-                umma_idesc_f16(std::is_same<T16, __half>::value ? 0u : 1u, static_cast<uint32_t>(kBM),
-                               static_cast<uint32_t>(BN));
-            for (int kt = 0; kt < KT; ++kt) {
-                const int s = kt % ST;
-                const uint32_t ph = (kt / ST) & 1u;
-                if (!mbar_wait(full_a(s), ph, abort_flag, status, kStatusTimeoutMma)) break;
-                if (!mbar_wait(full_b(s), ph, abort_flag, status, kStatusTimeoutMma)) break;
+            const uint32_t idesc = umma_idesc_f16(std::is_same<T16, __half>::value ? 0u : 1u, 128u,
+                                                  static_cast<uint32_t>(kBN));
+            int it = 0, i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+                const int b = i & 1;
+                const uint32_t u = static_cast<uint32_t>(i >> 1);
+                if (!mbar_wait(acc_empty(b), (u & 1u) ^ 1u, abort_flag, status, kStatusTimeoutMma)) break;
                 tc_fence_after_sync();
+                const uint32_t d0 = tmem_base + static_cast<uint32_t>(b * H * kBN);
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST;
+                    const uint32_t ph = (it / ST) & 1u;
+                    if (!mbar_wait(full_a(s), ph, abort_flag, status, kStatusTimeoutMma) ||
+                        !mbar_wait(full_b(s), ph, abort_flag, status, kStatusTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    const uint64_t ad = umma_desc_k_sw128(a_s + s * C::kABytes + kk * 32);
-                    const uint64_t bd = umma_desc_k_sw128(b_s + s * C::kBBytes + kk * 32);
-                    umma_f16_ss(tmem_d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint64_t bd = umma_desc_k_sw128(b_s + s * C::kBBytes + kk * 32);
+#pragma unroll
+                        for (int h = 0; h < H; ++h) {
+                            const uint64_t ad = umma_desc_k_sw128(a_s + s * C::kABytes + h * 16384 + kk * 32);
+                            umma_f16_ss(d0 + static_cast<uint32_t>(h * kBN), ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+                        }
+                    }
+                    umma_commit(empty(s));
                 }
-                umma_commit(empty(s));
+                if (ok) umma_commit(acc_full(b));
             }
-            umma_commit(acc_full);  // tracks every MMA issued above (also on abort)
+            umma_commit(done_bar);  // tracks every MMA issued above
+            mbar_drain(done_bar, 0u);
         }
-    } else {
+    } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------- dequant --
         const int dt = tid - 64;
-        float cs[C::kUnitsPerThread];   // 2^col_exp of the unit's column (exact)
-        float sc[C::kUnitsPerThread];   // scale of the current k-step
-        int nl[C::kUnitsPerThread], hh[C::kUnitsPerThread];
-#pragma unroll
-        for (int u = 0; u < C::kUnitsPerThread; ++u) {
-            const int unit = dt + u * kDequantThreads;
-            nl[u] = unit >> 1;
-            hh[u] = unit & 1;
-            const int n = n0 + nl[u];
-            cs[u] = (col_exp != nullptr && n < N) ? exp2i(col_exp[n]) : 1.0f;
-            const int g = hh[u];
-            sc[u] = (n < N && g < G) ? __ldg(scales + static_cast<size_t>(n) * G + g) : 0.0f;
-        }
-        for (int kt = 0; kt < KT; ++kt) {
-            const int s = kt % ST;
-            const uint32_t ph = (kt / ST) & 1u;
-            // prefetch the next k-step's scales while this step is converted
-            float sn[C::kUnitsPerThread];
-#pragma unroll
-            for (int u = 0; u < C::kUnitsPerThread; ++u) {
-                const int n = n0 + nl[u];
-                const int g = (kt + 1) * 2 + hh[u];
-                sn[u] = (n < N && g < G) ? __ldg(scales + static_cast<size_t>(n) * G + g) : 0.0f;
-            }
-            if (!mbar_wait(full_r(s), ph, abort_flag, status, kStatusTimeoutDequant)) break;
-            const uint8_t* rt = smem + C::kROff + s * C::kRBytes;
-            uint8_t* bt = smem + C::kBOff + s * C::kBBytes;
-#pragma unroll
-            for (int u = 0; u < C::kUnitsPerThread; ++u) {
-                const uint4 q = *reinterpret_cast<const uint4*>(rt + nl[u] * 32 + hh[u] * 16);
-                const float sv = sc[u] * cs[u];
+        const int nl = dt >> 1, hh = dt & 1;  // unit: column nl, group half hh of the k-step
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            const int n = (t / MT) * kBN + nl;
+            const bool col_ok = n < N;
+            const float cs = (col_exp != nullptr && col_ok) ? exp2i(col_exp[n]) : 1.0f;
+            const float* srow = scales + static_cast<size_t>(col_ok ? n : 0) * G;
+            float sc = (col_ok && hh < G) ? __ldg(srow + hh) : 0.0f;
+            for (int kt = 0; kt < KT; ++kt, ++it) {
+                const int s = it % ST;
+                const uint32_t ph = (it / ST) & 1u;
+                const int gn = (kt + 1) * 2 + hh;
+                const float sn = (col_ok && gn < G) ? __ldg(srow + gn) : 0.0f;  // next step's scale
+                if (!mbar_wait(full_r(s), ph, abort_flag, status, kStatusTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                const uint4 q = *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
+                const float sv = sc * cs;
+                const float2 s2 = make_float2(sv, sv);
+                uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
                 const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const uint4 o = dequant_word<T16>(words[j], sv);
-                    const int chunk = (hh[u] * 4 + j) ^ (nl[u] & 7);
-                    *reinterpret_cast<uint4*>(bt + nl[u] * 128 + chunk * 16) = o;
+                    const int chunk = (hh * 4 + j) ^ (nl & 7);
+                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_word<T16>(words[j], s2);
                 }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(full_b(s));
+                sc = sn;
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(full_b(s));
-#pragma unroll
-            for (int u = 0; u < C::kUnitsPerThread; ++u) sc[u] = sn[u];
         }
-
+    } else {
         // ------------------------------------------------------ epilogue --
-        if (warp < 6) {
-            const bool ok = mbar_wait(acc_full, 0u, abort_flag, status, kStatusTimeoutEpilogue);
+        const int quarter = warp & 3;
+        const bool vec_ok = (N % 4) == 0;
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const int b = i & 1;
+            const uint32_t u = static_cast<uint32_t>(i >> 1);
+            if (!mbar_wait(acc_full(b), u & 1u, abort_flag, status, kStatusTimeoutEpilogue)) break;
             tc_fence_after_sync();
-            const int quarter = warp & 3;
-            const int row = m0 + quarter * 32 + lane;
-            const bool row_ok = ok && !*abort_flag && row < M;
-            const float rs = (row_exp != nullptr && row < M) ? exp2i(-row_exp[row]) : 1.0f;
-            float* yrow = y + static_cast<size_t>(row < M ? row : 0) * N;
-            const bool vec_ok = (N % 4) == 0;
+            const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
 #pragma unroll 1
-            for (int c = 0; c < BN / 16; ++c) {
-                uint32_t r[16];
-                tmem_ld16(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c * 16), r);
-                tmem_ld_wait();
-                const int nb = n0 + c * 16;
-                if (nb >= N) continue;  // warp-uniform
-                float v[16];
+            for (int h = 0; h < H; ++h) {
+                const int row = m0 + h * 128 + quarter * 32 + lane;
+                const bool row_ok = row < M;
+                const float rs = (row_exp != nullptr && row_ok) ? exp2i(-row_exp[row]) : 1.0f;
+                float* yrow = y + static_cast<size_t>(row_ok ? row : 0) * N;
+                const uint32_t tcol = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                      static_cast<uint32_t>(b * H * kBN + h * kBN);
+#pragma unroll 1
+                for (int c = 0; c < kBN / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tcol + static_cast<uint32_t>(c * 16), r);
+                    tmem_ld_wait();
+                    const int nb = n0 + c * 16;
+                    if (nb >= N) continue;  // warp-uniform
+                    float v[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int n = nb + i;
-                    const float cinv = (col_exp != nullptr && n < N) ? exp2i(-col_exp[n]) : 1.0f;
-                    v[i] = __uint_as_float(r[i]) * rs * cinv;
-                }
-                if (lora_t != nullptr && row_ok) {
-                    float d[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) d[i] = 0.0f;
-                    const float* trow = lora_t + static_cast<size_t>(row) * rank;
-                    for (int j = 0; j < rank; ++j) {
-                        const float tj = __ldg(trow + j);
-                        const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
-#pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            if (nb + i < N) d[i] = fmaf(tj, __ldg(brow + i), d[i]);
+                    for (int e = 0; e < 16; ++e) {
+                        const int n = nb + e;
+                        const float cinv = (col_exp != nullptr && n < N) ? exp2i(-col_exp[n]) : 1.0f;
+                        v[e] = __uint_as_float(r[e]) * rs * cinv;
                     }
+                    if (lora_t != nullptr && row_ok) {
+                        float d[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) v[i] = fmaf(lora_scale, d[i], v[i]);
-                }
-                if (row_ok) {
-                    if (vec_ok && nb + 16 <= N) {
+                        for (int e = 0; e < 16; ++e) d[e] = 0.0f;
+                        const float* trow = lora_t + static_cast<size_t>(row) * rank;
+                        const bool full16 = nb + 16 <= N && vec_ok;
+                        for (int j = 0; j < rank; ++j) {
+                            const float tj = __ldg(trow + j);
+                            const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
+                            if (full16) {
 #pragma unroll
-                        for (int i = 0; i < 16; i += 4)
-                            *reinterpret_cast<float4*>(yrow + nb + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                    } else {
+                                for (int e = 0; e < 16; e += 4) {
+                                    const float4 bv = __ldg(reinterpret_cast<const float4*>(brow + e));
+                                    d[e] = fmaf(tj, bv.x, d[e]);
+                                    d[e + 1] = fmaf(tj, bv.y, d[e + 1]);
+                                    d[e + 2] = fmaf(tj, bv.z, d[e + 2]);
+                                    d[e + 3] = fmaf(tj, bv.w, d[e + 3]);
+                                }
+                            } else {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            if (nb + i < N) yrow[nb + i] = v[i];
+                                for (int e = 0; e < 16; ++e)
+                                    if (nb + e < N) d[e] = fmaf(tj, __ldg(brow + e), d[e]);
+                            }
+                        }
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] = fmaf(lora_scale, d[e], v[e]);
+                    }
+                    if (row_ok) {
+                        if (vec_ok && nb + 16 <= N) {
+#pragma unroll
+                            for (int e = 0; e < 16; e += 4)
+                                *reinterpret_cast<float4*>(yrow + nb + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e)
+                                if (nb + e < N) yrow[nb + e] = v[e];
+                        }
                     }
                 }
             }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(b));
         }
     }
 
@@ -285,17 +348,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after_sync();
-        tmem_dealloc(tmem_d, BN);
+        tmem_dealloc(tmem_base, C::kTmemCols);
     }
 }
 
-template <int BN, typename T16>
-int launch_gemm_t(const GemmArgs& a, cudaStream_t stream) {
-    using C = Cfg<BN>;
-    auto kern = q4_gemm_kernel<BN, T16>;
+template <int H, typename T16>
+int launch_gemm_t(const GemmArgs& a, int grid, cudaStream_t stream) {
+    using C = Cfg<H>;
+    auto kern = q4_gemm_kernel<H, T16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemAlloc);
     if (e != cudaSuccess) return static_cast<int>(e);
-    dim3 grid((a.M + kBM - 1) / kBM, (a.N + BN - 1) / BN, 1);
     kern<<<grid, kThreads, C::kSmemAlloc, stream>>>(a.tmap_x16, a.tmap_w, a.scales, a.col_exp, a.row_exp, a.y, a.M,
                                                     a.N, a.K, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
     return static_cast<int>(cudaGetLastError());
@@ -303,16 +365,18 @@ int launch_gemm_t(const GemmArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
-size_t gemm_smem_bytes(int bn) { return bn == 256 ? Cfg<256>::kSmemAlloc : Cfg<128>::kSmemAlloc; }
+int gemm_tiles(int M, int N, int halves) { return ((M + 128 * halves - 1) / (128 * halves)) * ((N + kBN - 1) / kBN); }
 
 int launch_gemm(const GemmArgs& a, cudaStream_t stream) {
-    if (a.bn == 256) {
-        return a.op == Operand16::kF16 ? launch_gemm_t<256, __half>(a, stream)
-                                       : launch_gemm_t<256, __nv_bfloat16>(a, stream);
+    const int tiles = gemm_tiles(a.M, a.N, a.halves);
+    const int grid = tiles < a.sm_count ? tiles : a.sm_count;
+    if (a.halves == 2) {
+        return a.op == Operand16::kF16 ? launch_gemm_t<2, __half>(a, grid, stream)
+                                       : launch_gemm_t<2, __nv_bfloat16>(a, grid, stream);
     }
-    if (a.bn == 128) {
-        return a.op == Operand16::kF16 ? launch_gemm_t<128, __half>(a, stream)
-                                       : launch_gemm_t<128, __nv_bfloat16>(a, stream);
+    if (a.halves == 1) {
+        return a.op == Operand16::kF16 ? launch_gemm_t<1, __half>(a, grid, stream)
+                                       : launch_gemm_t<1, __nv_bfloat16>(a, grid, stream);
     }
     return static_cast<int>(cudaErrorInvalidValue);
 }

@@ -6,23 +6,29 @@
 //   packed byte pb = n*(K/2) + k/2, low nibble = even k, v & 0xF two's complement;
 //   scale (k, n) = scales[n*(K/32) + k/32];  w = float(v) * scale.
 // Because K % 32 == 0, the 16 bytes of one column's 32-k scale group are one
-// aligned 128-bit word: lane l of a warp loads group l with one 16-byte load.
+// aligned 128-bit word.
 //
-// Structure (HBM-bound streaming):
-//   * a cluster of S CTAs splits K into S slices; each CTA stages its slice of
-//     X (all M rows) in shared memory once, swizzled so that 8 lanes reading
-//     the same float4 offset of 8 different groups hit 8 different bank quads;
-//   * each warp walks the cluster's column range C columns at a time, lanes
-//     over scale groups, with the next step's weights and scales already in
-//     flight (software pipeline, 2*C 16-byte loads per lane);
-//   * per group the integer dot product sum_j x_j*v_j is accumulated in fp32
-//     and multiplied by the group scale once (w = v*s is never materialised);
-//   * partial sums are reduced across lanes with warp shuffles, parked in
-//     shared memory, and reduced across the cluster's K slices through
-//     distributed shared memory in fixed rank order (deterministic, no
-//     atomics, no global scratch), then the optional LoRA term
-//     (alpha/r) * T[m,:] . B[:, n] with T = X*A is added and Y is stored.
+// Structure (HBM streaming, one CTA per SM):
+//   * a cluster of S CTAs splits K into S slices of GS <= 32 scale groups;
+//     the cluster owns a contiguous column range;
+//   * a producer warp streams the cluster range's packed weights (2-D TMA,
+//     CC columns x the slice's bytes per chunk) and scales (4-byte cp.async,
+//     zero-filled outside the matrix) for this CTA's K slice into a
+//     shared-memory ring, starting before griddepcontrol.wait, so under
+//     programmatic dependent launch the weights of this launch stream in while
+//     the previous launch drains;
+//   * 8 consumer warps: lane l owns scale group l of the slice and keeps that
+//     group's 32 x values (up to 4 rows) in registers for the whole kernel;
+//     per column it reads one 16-byte word (32 nibbles) and one scale from
+//     shared memory, forms sum_j x_j * v_j exactly-unpacked in fp32, scales
+//     once per group, and the warp reduce-scatters its CW columns x rows
+//     partials across lanes with a butterfly (V-1+5-log2 V shuffles);
+//   * the K-slice partials are summed across the cluster through distributed
+//     shared memory in fixed rank order (deterministic, no atomics, no global
+//     scratch), the optional LoRA term (alpha/r) * T[m,:] . B[:, n] with
+//     T = X*A is added and Y is stored.
 #include <cooperative_groups.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -36,206 +42,303 @@ namespace q4 {
 
 namespace {
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kGemvCols = 4;  // columns per warp step
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kCW = 2;                                   // columns per warp per chunk
+constexpr int kCC = kConsumerWarps * kCW;                // columns per chunk (16)
+constexpr int kStages = 4;
 
-// Nibble pair unpack: from a packed word q (8 nibbles, k = 0..7 at bits 4k),
-// returns v_k as an exact float via the 2^23 magic-number trick:
-//   (u ^ 8) = v + 8 in [0, 15];  float(0x4B000000 | (v+8)) = 2^23 + v + 8.
+// Exact unpack of one packed word (8 nibbles, k = 0..7 at bits 4k) to floats
+// with the 2^23 magic number: (u ^ 8) = v + 8 in [0, 15], and
+// float(0x4B000000 | (v + 8)) = 2^23 + v + 8.
 __device__ __forceinline__ void unpack8(uint32_t q, float (&v)[8]) {
-    const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;          // k = 0, 2, 4, 6
-    const uint32_t hi = ((q >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // k = 1, 3, 5, 7
-    const float bias = 8388616.0f;                                 // 2^23 + 8
+    const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;         // k = 0, 2, 4, 6
+    const uint32_t hi = ((q >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;  // k = 1, 3, 5, 7
+    const float bias = 8388616.0f;                                // 2^23 + 8
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-        // prmt selector 0x744b: byte b of the packed word into byte 0, zero
-        // bytes into bytes 1-2, 0x4B (exponent of 2^23) into byte 3.
-        uint32_t e = __byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b));
-        uint32_t o = __byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b));
-        v[2 * b] = __uint_as_float(e) - bias;
-        v[2 * b + 1] = __uint_as_float(o) - bias;
+        // byte_perm selector 0x744b: byte b of the word -> byte 0, zero bytes
+        // -> bytes 1-2, 0x4B (the exponent byte of 2^23) -> byte 3.
+        v[2 * b] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))) - bias;
+        v[2 * b + 1] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))) - bias;
     }
 }
 
-// Swizzled float offset of X value (row m, k within the slice) for M rows
-// stored group-major: [group][k in group 0..31][m], float4 units of a group
-// XOR-ed with (group & 7).
+// X slice in shared memory: [group][k in group 0..31][row m] (M floats per k),
+// float4 units of a group XOR-swizzled with (group & 7) so the 8 lanes of a
+// quarter warp, reading the same unit of 8 different groups, hit 8 different
+// bank quads.
 template <int M>
 __device__ __forceinline__ int xs_offset(int g, int unit) {
     return g * (32 * M) + ((unit ^ (g & 7)) << 2);
 }
 
+// Butterfly reduce-scatter of V values across the 32 lanes of a warp.  On
+// return v[0] of lane l holds the warp-wide sum of value index
+// idx(l) = (bit-reversal-free) ((l >> (5 - log2 V)) ... see value_index().
+template <int V>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[V], int lane) {
+    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
+#pragma unroll
+    for (int half = V / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+        const bool upper = (lane & bit) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+        }
+    }
+    float r = v[0];
+    constexpr int used = (V == 1) ? 0 : (V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5);
+#pragma unroll
+    for (int bit = 16 >> used; bit >= 1; bit >>= 1) r += __shfl_xor_sync(0xffffffffu, r, bit);
+    return r;
+}
+
+// Which of the V values lane `lane` holds after warp_reduce_scatter<V>: the
+// first step keeps the upper half when lane bit 16 is set, and so on, so the
+// index bits come from lane bits 16, 8, 4, ... (most significant first).
+template <int V>
+__device__ __forceinline__ int value_index(int lane) {
+    int idx = 0;
+#pragma unroll
+    for (int half = V / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1)
+        if (lane & bit) idx += half;
+    return idx;
+}
+
 template <int M>
-__global__ void __launch_bounds__(kGemvThreads)
-    q4_gemv_kernel(const float* __restrict__ x, const uint4* __restrict__ packed, const float* __restrict__ scales,
-                   float* __restrict__ y, int N, int K, int cols_per_cluster, const float* __restrict__ lora_t,
-                   const float* __restrict__ lora_b, int rank, float lora_scale) {
-    extern __shared__ __align__(16) float smem[];
+struct GemvCfg {
+    static constexpr int MR = M < 4 ? M : 4;           // rows per register pass
+    static constexpr int kPasses = (M + MR - 1) / MR;  // 1 or 2
+    static constexpr int V = kCW * (MR == 3 ? 4 : MR); // reduce-scatter width (power of 2)
+};
+
+struct GemvSmem {
+    int GS, GSp;               // groups in the slice; scale row pitch in the ring
+    int w_bytes, s_bytes;      // per stage
+    int stage_bytes;
+    int xs_floats;
+    int part_floats;
+};
+
+__host__ __device__ inline GemvSmem gemv_layout(int M, int K, int S, int cols_per_cluster) {
+    GemvSmem L;
+    L.GS = K / 32 / S;
+    L.GSp = L.GS;
+    L.w_bytes = kCC * L.GS * 16;
+    L.s_bytes = kCC * L.GSp * 4;
+    L.stage_bytes = L.w_bytes + L.s_bytes;
+    L.xs_floats = L.GS * 32 * M;
+    L.part_floats = cols_per_cluster * M;
+    return L;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    q4_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ scales,
+                   const float* __restrict__ x, float* __restrict__ y, int N, int K, int cols_per_cluster,
+                   const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
+                   float lora_scale, int* __restrict__ status) {
+    using C = GemvCfg<M>;
+    extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const int S = static_cast<int>(cluster.num_blocks());
     const int rank_k = static_cast<int>(cluster.block_rank());
     const int cluster_id = blockIdx.x / S;
-    const int KS = K / S;             // slice length (multiple of 32)
-    const int GS = KS / 32;           // groups in the slice
-    const int G = K / 32;             // groups per column
-    const int g0 = rank_k * GS;       // first group of the slice
+    const GemvSmem L = gemv_layout(M, K, S, cols_per_cluster);
+    const int GS = L.GS;
+    const int g0 = rank_k * GS;                // first group of this K slice
     const int n0 = cluster_id * cols_per_cluster;
-    const int n1 = min(N, n0 + cols_per_cluster);
-    const int ncols = max(0, n1 - n0);
+    const int ncols = max(0, min(N, n0 + cols_per_cluster) - n0);
+    const int nchunks = (ncols + kCC - 1) / kCC;
 
-    float* xs = smem;                                  // [GS][32][M] swizzled
-    float* part = smem + static_cast<size_t>(GS) * 32 * M;  // [cols_per_cluster][M]
+    uint8_t* stage_base = smem;
+    float* xs = reinterpret_cast<float*>(smem + kStages * L.stage_bytes);
+    float* part = xs + L.xs_floats;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + L.part_floats + ((L.part_floats & 1) ? 1 : 0));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kStages);
+    auto full = [&](int s) { return smem_u32(bars + s); };
+    auto empty = [&](int s) { return smem_u32(bars + kStages + s); };
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-    // Stage this slice of X (rows 0..M-1, k in [g0*32, g0*32+KS)).
-    for (int idx = tid; idx < GS * 8 * M; idx += kGemvThreads) {
-        // idx enumerates (g, unit) with unit = float4 index inside the group's 32*M floats
-        const int g = idx / (8 * M), unit = idx % (8 * M);
-        float tmp[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int flat = unit * 4 + e;  // = j*M + m
-            const int j = flat / M, m = flat % M;
-            tmp[e] = x[static_cast<size_t>(m) * K + (g0 + g) * 32 + j];
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full(s), 1 + 32);  // TMA expect_tx arrival + 32 producer cp.async arrivals
+            mbar_init(empty(s), kConsumerWarps);
         }
-        *reinterpret_cast<float4*>(xs + xs_offset<M>(g, unit)) = make_float4(tmp[0], tmp[1], tmp[2], tmp[3]);
+        *abort_flag = 0;
+        fence_mbarrier_init();
     }
     __syncthreads();
 
-    // Column steps: warp w handles columns n0 + (step*kGemvWarps + w)*kGemvCols + c.
-    const int steps = (ncols + kGemvCols * kGemvWarps - 1) / (kGemvCols * kGemvWarps);
-    for (int step = 0; step < steps; ++step) {
-        const int cbase = (step * kGemvWarps + warp) * kGemvCols;  // local column of c = 0
-        if (cbase >= ncols) break;
-        float acc[kGemvCols][M];
-#pragma unroll
-        for (int c = 0; c < kGemvCols; ++c)
-#pragma unroll
-            for (int m = 0; m < M; ++m) acc[c][m] = 0.0f;
-
-        // Lanes over the slice's groups; weights for the first group in flight.
-        int g = lane;
-        uint4 wq[kGemvCols];
-        float sc[kGemvCols];
-#pragma unroll
-        for (int c = 0; c < kGemvCols; ++c) {
-            const int n = n0 + cbase + c;
-            const bool ok = (g < GS) && (cbase + c < ncols);
-            const size_t widx = static_cast<size_t>(n) * G + g0 + g;
-            wq[c] = ok ? __ldg(packed + widx) : make_uint4(0u, 0u, 0u, 0u);
-            sc[c] = ok ? __ldg(scales + widx) : 0.0f;
-        }
-        while (g < GS) {
-            // Prefetch the next group of this lane.
-            const int gn = g + 32;
-            uint4 wn[kGemvCols];
-            float sn[kGemvCols];
-#pragma unroll
-            for (int c = 0; c < kGemvCols; ++c) {
-                const int n = n0 + cbase + c;
-                const bool ok = (gn < GS) && (cbase + c < ncols);
-                const size_t widx = static_cast<size_t>(n) * G + g0 + gn;
-                wn[c] = ok ? __ldg(packed + widx) : make_uint4(0u, 0u, 0u, 0u);
-                sn[c] = ok ? __ldg(scales + widx) : 0.0f;
-            }
-            float gacc[kGemvCols][M];
-#pragma unroll
-            for (int c = 0; c < kGemvCols; ++c)
-#pragma unroll
-                for (int m = 0; m < M; ++m) gacc[c][m] = 0.0f;
-#pragma unroll
-            for (int wd = 0; wd < 4; ++wd) {
-                // x values for k = 8*wd .. 8*wd+7, all rows: 8*M floats = 2*M float4 units.
-                float xv[8 * M];
-#pragma unroll
-                for (int u = 0; u < 2 * M; ++u) {
-                    const float4 t = *reinterpret_cast<const float4*>(xs + xs_offset<M>(g, wd * 2 * M + u));
-                    xv[4 * u + 0] = t.x;
-                    xv[4 * u + 1] = t.y;
-                    xv[4 * u + 2] = t.z;
-                    xv[4 * u + 3] = t.w;
-                }
-#pragma unroll
-                for (int c = 0; c < kGemvCols; ++c) {
-                    const uint32_t q = wd == 0 ? wq[c].x : wd == 1 ? wq[c].y : wd == 2 ? wq[c].z : wq[c].w;
-                    float v[8];
-                    unpack8(q, v);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-#pragma unroll
-                        for (int m = 0; m < M; ++m) gacc[c][m] = fmaf(xv[i * M + m], v[i], gacc[c][m]);
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < kGemvCols; ++c)
-#pragma unroll
-                for (int m = 0; m < M; ++m) acc[c][m] = fmaf(sc[c], gacc[c][m], acc[c][m]);
-#pragma unroll
-            for (int c = 0; c < kGemvCols; ++c) {
-                wq[c] = wn[c];
-                sc[c] = sn[c];
-            }
-            g = gn;
-        }
-        // Reduce across lanes (groups); lane 0 parks the slice partials.
-#pragma unroll
-        for (int c = 0; c < kGemvCols; ++c)
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float v = acc[c][m];
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-                acc[c][m] = v;
-            }
+    const int G = K / 32;
+    // Producer warp, all lanes: chunk j -> ring stage j % kStages.  Lane 0
+    // issues the weight TMA (expect_tx), every lane copies its share of the
+    // chunk's scales with cp.async and arrives once those land.
+    auto issue = [&](int j) {
+        const int s = j % kStages;
+        const uint32_t dst = smem_u32(stage_base + s * L.stage_bytes);
         if (lane == 0) {
-#pragma unroll
-            for (int c = 0; c < kGemvCols; ++c)
-                if (cbase + c < ncols)
-#pragma unroll
-                    for (int m = 0; m < M; ++m) part[(cbase + c) * M + m] = acc[c][m];
+            mbar_arrive_expect_tx(full(s), static_cast<uint32_t>(L.w_bytes));
+            tma_load_2d(dst, &tmap_w, full(s), g0 * 4, n0 + j * kCC);
         }
+        const uint32_t sdst = dst + L.w_bytes;
+        for (int e = lane; e < kCC * GS; e += 32) {
+            const int cl = e / GS, gg = e % GS;
+            const int n = n0 + j * kCC + cl;
+            const bool ok = n < N;
+            const float* src = scales + (static_cast<size_t>(ok ? n : 0) * G + g0 + gg);
+            cp_async4(sdst + e * 4, src, ok ? 4u : 0u);
+        }
+        cp_async_arrive_noinc(full(s));
+    };
+    int issued = 0;
+    if (warp == kConsumerWarps) {
+        if (lane == 0) tma_prefetch_desc(&tmap_w);
+        // Weights and scales do not depend on the previous launch: the first
+        // ring's worth streams in before griddepcontrol.wait.
+        for (; issued < nchunks && issued < kStages; ++issued) issue(issued);
+    }
+    pdl_wait();  // X (and LoRA T) may be written by the previous launch
+    if (warp < kConsumerWarps) {
+        // Stage this CTA's slice of X: rows 0..M-1, k in [g0*32, g0*32 + 32*GS).
+        for (int idx = tid; idx < GS * 8 * M; idx += kConsumerWarps * 32) {
+            const int g = idx / (8 * M), unit = idx % (8 * M);
+            float t[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int flat = unit * 4 + e;  // = j*M + m
+                t[e] = x[static_cast<size_t>(flat % M) * K + (g0 + g) * 32 + flat / M];
+            }
+            *reinterpret_cast<float4*>(xs + xs_offset<M>(g, unit)) = make_float4(t[0], t[1], t[2], t[3]);
+        }
+    }
+    __syncthreads();
+    // Dependent launches may start their prologue (their own weight stream).
+    pdl_launch_dependents();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------- producer: refill ring --
+        for (; issued < nchunks; ++issued) {
+            const int j = issued;
+            if (!mbar_wait(empty(j % kStages), ((j / kStages) - 1) & 1u, abort_flag, status, kStatusTimeoutGemv))
+                break;
+            issue(j);
+        }
+    }
+    if (warp < kConsumerWarps) {
+        // ---------------------------------------------------- consumers --
+        const bool active = lane < GS;
+        const int g = active ? lane : 0;
+        float xr[32][C::MR];
+        // This lane's 32 x values for rows mbase .. mbase+MR-1.
+        auto load_x = [&](int mbase) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+#pragma unroll
+                for (int r = 0; r < C::MR; ++r) {
+                    const int m = mbase + r;
+                    const int flat = j * M + (m < M ? m : 0);
+                    const float v = xs[xs_offset<M>(g, flat >> 2) + (flat & 3)];
+                    xr[j][r] = (active && m < M) ? v : 0.0f;
+                }
+        };
+        if (C::kPasses == 1) load_x(0);
+        for (int jc = 0; jc < nchunks; ++jc) {
+            const int s = jc % kStages;
+            if (!mbar_wait(full(s), (jc / kStages) & 1u, abort_flag, status, kStatusTimeoutGemv)) break;
+            const uint8_t* wst = stage_base + s * L.stage_bytes;
+            const float* sst = reinterpret_cast<const float*>(wst + L.w_bytes);
+#pragma unroll 1
+            for (int pass = 0; pass < C::kPasses; ++pass) {
+                const int mbase = pass * C::MR;
+                if (C::kPasses > 1) load_x(mbase);
+                float acc[C::V];
+#pragma unroll
+                for (int i = 0; i < C::V; ++i) acc[i] = 0.0f;
+                constexpr int RP = C::V / kCW;  // row slots per column (power of two)
+#pragma unroll
+                for (int c = 0; c < kCW; ++c) {
+                    const int cl = warp * kCW + c;  // column inside the chunk
+                    const uint4 q = *reinterpret_cast<const uint4*>(wst + (cl * GS + g) * 16);
+                    const float sc = active ? sst[cl * L.GSp + g] : 0.0f;
+                    float gacc[C::MR];
+#pragma unroll
+                    for (int r = 0; r < C::MR; ++r) gacc[r] = 0.0f;
+                    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int wd = 0; wd < 4; ++wd) {
+                        float v[8];
+                        unpack8(words[wd], v);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+#pragma unroll
+                            for (int r = 0; r < C::MR; ++r) gacc[r] = fmaf(xr[wd * 8 + i][r], v[i], gacc[r]);
+                    }
+#pragma unroll
+                    for (int r = 0; r < C::MR; ++r) acc[c * RP + r] = sc * gacc[r];
+                }
+                const float red = warp_reduce_scatter<C::V>(acc, lane);
+                const int idx = value_index<C::V>(lane);
+                const int c = idx / RP, r = idx % RP;
+                const int col = jc * kCC + warp * kCW + c;
+                const int m = mbase + r;
+                // Each value is held by 32/V lanes; the lowest one writes.
+                const bool writer = (lane & ((32 / C::V) - 1)) == 0;
+                if (writer && r < C::MR && m < M && col < ncols) part[col * M + m] = red;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty(s));
+        }
+    }
+
+    if (warp == kConsumerWarps && *abort_flag) {
+        // Abort path: let this CTA's copies in flight land before it exits.
+        cp_async_wait_all();
+        if (lane == 0)
+            for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
+                mbar_drain(full(j % kStages), (j / kStages) & 1u);
     }
 
     // Cross-slice reduction through distributed shared memory, fixed order.
     cluster.sync();
-    for (int idx = tid; idx < ncols * M; idx += kGemvThreads) {
-        const int lc = idx / M, m = idx % M;
-        if (lc % S != rank_k) continue;  // columns interleaved over the cluster's CTAs
-        float sum = 0.0f;
-        for (int r = 0; r < S; ++r) {
-            const float* rp = cluster.map_shared_rank(part, r);
-            sum += rp[idx];
+    if (*abort_flag == 0) {
+        for (int idx = tid; idx < ncols * M; idx += kGemvThreads) {
+            const int lc = idx / M, m = idx % M;
+            if (lc % S != rank_k) continue;  // columns interleaved over the cluster's CTAs
+            float sum = 0.0f;
+            for (int r = 0; r < S; ++r) sum += cluster.map_shared_rank(part, r)[idx];
+            const int n = n0 + lc;
+            if (lora_t != nullptr) {
+                float d = 0.0f;
+                for (int j = 0; j < rank; ++j)
+                    d = fmaf(lora_t[m * rank + j], lora_b[static_cast<size_t>(j) * N + n], d);
+                sum = fmaf(lora_scale, d, sum);
+            }
+            y[static_cast<size_t>(m) * N + n] = sum;
         }
-        const int n = n0 + lc;
-        if (lora_t != nullptr) {
-            float d = 0.0f;
-            for (int j = 0; j < rank; ++j)
-                d = fmaf(lora_t[m * rank + j], lora_b[static_cast<size_t>(j) * N + n], d);
-            sum = fmaf(lora_scale, d, sum);
-        }
-        y[static_cast<size_t>(m) * N + n] = sum;
     }
     cluster.sync();  // keep this CTA's partials alive until every peer has read them
 }
 
+size_t smem_bytes_for(int M, int K, int S, int cols_per_cluster) {
+    const GemvSmem L = gemv_layout(M, K, S, cols_per_cluster);
+    return static_cast<size_t>(kStages) * L.stage_bytes + (L.xs_floats + L.part_floats + 1) * 4 + 2 * kStages * 8 +
+           16;
+}
+
 template <int M>
-int launch_gemv_m(const GemvArgs& a, cudaStream_t stream) {
-    const int S = a.cluster_k;
-    const int KS = a.K / S;
-    const int GS = KS / 32;
-    const size_t smem = (static_cast<size_t>(GS) * 32 * M + static_cast<size_t>(a.cols_per_cluster) * M) * sizeof(float);
+int max_clusters_m(int K, int S, int cols_per_cluster) {
+    const size_t smem = smem_bytes_for(M, K, S, cols_per_cluster);
     auto kern = q4_gemv_kernel<M>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) return static_cast<int>(e);
-    }
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+        return 0;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(S * a.clusters), 1, 1);
+    cfg.gridDim = dim3(static_cast<unsigned>(S), 1, 1);
     cfg.blockDim = dim3(kGemvThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = static_cast<unsigned>(S);
@@ -243,17 +346,58 @@ int launch_gemv_m(const GemvArgs& a, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a.x, reinterpret_cast<const uint4*>(a.packed), a.scales, a.y, a.N,
-                                       a.K, a.cols_per_cluster, a.lora_t, a.lora_b, a.rank, a.lora_scale);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) return 0;
+    return n;
+}
+
+template <int M>
+int launch_gemv_m(const GemvArgs& a, cudaStream_t stream) {
+    const int S = a.cluster_k;
+    const size_t smem = smem_bytes_for(M, a.K, S, a.cols_per_cluster);
+    auto kern = q4_gemv_kernel<M>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(S * a.clusters), 1, 1);
+    cfg.blockDim = dim3(kGemvThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, kern, a.tmap_w, a.scales, a.x, a.y, a.N, a.K, a.cols_per_cluster, a.lora_t,
+                           a.lora_b, a.rank, a.lora_scale, a.status);
     return static_cast<int>(e);
 }
 
 }  // namespace
 
 size_t gemv_smem_bytes(int M, int K, int cluster_k, int cols_per_cluster) {
-    const int GS = K / cluster_k / 32;
-    return (static_cast<size_t>(GS) * 32 * M + static_cast<size_t>(cols_per_cluster) * M) * sizeof(float);
+    return smem_bytes_for(M, K, cluster_k, cols_per_cluster);
 }
+
+int gemv_max_active_clusters(int M, int K, int cluster_k, int cols_per_cluster) {
+    switch (M) {
+        case 1: return max_clusters_m<1>(K, cluster_k, cols_per_cluster);
+        case 2: return max_clusters_m<2>(K, cluster_k, cols_per_cluster);
+        case 3: return max_clusters_m<3>(K, cluster_k, cols_per_cluster);
+        case 4: return max_clusters_m<4>(K, cluster_k, cols_per_cluster);
+        case 5: return max_clusters_m<5>(K, cluster_k, cols_per_cluster);
+        case 6: return max_clusters_m<6>(K, cluster_k, cols_per_cluster);
+        case 7: return max_clusters_m<7>(K, cluster_k, cols_per_cluster);
+        case 8: return max_clusters_m<8>(K, cluster_k, cols_per_cluster);
+        default: return 0;
+    }
+}
+
+int gemv_chunk_columns() { return kCC; }
 
 int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
     switch (a.M) {

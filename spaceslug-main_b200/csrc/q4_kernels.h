@@ -14,8 +14,8 @@ namespace q4 {
 enum class Operand16 : int { kF16 = 0, kBF16 = 1 };
 
 struct GemvArgs {
+    CUtensorMap tmap_w;      // packed weights as uint32 [N][K/8], box (K/S/8) x 16 columns, no swizzle
     const float* x;          // [M][K] fp32, device
-    const uint32_t* packed;  // reference layout, K*N/8 words, device
     const float* scales;     // [N][K/32], device
     float* y;                // [M][N] fp32, device
     int M, N, K;
@@ -26,20 +26,25 @@ struct GemvArgs {
     const float* lora_b;     // [rank][N] or nullptr
     int rank;
     float lora_scale;        // alpha / rank
+    int* status;             // kernel status word (0 = ok)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t stream);
 size_t gemv_smem_bytes(int M, int K, int cluster_k, int cols_per_cluster);
+int gemv_chunk_columns();
+// Max co-resident clusters of the GEMV for these parameters (0 on error).
+int gemv_max_active_clusters(int M, int K, int cluster_k, int cols_per_cluster);
 
 struct GemmArgs {
-    CUtensorMap tmap_x16;     // [M][K] 16-bit, box 64 x 128, 128B swizzle
-    CUtensorMap tmap_w;       // packed as uint32 [N][K/8], box 8 x BN, no swizzle
+    CUtensorMap tmap_x16;     // [M][K] 16-bit, box 64 x (128 * halves), 128B swizzle
+    CUtensorMap tmap_w;       // packed as uint32 [N][K/8], box 8 x 128, no swizzle
     const float* scales;      // [N][K/32]
     const int* col_exp;       // [N] power-of-two exponent applied to the column's scales, or nullptr
     const int* row_exp;       // [M] power-of-two exponent applied to X rows, or nullptr
     float* y;                 // [M][N]
     int M, N, K;
     Operand16 op;
-    int bn;                   // 128 or 256
+    int halves;               // output tile rows = 128 * halves (1 or 2); tile columns = 128
+    int sm_count;             // persistent grid size limit
     const float* lora_t;      // [M][rank] fp32 or nullptr
     const float* lora_b;      // [rank][N] fp32
     int rank;
@@ -47,7 +52,7 @@ struct GemmArgs {
     int* status;              // kernel status word (0 = ok)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
-size_t gemm_smem_bytes(int bn);
+int gemm_tiles(int M, int N, int halves);
 
 // fp32 -> 16-bit cast of X with per-row power-of-two exponents (row_exp may be
 // nullptr: plain round-to-nearest cast).

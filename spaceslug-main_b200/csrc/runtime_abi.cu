@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -167,17 +168,57 @@ struct Problem {
     int M, N, K;
 };
 
-void choose_gemv(const DeviceCtx& c, int M, int N, int K, q4::GemvArgs& a) {
+// GEMV launch geometry.  K is split over a cluster of S CTAs (S | G, slice
+// of GS = G/S <= 32 groups so one lane owns one group); one CTA per SM; the
+// column range per cluster is a multiple of the 16-column chunk.  Returns
+// false when the GEMV cannot take the shape (the caller uses the GEMM).
+struct GemvGeom {
+    int S = 0, clusters = 0, cols = 0;
+};
+std::mutex g_geom_mu;
+std::vector<std::pair<std::array<int, 4>, int>> g_geom_cache;  // (M, K, S, cols) -> max clusters
+
+int cached_max_clusters(int M, int K, int S, int cols) {
+    std::array<int, 4> key{M, K, S, cols};
+    {
+        std::lock_guard<std::mutex> lk(g_geom_mu);
+        for (auto& e : g_geom_cache)
+            if (e.first == key) return e.second;
+    }
+    const int v = q4::gemv_max_active_clusters(M, K, S, cols);
+    std::lock_guard<std::mutex> lk(g_geom_mu);
+    g_geom_cache.emplace_back(key, v);
+    return v;
+}
+
+bool choose_gemv(const DeviceCtx& c, int M, int N, int K, GemvGeom& out) {
     const int G = K / 32;
-    int S = 1;
-    while (S < 8 && G % (2 * S) == 0 && G / (2 * S) >= 32) S *= 2;
-    const int target = std::max(1, (2 * c.sm_count) / S);
-    int cols = (N + target - 1) / target;
-    cols = (cols + 3) / 4 * 4;
-    a.cluster_k = S;
-    a.cols_per_cluster = cols;
-    a.clusters = (N + cols - 1) / cols;
-    (void)M;
+    int S = 0;
+    for (int cand = 1; cand <= 8; cand *= 2) {
+        if (G % cand) continue;
+        const int gs = G / cand;
+        if (gs > 32) continue;
+        S = cand;
+        break;
+    }
+    if (S == 0) return false;
+    const int cc = q4::gemv_chunk_columns();
+    const int target = std::max(1, c.sm_count / S);
+    int clusters = std::max(1, std::min(target, (N + cc - 1) / cc));
+    int cols = (N + clusters - 1) / clusters;
+    cols = (cols + cc - 1) / cc * cc;
+    if (q4::gemv_smem_bytes(M, K, S, cols) > 200 * 1024) return false;
+    const int resident = cached_max_clusters(M, K, S, cols);
+    if (resident <= 0) return false;
+    if (resident < clusters) {
+        clusters = resident;
+        cols = (N + clusters - 1) / clusters;
+        cols = (cols + cc - 1) / cc * cc;
+    }
+    out.S = S;
+    out.cols = cols;
+    out.clusters = (N + cols - 1) / cols;
+    return true;
 }
 
 void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
@@ -199,12 +240,18 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     if (p.rank > 0) check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream), "lora_xa");
     const float lscale = p.rank > 0 ? p.alpha / static_cast<float>(p.rank) : 0.0f;
 
-    if (p.M <= 8) {
+    GemvGeom geo;
+    if (p.M <= 8 && choose_gemv(c, p.M, p.N, p.K, geo)) {
         q4::GemvArgs a{};
-        a.x = p.x; a.packed = p.packed; a.scales = p.scales; a.y = p.y;
+        const int GS = p.K / 32 / geo.S;
+        encode_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
+                  static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, static_cast<uint32_t>(GS * 4),
+                  static_cast<uint32_t>(q4::gemv_chunk_columns()), CU_TENSOR_MAP_SWIZZLE_NONE);
+        a.x = p.x; a.scales = p.scales; a.y = p.y;
         a.M = p.M; a.N = p.N; a.K = p.K;
-        choose_gemv(c, p.M, p.N, p.K, a);
+        a.cluster_k = geo.S; a.clusters = geo.clusters; a.cols_per_cluster = geo.cols;
         a.lora_t = lora_t; a.lora_b = p.rank > 0 ? p.lora_b : nullptr; a.rank = p.rank; a.lora_scale = lscale;
+        a.status = c.status;
         check_launch(q4::launch_gemv(a, stream), "gemv launch");
         return;
     }
@@ -221,14 +268,15 @@ void run_problem(const Problem& p, cudaStream_t stream) {
         check_launch(q4::launch_col_exp(p.scales, static_cast<int*>(cexp.p), p.N, p.K, stream), "col_exp");
 
     q4::GemmArgs g{};
-    const long tiles256 = static_cast<long>((p.M + 127) / 128) * ((p.N + 255) / 256);
-    g.bn = tiles256 >= c.sm_count ? 256 : 128;
+    // 256-row tiles halve the dequant work per FLOP; fall back to 128-row
+    // tiles when 256-row tiles would leave SMs idle.
+    g.halves = q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count ? 2 : 1;
+    g.sm_count = c.sm_count;
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
-              static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) * 2, 64, 128,
-              CU_TENSOR_MAP_SWIZZLE_128B);
+              static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) * 2, 64,
+              static_cast<uint32_t>(128 * g.halves), CU_TENSOR_MAP_SWIZZLE_128B);
     encode_2d(&g.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
-              static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8, static_cast<uint32_t>(g.bn),
-              CU_TENSOR_MAP_SWIZZLE_NONE);
+              static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
     g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
     g.lora_t = lora_t; g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
