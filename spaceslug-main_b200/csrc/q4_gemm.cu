@@ -239,30 +239,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool col_ok = n < N;
             const float cs = (col_exp != nullptr && col_ok) ? exp2i(col_exp[n]) : 1.0f;
             const float* srow = scales + static_cast<size_t>(col_ok ? n : 0) * G;
-            float sc = (col_ok && hh < G) ? __ldg(srow + hh) : 0.0f;
+            // Scales of the next four k-steps in flight (L2 latency exceeds one
+            // k-step), rotated through registers.
+            auto scale_at = [&](int kt) {
+                const int g = kt * 2 + hh;
+                return (col_ok && g < G) ? __ldg(srow + g) : 0.0f;
+            };
+            float s0 = scale_at(0), s1 = scale_at(1), s2 = scale_at(2), s3 = scale_at(3);
             for (int kt = 0; kt < KT; ++kt, ++it) {
                 const int s = it % ST;
                 const uint32_t ph = (it / ST) & 1u;
-                const int gn = (kt + 1) * 2 + hh;
-                const float sn = (col_ok && gn < G) ? __ldg(srow + gn) : 0.0f;  // next step's scale
+                const float sc = s0;
+                s0 = s1;
+                s1 = s2;
+                s2 = s3;
+                s3 = scale_at(kt + 4);
                 if (!mbar_wait(full_r(s), ph, abort_flag, status, kStatusTimeoutDequant)) {
                     ok = false;
                     break;
                 }
                 const uint4 q = *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
                 const float sv = sc * cs;
-                const float2 s2 = make_float2(sv, sv);
+                const float2 s2v = make_float2(sv, sv);
                 uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
                 const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int chunk = (hh * 4 + j) ^ (nl & 7);
-                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_word<T16>(words[j], s2);
+                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_word<T16>(words[j], s2v);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(full_b(s));
-                sc = sn;
             }
         }
     } else {
@@ -276,6 +284,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(acc_full(b), u & 1u, abort_flag, status, kStatusTimeoutEpilogue)) break;
             tc_fence_after_sync();
             const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
+            // 2^-col_exp of the tile's 128 columns: lane l holds columns
+            // n0 + 4l .. 4l+3; element e of chunk c is shuffled from lane
+            // (16c + e) / 4.
+            float cf[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + lane * 4 + j;
+                cf[j] = (col_exp != nullptr && n < N) ? exp2i(-col_exp[n]) : 1.0f;
+            }
 #pragma unroll 1
             for (int h = 0; h < H; ++h) {
                 const int row = m0 + h * 128 + quarter * 32 + lane;
@@ -290,14 +307,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld16(tcol + static_cast<uint32_t>(c * 16), r);
                     tmem_ld_wait();
                     const int nb = n0 + c * 16;
-                    if (nb >= N) continue;  // warp-uniform
                     float v[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const int n = nb + e;
-                        const float cinv = (col_exp != nullptr && n < N) ? exp2i(-col_exp[n]) : 1.0f;
+                        const float cinv = __shfl_sync(0xffffffffu, cf[e & 3], c * 4 + (e >> 2));
                         v[e] = __uint_as_float(r[e]) * rs * cinv;
                     }
+                    if (nb >= N) continue;  // warp-uniform
                     if (lora_t != nullptr && row_ok) {
                         float d[16];
 #pragma unroll
