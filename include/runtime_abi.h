@@ -115,6 +115,22 @@ int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, 
 int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m);
 int spaceslug_q4_weights_destroy(spaceslug_q4_weights* w);
 
+/* No counterpart in the reference.  The decode GEMV with the fused LoRA term
+ * (device pointers, asynchronous on `stream`, same result as
+ * spaceslug_q4gemm_device with the same arguments) for callers that cannot
+ * allocate device memory: graph-capturing hosts whose graphs must hold no
+ * memory nodes, serving loops that forbid allocation on the hot path, plugin
+ * hosts that keep all device memory for themselves.  It allocates nothing: its
+ * only scratch, T = X*A, lives in a fixed 2 KB static device array, so
+ * 1 <= m <= 8 and 1 <= rank <= 64; and, as for the decode GEMV itself, K/32
+ * must split into 1, 2, 4 or 8 equal slices of at most 32 scale groups (every
+ * K <= 1024 and every multiple of 256 up to 8192 does); other shapes return 1.  The first call on each device
+ * sets up the array's address (make it before any stream capture).  All calls
+ * on a device share the array: calls that overlap on the GPU race. */
+int spaceslug_q4gemv_lora_noalloc(const float* x, const uint32_t* packed, const float* scales, const float* lora_a,
+                                  const float* lora_b, uint32_t rank, float alpha, float* y, uint32_t m, uint32_t n,
+                                  uint32_t k, void* stream);
+
 /* Operand type of the tensor-core path: 0 = f16 with exact power-of-two
  * row/column exponents (default), 1 = bf16.  Returns the previous value, or
  * -1 for an invalid type. */

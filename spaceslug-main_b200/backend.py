@@ -40,6 +40,8 @@ _SIGNATURES = {
                               ctypes.c_int),
     "spaceslug_q4gemm_device": ([_vp, _vp, _vp, _vp, _vp, _u32, ctypes.c_float, _vp, _u32, _u32, _u32, _vp],
                                 ctypes.c_int),
+    "spaceslug_q4gemv_lora_noalloc": ([_vp, _vp, _vp, _vp, _vp, _u32, ctypes.c_float, _vp, _u32, _u32, _u32, _vp],
+                                      ctypes.c_int),
     "spaceslug_q4_weights_create": ([_u32p, _f32p, _u32, _u32, _u32, _u32, ctypes.c_int, ctypes.POINTER(_vp)],
                                     ctypes.c_int),
     "spaceslug_q4_weights_set_lora": ([_vp, _f32p, _f32p, _u32, ctypes.c_float], ctypes.c_int),

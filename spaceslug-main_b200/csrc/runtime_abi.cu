@@ -317,6 +317,37 @@ void d2h(void* dst, const void* src, size_t bytes, cudaStream_t s) {
 
 }  // namespace
 
+// Helpers shared with csrc/noalloc.cu (the no-allocation entry point).  They
+// reuse the GEMV geometry and tensor-map encoding above without touching the
+// per-device context, which allocates on first use.
+namespace q4rt {
+bool gemv_geometry(int sm_count, int M, int N, int K, int* S, int* clusters, int* cols) {
+    DeviceCtx tmp;
+    tmp.sm_count = sm_count;
+    GemvGeom geo;
+    if (!choose_gemv(tmp, M, N, K, geo)) return false;
+    *S = geo.S;
+    *clusters = geo.clusters;
+    *cols = geo.cols;
+    return true;
+}
+
+bool encode_gemv_weights(CUtensorMap* map, const uint32_t* packed, int N, int K, int S) {
+    try {
+        encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, packed, static_cast<uint64_t>(K) / 8,
+                  static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, static_cast<uint32_t>(K / 32 / S * 4),
+                  static_cast<uint32_t>(q4::gemv_chunk_columns()), CU_TENSOR_MAP_SWIZZLE_NONE);
+        return true;
+    } catch (...) {
+        return false;
+    }
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int set_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace q4rt
+
 struct spaceslug_q4_weights {
     int device = 0;
     int K = 0, N = 0;  // N = number of kept columns
