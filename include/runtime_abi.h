@@ -136,6 +136,13 @@ int spaceslug_q4gemv_lora_noalloc(const float* x, const uint32_t* packed, const 
  * -1 for an invalid type. */
 int spaceslug_q4_set_operand_type(int type);
 
+/* Tensor-core GEMM kernel selection for M > 8: 0 = automatic (default),
+ * 1 = single-CTA kernel with 128-row tiles, 2 = CTA-pair (cta_group::2)
+ * kernel, 3 = single-CTA kernel with 256-row tiles.  Results are the
+ * same up to fp32 summation order.  Returns the previous value, or -1 for an
+ * invalid value. */
+int spaceslug_q4_set_gemm_variant(int variant);
+
 /* Reads and clears the kernel status word of `device` (0 = no kernel wait
  * has timed out since the last call).  Synchronises the device. */
 int spaceslug_q4_device_status(int device);

@@ -49,6 +49,7 @@ _SIGNATURES = {
     "spaceslug_q4_weights_run_host": ([_vp, _f32p, _f32p, _u32], ctypes.c_int),
     "spaceslug_q4_weights_destroy": ([_vp], ctypes.c_int),
     "spaceslug_q4_set_operand_type": ([ctypes.c_int], ctypes.c_int),
+    "spaceslug_q4_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
     "spaceslug_last_error": ([], ctypes.c_char_p),
@@ -190,6 +191,11 @@ class BackendSession:
     def set_operand_type(self, kind: str) -> str:
         prev = self.raw("spaceslug_q4_set_operand_type")({"f16": 0, "bf16": 1}[kind])
         return {0: "f16", 1: "bf16"}.get(prev, "?")
+
+    def set_gemm_variant(self, variant: str) -> str:
+        names = {"auto": 0, "single": 1, "pair": 2, "single256": 3}
+        prev = self.raw("spaceslug_q4_set_gemm_variant")(names[variant])
+        return {v: k for k, v in names.items()}.get(prev, "?")
 
     def device_status(self, device: int = 0) -> int:
         return int(self.raw("spaceslug_q4_device_status")(device))

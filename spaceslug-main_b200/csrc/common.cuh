@@ -109,6 +109,29 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// ----------------------------------------------------- cluster (CTA pair) --
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// Arrive on an mbarrier given by a shared::cluster address (possibly the
+// peer CTA's), with the default release semantics of mbarrier.arrive.  Data a
+// thread wrote to shared memory for the peer's UMMA is ordered by a
+// fence.proxy.async before this arrive.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // --------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -119,6 +142,17 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0, int32_t c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the CTA pair's leader (`bar` is a shared::cluster address,
+// e.g. from mapa_shared(local, 0)); the data lands only in this CTA.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
             dst),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
@@ -155,6 +189,35 @@ __device__ __forceinline__ void tc_fence_before_sync() {
 }
 __device__ __forceinline__ void tc_fence_after_sync() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// CTA-pair (cta_group::2) variants: TMEM is allocated in both CTAs by the
+// same warp of each; the leader issues M=256 MMAs whose A rows and B columns
+// are split between the two CTAs' shared memory at the same offsets.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on the mbarrier at shared::cluster address `bar` (this CTA's or the
+// peer's) once all previously issued pair MMAs of this thread completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+                 : "memory");
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f16 (A, B both f16 or both
@@ -221,6 +284,42 @@ __device__ __forceinline__ uint32_t elect_one() {
         "selp.b32 %0, 1, 0, px;\n\t}"
         : "=r"(pred));
     return pred;
+}
+
+// ------------------------------------------------------ warp reductions --
+// Butterfly reduce-scatter of V values across the 32 lanes of a warp: after
+// V-1 + 5-log2(V) shuffles each lane returns the warp-wide sum of one of the
+// V values, the one with index value_index<V>(lane).
+template <int V>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[V], int lane) {
+    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
+#pragma unroll
+    for (int half = V / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+        const bool upper = (lane & bit) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+        }
+    }
+    float r = v[0];
+    constexpr int used = (V == 1) ? 0 : (V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5);
+#pragma unroll
+    for (int bit = 16 >> used; bit >= 1; bit >>= 1) r += __shfl_xor_sync(0xffffffffu, r, bit);
+    return r;
+}
+
+// Which of the V values lane `lane` holds after warp_reduce_scatter<V>: the
+// first step keeps the upper half when lane bit 16 is set, and so on, so the
+// index bits come from lane bits 16, 8, 4, ... (most significant first).
+template <int V>
+__device__ __forceinline__ int value_index(int lane) {
+    int idx = 0;
+#pragma unroll
+    for (int half = V / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1)
+        if (lane & bit) idx += half;
+    return idx;
 }
 
 }  // namespace q4

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <type_traits>
 
+#include "common.cuh"
 #include "q4_kernels.h"
 
 namespace q4 {
@@ -137,35 +138,86 @@ __global__ void __launch_bounds__(256) pack_kernel(const int8_t* __restrict__ b_
     packed[static_cast<size_t>(n) * chunks + c] = word;
 }
 
-// One CTA per row m: T[m][j] = sum_k x[m][k] * A[k][j], rank <= 64.
+// T[M][rank] = X[M][K] * A[K][rank], fp32.  CTA (rows 8*blockIdx.x .. +7,
+// rank columns 16*blockIdx.y .. +15, k-chunk blockIdx.z of kXaChunk): threads
+// stride over the chunk's k; each k reads the 8 x values and one 64-byte run
+// of A (coalesced across the warp).  Partials are reduced across lanes with
+// shuffles and across warps in shared memory, then written to T directly
+// (one k-chunk) or to partial[z][M][rank] for lora_xa_reduce_kernel, which
+// sums the chunks in fixed order (deterministic).
+constexpr int kXaRows = 8;
+constexpr int kXaCols = 16;
+constexpr int kXaChunk = 1024;
+constexpr int kXaUnroll = 4;
 __global__ void __launch_bounds__(256) lora_xa_kernel(const float* __restrict__ x, const float* __restrict__ a,
-                                                      float* __restrict__ t, int K, int rank) {
-    __shared__ float part[8][64];
-    const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float acc[64];
+                                                      float* __restrict__ out, int M, int K, int rank, int kchunk) {
+    __shared__ float part[8][kXaRows * kXaCols];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int m0 = blockIdx.x * kXaRows, j0 = blockIdx.y * kXaCols;
+    const int rows = min(kXaRows, M - m0), cols = min(kXaCols, rank - j0);
+    const int k_begin = blockIdx.z * kchunk, k_end = min(K, k_begin + kchunk);
+    float acc[kXaRows][kXaCols];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-    const float* xr = x + static_cast<size_t>(m) * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float xv = xr[k];
-        const float* ar = a + static_cast<size_t>(k) * rank;
+    for (int r = 0; r < kXaRows; ++r)
 #pragma unroll
-        for (int j = 0; j < 64; ++j)
-            if (j < rank) acc[j] = fmaf(xv, ar[j], acc[j]);
+        for (int j = 0; j < kXaCols; ++j) acc[r][j] = 0.0f;
+    const bool vec = (rank % 4 == 0) && cols == kXaCols;
+    for (int kb = k_begin; kb < k_end; kb += kXaUnroll * 256) {
+#pragma unroll
+        for (int u = 0; u < kXaUnroll; ++u) {
+            // clamped indices keep every load in bounds, so the unrolled
+            // iterations' loads are independent
+            const int k = kb + u * 256 + static_cast<int>(threadIdx.x);
+            const bool kok = k < k_end;
+            const int kc = kok ? k : k_begin;
+            float av[kXaCols];
+            const float* arow = a + static_cast<size_t>(kc) * rank + j0;
+            if (vec) {
+#pragma unroll
+                for (int j = 0; j < kXaCols; j += 4) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(arow + j));
+                    av[j] = v.x; av[j + 1] = v.y; av[j + 2] = v.z; av[j + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kXaCols; ++j) av[j] = __ldg(arow + (j < cols ? j : 0));
+            }
+#pragma unroll
+            for (int r = 0; r < kXaRows; ++r) {
+                const float xv = __ldg(x + static_cast<size_t>(m0 + (r < rows ? r : 0)) * K + kc);
+                const float xm = (kok && r < rows) ? xv : 0.0f;
+#pragma unroll
+                for (int j = 0; j < kXaCols; ++j) acc[r][j] = fmaf(xm, j < cols ? av[j] : 0.0f, acc[r][j]);
+            }
+        }
     }
+    // 128 partial sums per thread: four reduce-scatters of 32 values
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-        if (j >= rank) break;
-        float v = acc[j];
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) part[warp][j] = v;
+    for (int q = 0; q < 4; ++q) {
+        float v32[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v32[i] = acc[(q * 32 + i) / kXaCols][(q * 32 + i) % kXaCols];
+        const float red = warp_reduce_scatter<32>(v32, lane);
+        part[warp][q * 32 + value_index<32>(lane)] = red;
     }
     __syncthreads();
-    if (threadIdx.x < rank) {
-        float s = 0.0f;
-        for (int w = 0; w < 8; ++w) s += part[w][threadIdx.x];
-        t[static_cast<size_t>(m) * rank + threadIdx.x] = s;
+    if (threadIdx.x < kXaRows * kXaCols) {
+        const int r = threadIdx.x / kXaCols, j = threadIdx.x % kXaCols;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sum += part[w][threadIdx.x];
+        if (r < rows && j < cols)
+            out[(static_cast<size_t>(blockIdx.z) * M + m0 + r) * rank + j0 + j] = sum;
     }
+}
+
+__global__ void __launch_bounds__(256) lora_xa_reduce_kernel(const float* __restrict__ partial,
+                                                             float* __restrict__ t, int MR, int chunks) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= MR) return;
+    float s = 0.0f;
+    for (int z = 0; z < chunks; ++z) s += partial[static_cast<size_t>(z) * MR + i];
+    t[i] = s;
 }
 
 // Legacy delta (vulkan-runtime/shaders/lora_delta.comp:10-21): one CTA of 64
@@ -219,8 +271,18 @@ int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t
     return static_cast<int>(cudaGetLastError());
 }
 
-int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream) {
-    lora_xa_kernel<<<M, 256, 0, stream>>>(x, a, t, K, rank);
+int lora_xa_chunks(int K) { return (K + kXaChunk - 1) / kXaChunk; }
+
+int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
+                   float* partial) {
+    const int chunks = partial != nullptr ? lora_xa_chunks(K) : 1;
+    const dim3 grid((M + kXaRows - 1) / kXaRows, (rank + kXaCols - 1) / kXaCols, chunks);
+    lora_xa_kernel<<<grid, 256, 0, stream>>>(x, a, chunks > 1 ? partial : t, M, K, rank,
+                                             chunks > 1 ? kXaChunk : K);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || chunks == 1) return static_cast<int>(e);
+    const int mr = M * rank;
+    lora_xa_reduce_kernel<<<(mr + 255) / 256, 256, 0, stream>>>(partial, t, mr, chunks);
     return static_cast<int>(cudaGetLastError());
 }
 

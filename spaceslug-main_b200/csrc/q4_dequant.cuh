@@ -1,0 +1,52 @@
+// Dequantisation helpers shared by the tensor-core GEMM kernels.
+//
+// One packed word holds 8 consecutive k of one column (k = 0..7 at bits 4k,
+// int4 two's complement, vulkan-runtime/shaders/q4gemm.comp:104-116).  The
+// nibbles are unpacked exactly with the 2^23 magic number ((u ^ 8) = v + 8 in
+// [0, 15], float(0x4B000000 | (v + 8)) = 2^23 + v + 8), multiplied by the
+// group scale in fp32 (one rounding: the reference's w = float(v) * scale,
+// q4gemm.comp:116-122) and rounded to the 16-bit MMA operand type.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+#include <type_traits>
+
+namespace q4 {
+
+template <typename T16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (std::is_same<T16, __half>::value) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+
+// Eight weights of one column times s (both lanes of s2) as four 16-bit pairs
+// (k, k+1), processed as packed f32x2.
+template <typename T16>
+__device__ __forceinline__ uint4 dequant_word(uint32_t q, float2 s2) {
+    const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;         // k = 0, 2, 4, 6
+    const uint32_t hi = ((q >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;  // k = 1, 3, 5, 7
+    const float2 nbias = make_float2(-8388616.0f, -8388616.0f);   // -(2^23 + 8)
+    uint32_t out[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        // byte_perm selector 0x744b: byte b -> byte 0, zeros -> bytes 1-2,
+        // 0x4B (the exponent byte of 2^23) -> byte 3.
+        const float2 mg = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))),
+                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))));
+        const float2 w = __fmul2_rn(__fadd2_rn(mg, nbias), s2);
+        out[b] = pack2<T16>(w.x, w.y);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
+
+}  // namespace q4

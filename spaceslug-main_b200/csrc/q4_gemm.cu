@@ -37,6 +37,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "q4_dequant.cuh"
 #include "q4_kernels.h"
 
 namespace q4 {
@@ -69,38 +70,6 @@ struct Cfg {
     static_assert(kSmemAlloc <= 232448, "shared memory budget");
     static_assert(kDequantWarps * 32 == kBN * 2, "one (column, group) unit per dequant thread");
 };
-
-__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
-
-template <typename T16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-    if constexpr (std::is_same<T16, __half>::value) {
-        __half2 h = __floats2half2_rn(lo, hi);
-        return *reinterpret_cast<uint32_t*>(&h);
-    } else {
-        __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-        return *reinterpret_cast<uint32_t*>(&h);
-    }
-}
-
-// Dequantise one packed word (8 consecutive k of one column) times s into
-// four 16-bit pairs: magic-number unpack (exact), one fp32 multiply (RN),
-// 16-bit RN; pairs (k, k+1) are processed as packed f32x2.
-template <typename T16>
-__device__ __forceinline__ uint4 dequant_word(uint32_t q, float2 s2) {
-    const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;
-    const uint32_t hi = ((q >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;
-    const float2 nbias = make_float2(-8388616.0f, -8388616.0f);
-    uint32_t out[4];
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const float2 mg = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))),
-                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))));
-        const float2 w = __fmul2_rn(__fadd2_rn(mg, nbias), s2);
-        out[b] = pack2<T16>(w.x, w.y);
-    }
-    return make_uint4(out[0], out[1], out[2], out[3]);
-}
 
 template <int H, typename T16>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -315,27 +284,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (nb >= N) continue;  // warp-uniform
                     if (lora_t != nullptr && row_ok) {
+                        // (alpha/r) * T[row, :] . B[:, nb .. nb+15], T row in blocks of 16.  Row
+                        // and column indices are clamped instead of branched on, so every load
+                        // stays in bounds and all of a block's loads can be in flight together.
                         float d[16];
 #pragma unroll
                         for (int e = 0; e < 16; ++e) d[e] = 0.0f;
                         const float* trow = lora_t + static_cast<size_t>(row) * rank;
                         const bool full16 = nb + 16 <= N && vec_ok;
-                        for (int j = 0; j < rank; ++j) {
-                            const float tj = __ldg(trow + j);
-                            const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
-                            if (full16) {
+                        for (int j0 = 0; j0 < rank; j0 += 16) {
+                            const int jn = min(16, rank - j0);
+                            float tj[16];
 #pragma unroll
-                                for (int e = 0; e < 16; e += 4) {
-                                    const float4 bv = __ldg(reinterpret_cast<const float4*>(brow + e));
-                                    d[e] = fmaf(tj, bv.x, d[e]);
-                                    d[e + 1] = fmaf(tj, bv.y, d[e + 1]);
-                                    d[e + 2] = fmaf(tj, bv.z, d[e + 2]);
-                                    d[e + 3] = fmaf(tj, bv.w, d[e + 3]);
+                            for (int jj = 0; jj < 16; ++jj) {
+                                const int j = j0 + jj < rank ? j0 + jj : rank - 1;
+                                tj[jj] = jj < jn ? __ldg(trow + j) : 0.0f;
+                            }
+#pragma unroll
+                            for (int jj = 0; jj < 16; ++jj) {
+                                const int j = j0 + jj < rank ? j0 + jj : rank - 1;
+                                const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
+                                if (full16) {
+#pragma unroll
+                                    for (int e = 0; e < 16; e += 4) {
+                                        const float4 bv = __ldg(reinterpret_cast<const float4*>(brow + e));
+                                        d[e] = fmaf(tj[jj], bv.x, d[e]);
+                                        d[e + 1] = fmaf(tj[jj], bv.y, d[e + 1]);
+                                        d[e + 2] = fmaf(tj[jj], bv.z, d[e + 2]);
+                                        d[e + 3] = fmaf(tj[jj], bv.w, d[e + 3]);
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int e = 0; e < 16; ++e) {
+                                        const int n = nb + e < N ? nb + e : N - 1;
+                                        d[e] = fmaf(tj[jj], __ldg(lora_b + static_cast<size_t>(j) * N + n), d[e]);
+                                    }
                                 }
-                            } else {
-#pragma unroll
-                                for (int e = 0; e < 16; ++e)
-                                    if (nb + e < N) d[e] = fmaf(tj, __ldg(brow + e), d[e]);
                             }
                         }
 #pragma unroll

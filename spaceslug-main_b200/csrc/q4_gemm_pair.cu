@@ -1,0 +1,409 @@
+// Prefill GEMM on CTA pairs (cta_group::2):  Y = X . dequant(W) (+ LoRA).
+//
+// Same computation as q4_gemm.cu (the reference's q4gemm.comp:61-175 with
+// w = float(v) * scale, q4gemm.comp:116-122), for large problems.  A cluster
+// of two CTAs on two SMs owns a 256 x 256 output tile:
+//
+//   * each CTA TMA-loads its own 128 rows of the 16-bit X tile and its own
+//     128 columns of packed W per 64-wide k-step, and dequantises those 128
+//     columns into its own shared memory; the X loads count their bytes on
+//     the leader CTA's barrier, the dequant warps of both CTAs arrive on the
+//     leader's barrier;
+//   * the leader issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16): A rows
+//     and B columns are split between the two CTAs' shared memory at the
+//     same offsets, each CTA's TMEM receives its 128 rows x 256 columns;
+//   * each MMA stage is committed to both CTAs' empty barriers, each finished
+//     accumulator to both CTAs' epilogues (two commits, one per CTA);
+//   * both CTAs run their epilogue on their own TMEM (double-buffered: 2 x 256
+//     columns) while the pair computes the next tile.
+//
+// Per SM and k-step this moves 20 KB from L2 (16 KB X + 4 KB W) for 128 x 256
+// x 64 MACs: half the bytes per FLOP of the single-CTA 256 x 128 tile, and
+// each dequantised weight still feeds 256 rows.  Every load lands only in the
+// CTA that issued it.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <type_traits>
+
+#include "common.cuh"
+#include "q4_dequant.cuh"
+#include "q4_kernels.h"
+
+namespace q4 {
+
+namespace {
+
+constexpr int kPairRows = 256;  // tile rows of the pair (128 per CTA)
+constexpr int kPairCols = 256;  // tile columns (128 dequantised per CTA)
+constexpr int kHalf = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 6;
+constexpr int kThreads = 448;   // 14 warps
+constexpr int kDequantWarps = 8;
+constexpr int kEpiWarp0 = 10;
+constexpr int kEpiWarps = 4;
+
+struct PCfg {
+    static constexpr int kABytes = kHalf * kBK * 2;  // 16 KB: this CTA's 128 rows of X
+    static constexpr int kBBytes = kHalf * kBK * 2;  // 16 KB: this CTA's 128 dequantised columns
+    static constexpr int kRBytes = kHalf * kBK / 2;  // 4 KB: their packed nibbles
+    static constexpr int kAOff = 0;
+    static constexpr int kBOff = kAOff + kStages * kABytes;
+    static constexpr int kROff = kBOff + kStages * kBBytes;
+    static constexpr int kBarOff = kROff + kStages * kRBytes;
+    // full_a[S] (leader), full_r[S] (local), full_b[S] (leader), empty[S] (both),
+    // acc_full[2] (both), acc_empty[2] (leader), done (leader)
+    static constexpr int kNumBars = 4 * kStages + 5;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+    static constexpr int kBytes = kMiscOff + 16;
+    static constexpr int kSmemAlloc = kBytes + 1024;
+    static constexpr int kTmemCols = 2 * kPairCols;  // 512
+    static_assert(kSmemAlloc <= 232448, "shared memory budget");
+};
+
+template <typename T16>
+__global__ void __launch_bounds__(kThreads, 1)
+    q4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                        const float* __restrict__ scales, const int* __restrict__ col_exp,
+                        const int* __restrict__ row_exp, float* __restrict__ y, int M, int N, int K,
+                        const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
+                        float lora_scale, int* __restrict__ status) {
+    using C = PCfg;
+    constexpr int ST = kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_base);
+
+    const uint32_t a_s = base + C::kAOff;
+    const uint32_t b_s = base + C::kBOff;
+    const uint32_t r_s = base + C::kROff;
+    const uint32_t bar = base + C::kBarOff;
+    auto full_a = [&](int s) { return bar + 8u * s; };
+    auto full_r = [&](int s) { return bar + 8u * (ST + s); };
+    auto full_b = [&](int s) { return bar + 8u * (2 * ST + s); };
+    auto empty = [&](int s) { return bar + 8u * (3 * ST + s); };
+    auto acc_full = [&](int b) { return bar + 8u * (4 * ST + b); };
+    auto acc_empty = [&](int b) { return bar + 8u * (4 * ST + 2 + b); };
+    const uint32_t done_bar = bar + 8u * (4 * ST + 4);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t crank = cluster_ctarank();
+    const bool leader = crank == 0;
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int npairs = static_cast<int>(gridDim.x >> 1);
+    const int MT = (M + kPairRows - 1) / kPairRows;
+    const int NT = (N + kPairCols - 1) / kPairCols;
+    const int tiles = MT * NT;
+    const int KT = (K + kBK - 1) / kBK;
+    const int G = K / 32;
+    auto leader_addr = [&](uint32_t a) { return mapa_shared(a, 0); };
+
+    if (tid == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(full_a(s), 1);                     // leader's expect_tx (both CTAs' bytes)
+            mbar_init(full_r(s), 1);                     // own expect_tx
+            mbar_init(full_b(s), 2 * kDequantWarps);     // dequant warps of both CTAs
+            mbar_init(empty(s), 1);                      // leader's commit
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full(b), 1);                   // leader's commit
+            mbar_init(acc_empty(b), 2 * kEpiWarps);      // epilogue warps of both CTAs
+        }
+        mbar_init(done_bar, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_holder), C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before_sync();
+    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer --
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                const int m0 = (t % MT) * kPairRows + static_cast<int>(crank) * kHalf;
+                const int nb = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST;
+                    const uint32_t ph = (it / ST) & 1u;
+                    if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(full_a(s), 2u * C::kABytes);
+                    tma_load_2d_pair(a_s + s * C::kABytes, &tmap_x, leader_addr(full_a(s)), kt * kBK, m0);
+                    mbar_arrive_expect_tx(full_r(s), C::kRBytes);
+                    tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), nb);
+                }
+            }
+            if (*abort_flag) {  // let this CTA's copies in flight land before exit
+                for (int j = (it > ST ? it - ST : 0); j < it; ++j) {
+                    mbar_drain(full_r(j % ST), (j / ST) & 1u);
+                    if (leader) mbar_drain(full_a(j % ST), (j / ST) & 1u);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------- MMA (leader CTA only) --
+        if (leader && elect_one()) {
+            const uint32_t idesc = umma_idesc_f16(std::is_same<T16, __half>::value ? 0u : 1u,
+                                                  static_cast<uint32_t>(kPairRows), static_cast<uint32_t>(kPairCols));
+            int it = 0, i = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs, ++i) {
+                const int b = i & 1;
+                const uint32_t u = static_cast<uint32_t>(i >> 1);
+                if (!mbar_wait(acc_empty(b), (u & 1u) ^ 1u, abort_flag, status, kStatusTimeoutMma)) break;
+                tc_fence_after_sync();
+                const uint32_t d0 = tmem_base + static_cast<uint32_t>(b * kPairCols);
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST;
+                    const uint32_t ph = (it / ST) & 1u;
+                    if (!mbar_wait(full_a(s), ph, abort_flag, status, kStatusTimeoutMma) ||
+                        !mbar_wait(full_b(s), ph, abort_flag, status, kStatusTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint64_t ad = umma_desc_k_sw128(a_s + s * C::kABytes + kk * 32);
+                        const uint64_t bd = umma_desc_k_sw128(b_s + s * C::kBBytes + kk * 32);
+                        umma_f16_ss_pair(d0, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit_pair(mapa_shared(empty(s), 0));
+                    umma_commit_pair(mapa_shared(empty(s), 1));
+                }
+                if (ok) {
+                    umma_commit_pair(mapa_shared(acc_full(b), 0));
+                    umma_commit_pair(mapa_shared(acc_full(b), 1));
+                }
+            }
+            umma_commit_pair(mapa_shared(done_bar, 0));  // tracks every MMA issued above
+            mbar_drain(done_bar, 0u);
+        }
+    } else if (warp < kEpiWarp0) {
+        // ------------------------------------------------------- dequant --
+        const int dt = tid - 64;
+        const int nl = dt >> 1, hh = dt & 1;  // unit: column nl of this CTA's half, group half hh
+        int it = 0;
+        bool ok = true;
+        for (int t = pair; t < tiles && ok; t += npairs) {
+            const int n = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf + nl;
+            const bool col_ok = n < N;
+            const float cs = (col_exp != nullptr && col_ok) ? exp2i(col_exp[n]) : 1.0f;
+            const float* srow = scales + static_cast<size_t>(col_ok ? n : 0) * G;
+            auto scale_at = [&](int kt) {
+                const int g = kt * 2 + hh;
+                return (col_ok && g < G) ? __ldg(srow + g) : 0.0f;
+            };
+            float s0 = scale_at(0), s1 = scale_at(1), s2 = scale_at(2), s3 = scale_at(3);
+            for (int kt = 0; kt < KT; ++kt, ++it) {
+                const int s = it % ST;
+                const uint32_t ph = (it / ST) & 1u;
+                const float sc = s0;
+                s0 = s1;
+                s1 = s2;
+                s2 = s3;
+                s3 = scale_at(kt + 4);
+                if (!mbar_wait(full_r(s), ph, abort_flag, status, kStatusTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                const uint4 q = *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
+                const float sv = sc * cs;
+                const float2 s2v = make_float2(sv, sv);
+                uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
+                const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int chunk = (hh * 4 + j) ^ (nl & 7);
+                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_word<T16>(words[j], s2v);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(leader_addr(full_b(s)));
+            }
+        }
+    } else {
+        // ------------------------------------------------------ epilogue --
+        const int quarter = warp & 3;
+        const bool vec_ok = (N % 4) == 0;
+        int i = 0;
+        for (int t = pair; t < tiles; t += npairs, ++i) {
+            const int b = i & 1;
+            const uint32_t u = static_cast<uint32_t>(i >> 1);
+            if (!mbar_wait(acc_full(b), u & 1u, abort_flag, status, kStatusTimeoutEpilogue)) break;
+            tc_fence_after_sync();
+            const int m0 = (t % MT) * kPairRows + static_cast<int>(crank) * kHalf;
+            const int n0 = (t / MT) * kPairCols;
+            // 2^-col_exp of the tile's 256 columns: lane l holds 8l .. 8l+7.
+            float cf[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int n = n0 + lane * 8 + j;
+                cf[j] = (col_exp != nullptr && n < N) ? exp2i(-col_exp[n]) : 1.0f;
+            }
+            const int row = m0 + quarter * 32 + lane;
+            const bool row_ok = row < M;
+            const float rs = (row_exp != nullptr && row_ok) ? exp2i(-row_exp[row]) : 1.0f;
+            float* yrow = y + static_cast<size_t>(row_ok ? row : 0) * N;
+            const uint32_t tcol =
+                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(b * kPairCols);
+#pragma unroll 1
+            for (int c = 0; c < kPairCols / 16; ++c) {
+                uint32_t r[16];
+                tmem_ld16(tcol + static_cast<uint32_t>(c * 16), r);
+                tmem_ld_wait();
+                const int nb = n0 + c * 16;
+                float v[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float cinv = __shfl_sync(0xffffffffu, cf[e & 7], c * 2 + (e >> 3));
+                    v[e] = __uint_as_float(r[e]) * rs * cinv;
+                }
+                if (nb >= N) continue;  // warp-uniform
+                if (lora_t != nullptr && row_ok) {
+                    // (alpha/r) * T[row, :] . B[:, nb .. nb+15], T row in blocks of 16.  Row
+                    // and column indices are clamped instead of branched on, so every load
+                    // stays in bounds and all of a block's loads can be in flight together.
+                    float d[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) d[e] = 0.0f;
+                    const float* trow = lora_t + static_cast<size_t>(row) * rank;
+                    const bool full16 = nb + 16 <= N && vec_ok;
+                    for (int j0 = 0; j0 < rank; j0 += 16) {
+                        const int jn = min(16, rank - j0);
+                        float tj[16];
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int j = j0 + jj < rank ? j0 + jj : rank - 1;
+                            tj[jj] = jj < jn ? __ldg(trow + j) : 0.0f;
+                        }
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int j = j0 + jj < rank ? j0 + jj : rank - 1;
+                            const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
+                            if (full16) {
+#pragma unroll
+                                for (int e = 0; e < 16; e += 4) {
+                                    const float4 bv = __ldg(reinterpret_cast<const float4*>(brow + e));
+                                    d[e] = fmaf(tj[jj], bv.x, d[e]);
+                                    d[e + 1] = fmaf(tj[jj], bv.y, d[e + 1]);
+                                    d[e + 2] = fmaf(tj[jj], bv.z, d[e + 2]);
+                                    d[e + 3] = fmaf(tj[jj], bv.w, d[e + 3]);
+                                }
+                            } else {
+#pragma unroll
+                                for (int e = 0; e < 16; ++e) {
+                                    const int n = nb + e < N ? nb + e : N - 1;
+                                    d[e] = fmaf(tj[jj], __ldg(lora_b + static_cast<size_t>(j) * N + n), d[e]);
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) v[e] = fmaf(lora_scale, d[e], v[e]);
+                }
+                if (row_ok) {
+                    if (vec_ok && nb + 16 <= N) {
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4)
+                            *reinterpret_cast<float4*>(yrow + nb + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            if (nb + e < N) yrow[nb + e] = v[e];
+                    }
+                }
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(leader_addr(acc_empty(b)));
+        }
+    }
+
+    tc_fence_before_sync();
+    cluster_sync_all();  // no CTA leaves while its peer may still use its smem or TMEM
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    }
+}
+
+template <typename T16>
+int launch_pair_t(const GemmArgs& a, int pairs, cudaStream_t stream) {
+    auto kern = q4_gemm_pair_kernel<T16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::kSmemAlloc);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = PCfg::kSmemAlloc;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.scales, a.col_exp, a.row_exp, a.y, a.M, a.N, a.K,
+                           a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
+    return static_cast<int>(e);
+}
+
+template <typename T16>
+int max_pairs_t() {
+    auto kern = q4_gemm_pair_kernel<T16>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::kSmemAlloc) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = PCfg::kSmemAlloc;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) return 0;
+    return n;
+}
+
+}  // namespace
+
+int gemm_pair_tiles(int M, int N) {
+    return ((M + kPairRows - 1) / kPairRows) * ((N + kPairCols - 1) / kPairCols);
+}
+
+int gemm_pair_max_active(Operand16 op) { return op == Operand16::kF16 ? max_pairs_t<__half>() : max_pairs_t<__nv_bfloat16>(); }
+
+int launch_gemm_pair(const GemmArgs& a, int max_pairs, cudaStream_t stream) {
+    const int tiles = gemm_pair_tiles(a.M, a.N);
+    const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    if (pairs < 1) return static_cast<int>(cudaErrorInvalidValue);
+    return a.op == Operand16::kF16 ? launch_pair_t<__half>(a, pairs, stream)
+                                   : launch_pair_t<__nv_bfloat16>(a, pairs, stream);
+}
+
+}  // namespace q4

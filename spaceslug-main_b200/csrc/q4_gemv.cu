@@ -73,41 +73,6 @@ __device__ __forceinline__ int xs_offset(int g, int unit) {
     return g * (32 * M) + ((unit ^ (g & 7)) << 2);
 }
 
-// Butterfly reduce-scatter of V values across the 32 lanes of a warp.  On
-// return v[0] of lane l holds the warp-wide sum of value index
-// idx(l) = (bit-reversal-free) ((l >> (5 - log2 V)) ... see value_index().
-template <int V>
-__device__ __forceinline__ float warp_reduce_scatter(float (&v)[V], int lane) {
-    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
-#pragma unroll
-    for (int half = V / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
-        const bool upper = (lane & bit) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-            const float send = upper ? v[i] : v[i + half];
-            const float keep = upper ? v[i + half] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
-        }
-    }
-    float r = v[0];
-    constexpr int used = (V == 1) ? 0 : (V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5);
-#pragma unroll
-    for (int bit = 16 >> used; bit >= 1; bit >>= 1) r += __shfl_xor_sync(0xffffffffu, r, bit);
-    return r;
-}
-
-// Which of the V values lane `lane` holds after warp_reduce_scatter<V>: the
-// first step keeps the upper half when lane bit 16 is set, and so on, so the
-// index bits come from lane bits 16, 8, 4, ... (most significant first).
-template <int V>
-__device__ __forceinline__ int value_index(int lane) {
-    int idx = 0;
-#pragma unroll
-    for (int half = V / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1)
-        if (lane & bit) idx += half;
-    return idx;
-}
-
 template <int M>
 struct GemvCfg {
     static constexpr int MR = M < 4 ? M : 4;           // rows per register pass

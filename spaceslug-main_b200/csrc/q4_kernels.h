@@ -53,6 +53,10 @@ struct GemmArgs {
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
 int gemm_tiles(int M, int N, int halves);
+// CTA-pair (cta_group::2) variant, 256 x 256 tiles; X tensor map box 64 x 128.
+int launch_gemm_pair(const GemmArgs& a, int max_pairs, cudaStream_t stream);
+int gemm_pair_tiles(int M, int N);
+int gemm_pair_max_active(Operand16 op);
 
 // fp32 -> 16-bit cast of X with per-row power-of-two exponents (row_exp may be
 // nullptr: plain round-to-nearest cast).
@@ -63,8 +67,12 @@ int launch_col_exp(const float* scales, int* col_exp, int N, int K, cudaStream_t
 int launch_dequant(const uint32_t* packed, const float* scales, float* w_kn, int K, int N, cudaStream_t stream);
 // Device packer: logical int8 b[k*N + n] in [-8,7] -> reference layout.
 int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t stream);
-// T[M][rank] = X[M][K] * A[K][rank] in fp32.
-int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream);
+// T[M][rank] = X[M][K] * A[K][rank] in fp32.  With `partial` (scratch of
+// lora_xa_chunks(K) * M * rank floats) K is split over CTAs and reduced in a
+// second kernel in fixed order; with nullptr one pass per (8 rows, 16 ranks).
+int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
+                   float* partial = nullptr);
+int lora_xa_chunks(int K);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream);

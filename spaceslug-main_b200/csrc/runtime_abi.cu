@@ -30,6 +30,7 @@ namespace {
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_operand{static_cast<int>(q4::Operand16::kF16)};
+std::atomic<int> g_gemm_variant{0};  // 0 auto, 1 single-CTA 128-row tiles, 2 CTA pair, 3 single-CTA 256-row tiles
 std::once_flag g_operand_env_once;
 
 int fail(int code, const std::string& msg) {
@@ -58,6 +59,8 @@ struct DeviceCtx {
     int* status = nullptr;  // device int, kernels record wait timeouts here
     cudaStream_t stream = nullptr;  // for the synchronous host-pointer entry points
     std::mutex host_mu;             // serialises use of `stream` by host entry points
+    int max_pairs[2] = {-1, -1};    // co-resident CTA pairs of the pair GEMM, per operand type
+    std::mutex pair_mu;
 };
 
 constexpr int kMaxDevices = 64;
@@ -236,8 +239,13 @@ void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
 void run_problem(const Problem& p, cudaStream_t stream) {
     DeviceCtx& c = ctx_for(current_device());
     Scratch t_buf(p.rank > 0 ? static_cast<size_t>(p.M) * p.rank * sizeof(float) : 0, stream);
+    Scratch t_part(p.rank > 0 ? static_cast<size_t>(q4::lora_xa_chunks(p.K)) * p.M * p.rank * sizeof(float) : 0,
+                   stream);
     float* lora_t = static_cast<float*>(t_buf.p);
-    if (p.rank > 0) check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream), "lora_xa");
+    if (p.rank > 0)
+        check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
+                                        static_cast<float*>(t_part.p)),
+                     "lora_xa");
     const float lscale = p.rank > 0 ? p.alpha / static_cast<float>(p.rank) : 0.0f;
 
     GemvGeom geo;
@@ -268,9 +276,20 @@ void run_problem(const Problem& p, cudaStream_t stream) {
         check_launch(q4::launch_col_exp(p.scales, static_cast<int*>(cexp.p), p.N, p.K, stream), "col_exp");
 
     q4::GemmArgs g{};
-    // 256-row tiles halve the dequant work per FLOP; fall back to 128-row
-    // tiles when 256-row tiles would leave SMs idle.
-    g.halves = q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count ? 2 : 1;
+    // Variant: the CTA-pair kernel (256 x 256 tiles, half the operand bytes
+    // per FLOP) when it still fills every co-resident pair; else the
+    // single-CTA kernel with 256-row tiles when they fill every SM; else
+    // 128-row tiles.
+    int pairs = 0;
+    {
+        std::lock_guard<std::mutex> lk(c.pair_mu);
+        int& mp = c.max_pairs[static_cast<int>(op)];
+        if (mp < 0) mp = q4::gemm_pair_max_active(op);
+        pairs = mp;
+    }
+    const int variant = g_gemm_variant.load();
+    const bool use_pair = pairs > 0 && (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
+    g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
     g.sm_count = c.sm_count;
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
               static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) * 2, 64,
@@ -281,7 +300,10 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
     g.lora_t = lora_t; g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
     g.status = c.status;
-    check_launch(q4::launch_gemm(g, stream), "gemm launch");
+    if (use_pair)
+        check_launch(q4::launch_gemm_pair(g, pairs, stream), "gemm (CTA pair) launch");
+    else
+        check_launch(q4::launch_gemm(g, stream), "gemm launch");
 }
 
 // Reads and clears the status word (synchronises `stream` first).
@@ -637,6 +659,11 @@ int spaceslug_q4_set_operand_type(int type) {
     if (type != 0 && type != 1) return -1;
     operand_type();  // apply the environment default first
     return g_operand.exchange(type);
+}
+
+int spaceslug_q4_set_gemm_variant(int variant) {
+    if (variant < 0 || variant > 3) return -1;
+    return g_gemm_variant.exchange(variant);
 }
 
 int spaceslug_q4_device_status(int device) {

@@ -127,3 +127,49 @@ def test_gemm_deterministic_and_status_clean(session, cuda):
     y2 = session.q4gemm(inp.x, inp.packed, inp.scales, 256)
     assert np.array_equal(y1, y2)
     assert session.device_status(0) == 0
+
+
+@pytest.fixture(params=["single", "single256", "pair"])
+def variant(request, session):
+    prev = session.set_gemm_variant(request.param)
+    yield request.param
+    session.set_gemm_variant(prev)
+
+
+@pytest.mark.parametrize("m,n,k", [(9, 8, 32), (300, 1000, 1056), (256, 256, 64), (513, 700, 4096)])
+def test_gemm_variants_ragged(session, oracle, cuda, variant, m, n, k):
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=m * 3 + n + k)
+    x = synth.make_x(m, k, seed=m + 11)
+    y = session.q4gemm(x, packed, scales, n)
+    ref = oracle.gemm(x, w_kn, scales)
+    _check(y, ref, x, scales, k)
+
+
+def test_gemm_variants_agree_and_lora(session, oracle, cuda):
+    inp = synth.make_inputs("lora", m=640)
+    outs = {}
+    for v in ("single", "single256", "pair"):
+        prev = session.set_gemm_variant(v)
+        try:
+            outs[v] = session.q4gemm(inp.x, inp.packed, inp.scales, 4096, inp.lora_a, inp.lora_b, inp.alpha)
+        finally:
+            session.set_gemm_variant(prev)
+    # identical operands; only the tensor core's fp32 summation order may differ
+    for v in ("single256", "pair"):
+        assert np.max(np.abs(outs[v] - outs["single"])) <= 1e-5 * np.max(np.abs(outs["single"])), v
+    sel = np.r_[0:8, 600:640]
+    ref = oracle.gemm(inp.x[sel], inp.w_kn, inp.scales)
+    oracle.lora_add(ref, inp.x[sel], inp.lora_a, inp.lora_b, inp.alpha)
+    _check(outs["pair"][sel], ref, inp.x, inp.scales, 4096)
+
+
+def test_gemm_pair_kernel_on_large_ragged_problem(session, oracle, cuda):
+    # large enough that the automatic choice is the CTA-pair kernel
+    m, n, k = 1100, 4500, 1056
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=5)
+    x = synth.make_x(m, k, seed=6)
+    y = session.q4gemm(x, packed, scales, n)
+    sel = np.r_[0:4, 255:261, 1096:1100]
+    ref = oracle.gemm(x[sel], w_kn, scales)
+    _check(y[sel], ref, x, scales, k)
+    assert np.all(np.isfinite(y))
