@@ -40,5 +40,8 @@ def allgather_columns(y_shard, n_total: int, pg, stream=None):
     world = pg.get_world_size()
     m, w = y_shard.shape
     buf = torch.empty((world, m, w), dtype=y_shard.dtype, device=y_shard.device)
-    pg.all_gather_into_tensor(buf, y_shard.contiguous())
+    if y_shard.is_cuda:
+        pg.all_gather_into_tensor(buf, y_shard.contiguous())
+    else:  # gloo (CPU): list form
+        pg.all_gather(list(buf.unbind(0)), y_shard.contiguous())
     return buf.permute(1, 0, 2).reshape(m, world * w)[:, :n_total]

@@ -1,0 +1,70 @@
+"""Worker for tests/test_multigpu_gpu.py (one process per GPU under
+torch.distributed.run): N-sharded int4 GEMM (+ LoRA) through the library on
+each rank, NCCL all-gather of the fp32 Y shards, rank 0 checks the gathered
+Y against the oracle and against an unsharded run on its own GPU."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+
+def main() -> int:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from conftest import load_package
+    load_package()
+    from oracle.oracle import Oracle
+    from spaceslug_b200 import backend, parity, sharding, synth
+
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    s = backend.BackendSession()
+    ok = True
+    for (m, k, n, r) in [(300, 1024, 2048, 8), (4, 4096, 4096, 0), (600, 2048, 1600, 0)]:
+        w_kn, packed, scales = synth.make_weights(k, n, 0.003, 0.01, seed=k + n)
+        x = synth.make_x(m, k, seed=m)
+        a = synth.normal(k * r, 3, 0.02).reshape(k, r) if r else None
+        b = synth.normal(r * n, 4, 0.02).reshape(r, n) if r else None
+        c0, c1 = sharding.shard_columns(n, world, rank)
+        width = sharding.shard_width(n, world)
+        with s.weights(packed, scales, k, n, c0, c1, device=local) as h:
+            if r:
+                h.set_lora(a, b, 16.0)
+            xd = torch.from_numpy(x).to(dev)
+            ys = torch.zeros((m, width), dtype=torch.float32, device=dev)
+            yv = torch.empty((m, c1 - c0), dtype=torch.float32, device=dev)
+            h.run(xd.data_ptr(), yv.data_ptr(), m, torch.cuda.current_stream().cuda_stream)
+            ys[:, : c1 - c0] = yv
+        y = sharding.allgather_columns(ys, n, dist).cpu().numpy()
+        if rank == 0:
+            full = s.q4gemm(x, packed, scales, n, a, b, 16.0) if r else s.q4gemm(x, packed, scales, n)
+            same = np.max(np.abs(full - y)) <= 1e-5 * max(1.0, float(np.max(np.abs(full))))
+            sel = np.r_[0:2, m - 2:m]
+            ref = Oracle().gemm(x[sel], w_kn, scales)
+            if r:
+                Oracle().lora_add(ref, x[sel], a, b, 16.0)
+            if m <= 8:
+                rep = parity.compare_float_arrays(y[sel], ref, tolerance=parity.GEMV_REL_TOL)
+                good = rep["status"] == "pass"
+            else:
+                rep = parity.gemm_error_report(y[sel], ref, x, 8 * float(np.abs(scales).max()), k)
+                good = rep["max_abs"] <= rep["abs_bound"] and rep["norm_rel"] <= parity.GEMM_NORM_REL_TOL
+            print(f"shape {(m, k, n, r)} world {world}: gathered==unsharded {same}, oracle {rep}", flush=True)
+            ok &= bool(same and good)
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.broadcast(flag, 0)
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
