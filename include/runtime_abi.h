@@ -143,6 +143,13 @@ int spaceslug_q4_set_operand_type(int type);
  * invalid value. */
 int spaceslug_q4_set_gemm_variant(int variant);
 
+/* Decode (M <= 8) kernel selection: 0 = automatic (default), 1 = CUDA-core
+ * GEMV with a streamed shared-memory ring, 2 = tensor-core decode, 3 = CUDA-core
+ * GEMV with the whole tile resident.  A variant the shape does not allow falls
+ * back to the automatic choice.  Results agree to fp32 summation order.
+ * Returns the previous value, or -1 for an invalid value. */
+int spaceslug_q4_set_decode_variant(int variant);
+
 /* Reads and clears the kernel status word of `device` (0 = no kernel wait
  * has timed out since the last call).  Synchronises the device. */
 int spaceslug_q4_device_status(int device);

@@ -50,6 +50,7 @@ _SIGNATURES = {
     "spaceslug_q4_weights_destroy": ([_vp], ctypes.c_int),
     "spaceslug_q4_set_operand_type": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
+    "spaceslug_q4_set_decode_variant": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
     "spaceslug_last_error": ([], ctypes.c_char_p),
@@ -195,6 +196,11 @@ class BackendSession:
     def set_gemm_variant(self, variant: str) -> str:
         names = {"auto": 0, "single": 1, "pair": 2, "single256": 3}
         prev = self.raw("spaceslug_q4_set_gemm_variant")(names[variant])
+        return {v: k for k, v in names.items()}.get(prev, "?")
+
+    def set_decode_variant(self, variant: str) -> str:
+        names = {"auto": 0, "gemv": 1, "mma": 2, "tile": 3}
+        prev = self.raw("spaceslug_q4_set_decode_variant")(names[variant])
         return {v: k for k, v in names.items()}.get(prev, "?")
 
     def device_status(self, device: int = 0) -> int:

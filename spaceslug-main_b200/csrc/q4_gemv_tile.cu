@@ -1,0 +1,410 @@
+// Decode GEMV, whole tile resident (M <= 8):  Y[M x N] = X . dequant(W) (+ LoRA), fp32.
+//
+// Same math and weight layout as the reference kernel (q4gemm.comp:7-19,
+// 104-122): nibble v of column n at byte n*(K/2) + k/2 (low nibble = even k),
+// w = float(v) * scales[n*(K/32) + k/32], y = sum_k x * w, all fp32.  The
+// reference itself has no decode path (q4gemm.comp:36-37 needs M % 64 == 0).
+//
+// Designed for the latency of one small layer (4096 x 4096 int4 is 10.5 MB,
+// ~1.6 us of HBM time): nothing waits on anything but the arrival of data.
+//   * A CTA owns 32 columns and a K slice (the whole of K, or 1/S of it with a
+//     cluster of S CTAs).  At entry one thread issues every TMA load of the
+//     CTA's tile into its own shared memory: the packed weights as 128-byte
+//     swizzled boxes of 32 columns x 256 k (one mbarrier per box), the scales
+//     as swizzled boxes of 32 columns x 32 groups.  These do not depend on the
+//     previous launch, so they go out before griddepcontrol.wait, and the CTA
+//     signals its dependents at once: the next layer's CTAs can stream their
+//     weights while this layer computes.  X (after the wait) is one TMA box
+//     per row.
+//   * 8 warps take the weight boxes round robin.  Lane (cq = lane/4, j =
+//     lane%4) handles columns cq, cq+8, cq+16, cq+24 and, in each 32-k scale
+//     group, the 8 k of word j: the weights are unpacked exactly (2^23 magic
+//     number), scaled in fp32 (the reference's single rounding) and multiplied
+//     into packed f32x2 accumulators; one x load serves four columns.  With the
+//     swizzle every shared-memory load is free of bank conflicts.
+//   * lanes j are summed with two shuffles, warps through shared memory, the
+//     cluster's K slices through distributed shared memory, all in a fixed
+//     order (deterministic).  The LoRA term (alpha/r) * T[m,:] . B[:,n] with
+//     T = X*A is added and Y stored.
+// No TMEM, no producer/consumer ring: the only waits are for TMA arrivals,
+// each bounded (status word + abort flag).
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.cuh"
+#include "q4_kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace q4 {
+
+namespace {
+
+constexpr int kTSlot = 32;       // rows (columns of W) per shared-memory box slot
+constexpr int kTBoxK = 256;      // k per weight box: one 128-byte row (32 words) per column
+constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row per column
+
+// Warps per CTA: 16 for M <= 2 (latency hiding at <= 64 registers, so two
+// CTAs share an SM), 8 above.
+template <int M>
+struct TileCfg {
+    static constexpr int kWarps = M <= 2 ? 16 : 8;
+    static constexpr int kThreads = kWarps * 32;
+};
+
+__host__ __device__ inline int tile_warps(int M) { return M <= 2 ? 16 : 8; }
+
+struct TileLayout {
+    int kslice, nbox, nsbox;
+    int w_off, s_off, x_off, part_off, cpart_off, bar_off, misc_off, bytes;
+};
+
+__host__ __device__ inline TileLayout tile_layout(int M, int K, int S) {
+    TileLayout L;
+    L.kslice = K / S;
+    L.nbox = L.kslice / kTBoxK;
+    L.nsbox = (L.kslice / 32 + kTScaleBoxG - 1) / kTScaleBoxG;
+    L.w_off = 0;                                       // nbox x [32 rows][128 B], swizzled
+    L.s_off = L.w_off + L.nbox * kTSlot * 128;        // nsbox x [32 rows][128 B], swizzled
+    L.x_off = L.s_off + L.nsbox * kTSlot * 128;       // [M][kslice] fp32
+    L.part_off = L.x_off + M * L.kslice * 4;          // [warp][M][32] fp32
+    L.cpart_off = L.part_off + tile_warps(M) * kTSlot * M * 4;  // [M][32] fp32 (the CTA's K-slice sum)
+    L.bar_off = L.cpart_off + kTSlot * M * 4;
+    L.misc_off = L.bar_off + (L.nbox + 2) * 8;         // wfull[nbox], sfull, xfull
+    L.bytes = L.misc_off + 16;                         // abort flag
+    return L;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+
+// 2-D TMA load with an L2 evict-first policy (streamed-once weights).
+__device__ __forceinline__ void tma_load_2d_stream(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0,
+                                                   int32_t c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// The eight int4 values of one packed word (k = 0..7 at bits 4k) as four
+// f32x2 pairs (k, k+1), exactly: (u ^ 8) = v + 8 lies in [0, 15] and
+// float(0x4B000000 | (v + 8)) = 2^23 + v + 8, so subtracting 2^23 + 8 gives v.
+__device__ __forceinline__ void unpack_word_f32(uint32_t q, float2 (&v)[4]) {
+    const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;         // k = 0, 2, 4, 6
+    // q >> 4 as the high word of q * 2^28 (an integer multiply, off the
+    // logic pipe that the byte permutes below saturate)
+    const uint32_t hi = (__umulhi(q, 1u << 28) ^ 0x08080808u) & 0x0F0F0F0Fu;  // k = 1, 3, 5, 7
+    const float2 nbias = make_float2(-8388616.0f, -8388616.0f);                 // -(2^23 + 8)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        // byte_perm selector 0x744b: byte b -> byte 0, zeros -> bytes 1-2,
+        // 0x4B (the exponent byte of 2^23) -> byte 3.
+        const float2 mg = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))),
+                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))));
+        v[b] = __fadd2_rn(mg, nbias);
+    }
+}
+
+// The same eight weights times the group scale: float(v) * s rounded once, as
+// the reference's dequant.
+__device__ __forceinline__ void dequant_word_f32(uint32_t q, float s, float2 (&w)[4]) {
+    float2 v[4];
+    unpack_word_f32(q, v);
+    const float2 s2 = make_float2(s, s);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) w[b] = __fmul2_rn(v[b], s2);
+}
+
+template <int M>
+__global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
+    q4_gemv_tile_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
+                        const __grid_constant__ CUtensorMap tmap_x, float* __restrict__ y, int N, int K, int G,
+                        const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
+                        float lora_scale, int* __restrict__ status) {
+    constexpr int kWarps = TileCfg<M>::kWarps;
+    constexpr int kThreads = TileCfg<M>::kThreads;
+    extern __shared__ uint8_t smem_raw[];
+    // 128-byte swizzled TMA destinations need 1024-byte alignment.
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t base = smem_u32(smem);
+    const int S = static_cast<int>(cluster_nctarank());
+    const int crank = static_cast<int>(cluster_ctarank());
+    const TileLayout L = tile_layout(M, K, S);
+    // Column block blk of G: columns [blk*N/G, (blk+1)*N/G), at most 32.  The
+    // boxes load ceil(N/G) rows from n0; a row past the block belongs to the
+    // next block (or lies past N, zero-filled) and is never stored.
+    const int blk = static_cast<int>(blockIdx.x) / S;
+    const int n0 = static_cast<int>(static_cast<long long>(blk) * N / G);
+    const int C = static_cast<int>(static_cast<long long>(blk + 1) * N / G) - n0;
+    const int box_rows = (N + G - 1) / G;
+    const int k0 = crank * L.kslice;
+
+    const uint32_t bar = base + L.bar_off;
+    auto wfull = [&](int b) { return bar + 8u * b; };
+    const uint32_t sfull = bar + 8u * L.nbox;
+    const uint32_t xfull = bar + 8u * (L.nbox + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int b = 0; b < L.nbox + 2; ++b) mbar_init(bar + 8u * b, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+
+    if (tid == 0) {
+        // Weights and scales do not depend on the previous launch.
+        tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_s);
+        tma_prefetch_desc(&tmap_x);
+        const uint64_t pol = policy_evict_first();
+        // boxes are C rows; each lands in a 32-row (4 KB) slot
+        mbar_arrive_expect_tx(sfull, static_cast<uint32_t>(L.nsbox * box_rows * 128));
+        for (int sb = 0; sb < L.nsbox; ++sb)
+            tma_load_2d_stream(base + L.s_off + sb * kTSlot * 128, &tmap_s, sfull, k0 / 32 + sb * kTScaleBoxG, n0,
+                               pol);
+        for (int b = 0; b < L.nbox; ++b) {
+            mbar_arrive_expect_tx(wfull(b), static_cast<uint32_t>(box_rows * 128));
+            tma_load_2d_stream(base + L.w_off + b * kTSlot * 128, &tmap_w, wfull(b), (k0 + b * kTBoxK) / 8, n0, pol);
+        }
+    }
+    // Dependents may launch now: their weight loads overlap this launch.
+    pdl_launch_dependents();
+    pdl_wait();  // X, T and Y may be touched by the previous launch
+    if (tid == 0) {
+        mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(M * L.kslice * 4));
+        const int rows_per_m = K / kTBoxK;
+        for (int m = 0; m < M; ++m)
+            tma_load_2d(base + L.x_off + m * L.kslice * 4, &tmap_x, xfull, 0, m * rows_per_m + k0 / kTBoxK);
+    }
+
+    // ------------------------------------------------------------ compute --
+    // Lane (cq, j) handles slot rows cq + 8r (r < 4) and word j of each group;
+    // rows >= C (C < 32) hold no column and their sums are never read.  All
+    // four rows of a lane share row & 7 = cq, so in the 128-byte swizzle the
+    // 16-byte chunk of group t is t ^ cq for every r: one LOP3 per group
+    // addresses the four words (and another the four scales), and the eight
+    // lanes cq of a quarter warp hit distinct bank quads.
+    const int cq = lane >> 2, j = lane & 3;
+    const uint32_t cq16 = static_cast<uint32_t>(cq) << 4;
+    float2 acc[4][M];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
+
+    bool ok = mbar_wait(sfull, 0u, abort_flag, status, kStatusTimeoutGemv) &&
+              mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
+    const uint32_t xs = base + L.x_off + j * 32;  // this lane's 8 x of word j in a group
+#pragma unroll 1
+    for (int b = warp; b < L.nbox && ok; b += kWarps) {
+        if (!mbar_wait(wfull(b), 0u, abort_flag, status, kStatusTimeoutGemv)) {
+            ok = false;
+            break;
+        }
+        // bits 4-6 of both bases are zero, so "| chunk << 4" places the chunk
+        const uint32_t wrow = base + L.w_off + b * kTSlot * 128 + cq * 128 + j * 4;
+        const uint32_t srow = base + L.s_off + (b >> 2) * kTSlot * 128 + cq * 128;
+        const uint32_t sx = (static_cast<uint32_t>((b & 3) * 2) << 4) ^ cq16;  // scale chunk of group 0, swizzled
+        const uint32_t xrow = xs + b * kTBoxK * 4;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint32_t wa = wrow | ((static_cast<uint32_t>(t) << 4) ^ cq16);
+            const uint32_t sa = (srow | (sx ^ (static_cast<uint32_t>(t >> 2) << 4))) + (t & 3) * 4;
+            float2 xv[M][4];
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
+                const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
+                xv[m][0] = make_float2(xa.x, xa.y);
+                xv[m][1] = make_float2(xa.z, xa.w);
+                xv[m][2] = make_float2(xc.x, xc.y);
+                xv[m][3] = make_float2(xc.z, xc.w);
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t q = lds_u32(wa + r * 8 * 128);
+                const float s = __uint_as_float(lds_u32(sa + r * 8 * 128));
+                if constexpr (M <= 2) {
+                    // per-word partial sum of v * x, scaled once (fewer fp32 ops)
+                    float2 v[4];
+                    unpack_word_f32(q, v);
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        float2 p = __fmul2_rn(v[0], xv[m][0]);
+                        p = __ffma2_rn(v[1], xv[m][1], p);
+                        p = __ffma2_rn(v[2], xv[m][2], p);
+                        p = __ffma2_rn(v[3], xv[m][3], p);
+                        acc[r][m].x = fmaf(s, p.x + p.y, acc[r][m].x);
+                    }
+                } else {
+                    float2 w[4];
+                    dequant_word_f32(q, s, w);
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        acc[r][m] = __ffma2_rn(w[0], xv[m][0], acc[r][m]);
+                        acc[r][m] = __ffma2_rn(w[1], xv[m][1], acc[r][m]);
+                        acc[r][m] = __ffma2_rn(w[2], xv[m][2], acc[r][m]);
+                        acc[r][m] = __ffma2_rn(w[3], xv[m][3], acc[r][m]);
+                    }
+                }
+            }
+        }
+    }
+
+    // ------------------------------------------------------------- reduce --
+    float* part = reinterpret_cast<float*>(smem + L.part_off);  // [warp][M][col]
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float v = acc[r][m].x + acc[r][m].y;
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            if (j == 0) part[(warp * M + m) * kTSlot + cq + 8 * r] = v;
+        }
+    }
+    __syncthreads();
+
+    float* cpart = reinterpret_cast<float*>(smem + L.cpart_off);  // [M][32]
+    for (int idx = tid; idx < kTSlot * M; idx += kThreads) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int w8 = 0; w8 < kWarps; ++w8) sum += part[w8 * kTSlot * M + idx];
+        cpart[idx] = sum;
+    }
+    if (S > 1) {
+        cluster_sync_all();
+    } else {
+        __syncthreads();
+    }
+    cg::cluster_group cluster = cg::this_cluster();
+    for (int idx = crank + S * tid; idx < kTSlot * M; idx += kThreads * S) {
+        const int m = idx / kTSlot, c = idx % kTSlot;
+        const int n = n0 + c;
+        float sum = 0.0f;
+        if (S > 1) {
+            for (int q = 0; q < S; ++q) sum += cluster.map_shared_rank(cpart, q)[idx];
+        } else {
+            sum = cpart[idx];
+        }
+        if (c < C && n < N) {
+            if (lora_b != nullptr) {
+                float d = 0.0f;
+                for (int jr = 0; jr < rank; ++jr) d = fmaf(lora_t[m * rank + jr], lora_b[static_cast<size_t>(jr) * N + n], d);
+                sum = fmaf(lora_scale, d, sum);
+            }
+            y[static_cast<size_t>(m) * N + n] = sum;
+        }
+    }
+    if (S > 1) cluster_sync_all();  // peers may still read this CTA's partials
+
+    if (tid == 0 && *abort_flag) {
+        // copies already issued land before the CTA's shared memory is released
+        for (int b = 0; b < L.nbox; ++b) mbar_drain(wfull(b), 0u);
+        mbar_drain(sfull, 0u);
+        mbar_drain(xfull, 0u);
+    }
+}
+
+template <int M>
+int launch_tile_m(const GemvTileArgs& a, cudaStream_t stream) {
+    const TileLayout L = tile_layout(M, a.K, a.cluster_k);
+    const size_t smem = static_cast<size_t>(L.bytes) + 1024;
+    auto kern = q4_gemv_tile_kernel<M>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.col_blocks * a.cluster_k));
+    cfg.blockDim = dim3(TileCfg<M>::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (a.cluster_k > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = static_cast<unsigned>(a.cluster_k);
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    e = cudaLaunchKernelEx(&cfg, kern, a.tmap_w, a.tmap_s, a.tmap_x, a.y, a.N, a.K, a.col_blocks, a.lora_t, a.lora_b,
+                           a.rank, a.lora_scale, a.status);
+    return static_cast<int>(e);
+}
+
+}  // namespace
+
+size_t gemv_tile_smem_bytes(int M, int K, int S) {
+    return static_cast<size_t>(tile_layout(M, K, S).bytes) + 1024;
+}
+
+bool gemv_tile_supported(int M, int K, int S) {
+    if (M < 1 || M > 8 || S < 1 || S > 8 || (S & (S - 1)) != 0) return false;
+    if (K <= 0 || K % (kTBoxK * S) != 0) return false;
+    return gemv_tile_smem_bytes(M, K, S) <= 227 * 1024;
+}
+
+// Column blocks: one per SM while that keeps blocks at <= 32 columns, so a
+// launch holds exactly one CTA per SM and the next launch (programmatic
+// dependent launch) finds exactly one free slot on every SM; wider matrices
+// take 32-column blocks in several waves.  N = 4096 on 148 SMs: 148 blocks of
+// 27 or 28 columns.
+int gemv_tile_col_blocks(int N, int sm_count) {
+    if (N <= 32 * sm_count) return N < sm_count ? N : sm_count;
+    return (N + 31) / 32;
+}
+
+int gemv_tile_box_rows(int N, int col_blocks) { return (N + col_blocks - 1) / col_blocks; }
+
+int gemv_tile_box_k() { return kTBoxK; }
+int gemv_tile_scale_box_groups() { return kTScaleBoxG; }
+
+int launch_gemv_tile(const GemvTileArgs& a, cudaStream_t stream) {
+    if (!gemv_tile_supported(a.M, a.K, a.cluster_k) || a.col_blocks < 1 || a.col_blocks > a.N ||
+        gemv_tile_box_rows(a.N, a.col_blocks) > kTSlot)
+        return static_cast<int>(cudaErrorInvalidValue);
+    switch (a.M) {
+        case 1: return launch_tile_m<1>(a, stream);
+        case 2: return launch_tile_m<2>(a, stream);
+        case 3: return launch_tile_m<3>(a, stream);
+        case 4: return launch_tile_m<4>(a, stream);
+        case 5: return launch_tile_m<5>(a, stream);
+        case 6: return launch_tile_m<6>(a, stream);
+        case 7: return launch_tile_m<7>(a, stream);
+        default: return launch_tile_m<8>(a, stream);
+    }
+}
+
+}  // namespace q4

@@ -29,6 +29,37 @@ struct GemvArgs {
     int* status;             // kernel status word (0 = ok)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t stream);
+// Tensor-core decode (M <= 8): clusters of `cluster_k` CTAs over K, 128
+// columns per cluster; a.tmap_w box = 8 words x 128 columns.
+bool decode_supported(int M, int K, int S);
+size_t decode_smem_bytes(int K, int S);
+int decode_columns_per_cluster();
+int launch_decode(const GemvArgs& a, cudaStream_t stream);
+// Whole-tile GEMV (M <= 8): col_blocks blocks of <= 32 columns x K/S per CTA,
+// every load issued at entry.  Needs K % (256 * S) == 0 and 16-byte aligned x,
+// packed and scales.
+struct GemvTileArgs {
+    CUtensorMap tmap_w;      // packed uint32 [N][K/8], box 32 words x box_rows, 128B swizzle
+    CUtensorMap tmap_s;      // scales fp32 [N][K/32], box 32 x box_rows, 128B swizzle
+    CUtensorMap tmap_x;      // X fp32 viewed as [M*K/256][256], box 256 x (K/S/256)
+    float* y;                // [M][N]
+    int M, N, K;
+    int cluster_k;           // S: CTAs per cluster splitting K
+    int col_blocks;          // G: block g holds columns [g*N/G, (g+1)*N/G)
+    const float* lora_t;     // [M][rank] or nullptr
+    const float* lora_b;     // [rank][N] or nullptr
+    int rank;
+    float lora_scale;
+    int* status;
+};
+bool gemv_tile_supported(int M, int K, int S);
+size_t gemv_tile_smem_bytes(int M, int K, int S);
+// Column blocks for N on sm_count SMs, and the rows of its boxes (<= 32).
+int gemv_tile_col_blocks(int N, int sm_count);
+int gemv_tile_box_rows(int N, int col_blocks);
+int gemv_tile_box_k();
+int gemv_tile_scale_box_groups();
+int launch_gemv_tile(const GemvTileArgs& a, cudaStream_t stream);
 size_t gemv_smem_bytes(int M, int K, int cluster_k, int cols_per_cluster);
 int gemv_chunk_columns();
 // Max co-resident clusters of the GEMV for these parameters (0 on error).

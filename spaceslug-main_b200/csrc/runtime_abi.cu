@@ -30,6 +30,7 @@ namespace {
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_operand{static_cast<int>(q4::Operand16::kF16)};
+std::atomic<int> g_decode_variant{0};  // 0 auto, 1 ring GEMV, 2 tensor-core decode, 3 whole-tile GEMV
 std::atomic<int> g_gemm_variant{0};  // 0 auto, 1 single-CTA 128-row tiles, 2 CTA pair, 3 single-CTA 256-row tiles
 std::once_flag g_operand_env_once;
 
@@ -116,6 +117,15 @@ int current_device() {
     int d = 0;
     check(cudaGetDevice(&d), "cudaGetDevice");
     return d;
+}
+
+int decode_split_override() {
+    static const int v = [] {
+        const char* e = std::getenv("SPACESLUG_Q4_DECODE_SPLIT");
+        const int s = e ? std::atoi(e) : 0;
+        return (s == 1 || s == 2 || s == 4 || s == 8) ? s : 0;
+    }();
+    return v;
 }
 
 q4::Operand16 operand_type() {
@@ -224,6 +234,20 @@ bool choose_gemv(const DeviceCtx& c, int M, int N, int K, GemvGeom& out) {
     return true;
 }
 
+// K split (cluster size) of the whole-tile GEMV: the smallest that fits in
+// shared memory; SPACESLUG_Q4_TILE_SPLIT overrides (1, 2, 4 or 8).
+int tile_split(int M, int K) {
+    static const int forced = [] {
+        const char* e = std::getenv("SPACESLUG_Q4_TILE_SPLIT");
+        const int s = e ? std::atoi(e) : 0;
+        return (s == 1 || s == 2 || s == 4 || s == 8) ? s : 0;
+    }();
+    if (forced > 0) return q4::gemv_tile_supported(M, K, forced) ? forced : 0;
+    for (int S = 1; S <= 8; S *= 2)
+        if (q4::gemv_tile_supported(M, K, S)) return S;
+    return 0;
+}
+
 void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
     cuuint64_t dims[2] = {inner, outer};
@@ -248,6 +272,63 @@ void run_problem(const Problem& p, cudaStream_t stream) {
                      "lora_xa");
     const float lscale = p.rank > 0 ? p.alpha / static_cast<float>(p.rank) : 0.0f;
 
+    // Decode (M <= 8).  Automatic choice: the whole-tile GEMV where the shape
+    // allows it, else the streamed-ring GEMV; the tensor-core decode only on
+    // request.
+    const int dv = g_decode_variant.load();
+    if (p.M <= 8 && (dv == 0 || dv == 3)) {
+        const int S = tile_split(p.M, p.K);
+        if (S > 0 && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
+            q4::GemvTileArgs a{};
+            const int K = p.K, N = p.N;
+            a.col_blocks = q4::gemv_tile_col_blocks(N, c.sm_count);
+            const uint32_t rows = static_cast<uint32_t>(q4::gemv_tile_box_rows(N, a.col_blocks));
+            encode_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(K) / 8,
+                      static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, 32, rows, CU_TENSOR_MAP_SWIZZLE_128B);
+            encode_2d(&a.tmap_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.scales, static_cast<uint64_t>(K) / 32,
+                      static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 8,
+                      static_cast<uint32_t>(q4::gemv_tile_scale_box_groups()), rows, CU_TENSOR_MAP_SWIZZLE_128B);
+            const int bk = q4::gemv_tile_box_k();
+            encode_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.x, static_cast<uint64_t>(bk),
+                      static_cast<uint64_t>(p.M) * (K / bk), static_cast<uint64_t>(bk) * 4,
+                      static_cast<uint32_t>(bk), static_cast<uint32_t>(K / S / bk), CU_TENSOR_MAP_SWIZZLE_NONE);
+            a.y = p.y;
+            a.M = p.M; a.N = N; a.K = K;
+            a.cluster_k = S;
+            a.lora_t = lora_t; a.lora_b = p.rank > 0 ? p.lora_b : nullptr; a.rank = p.rank; a.lora_scale = lscale;
+            a.status = c.status;
+            check_launch(q4::launch_gemv_tile(a, stream), "gemv tile launch");
+            return;
+        }
+    }
+    if (p.M <= 8 && dv == 2) {
+        // K split of the tensor-core decode: the first of 8, 4, 2, 1 that fits;
+        // SPACESLUG_Q4_DECODE_SPLIT overrides (1, 2, 4 or 8).
+        int S = 0;
+        const int order[4] = {8, 4, 2, 1};
+        const int forced = decode_split_override();
+        for (int cand : order) {
+            const int c2 = forced > 0 ? forced : cand;
+            if (q4::decode_supported(p.M, p.K, c2) && q4::decode_smem_bytes(p.K, c2) <= 200 * 1024) {
+                S = c2;
+                break;
+            }
+            if (forced > 0) break;
+        }
+        if (S > 0) {
+            q4::GemvArgs a{};
+            encode_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
+                      static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8,
+                      static_cast<uint32_t>(q4::decode_columns_per_cluster()), CU_TENSOR_MAP_SWIZZLE_NONE);
+            a.x = p.x; a.scales = p.scales; a.y = p.y;
+            a.M = p.M; a.N = p.N; a.K = p.K;
+            a.cluster_k = S;
+            a.lora_t = lora_t; a.lora_b = p.rank > 0 ? p.lora_b : nullptr; a.rank = p.rank; a.lora_scale = lscale;
+            a.status = c.status;
+            check_launch(q4::launch_decode(a, stream), "decode launch");
+            return;
+        }
+    }
     GemvGeom geo;
     if (p.M <= 8 && choose_gemv(c, p.M, p.N, p.K, geo)) {
         q4::GemvArgs a{};
@@ -659,6 +740,11 @@ int spaceslug_q4_set_operand_type(int type) {
     if (type != 0 && type != 1) return -1;
     operand_type();  // apply the environment default first
     return g_operand.exchange(type);
+}
+
+int spaceslug_q4_set_decode_variant(int variant) {
+    if (variant < 0 || variant > 3) return -1;
+    return g_decode_variant.exchange(variant);
 }
 
 int spaceslug_q4_set_gemm_variant(int variant) {

@@ -16,6 +16,13 @@ pytestmark = pytest.mark.gpu
 TOL = parity.GEMV_REL_TOL
 
 
+@pytest.fixture(params=["tile", "mma", "gemv"])
+def decode_variant(request, session):
+    prev = session.set_decode_variant(request.param)
+    yield request.param
+    session.set_decode_variant(prev)
+
+
 @pytest.fixture(scope="module")
 def decode_weights():
     cfg = synth.CONFIGS["decode"]
@@ -23,7 +30,7 @@ def decode_weights():
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 6, 7, 8])
-def test_gemv_config2_full(session, oracle, cuda, decode_weights, m):
+def test_gemv_config2_full(session, oracle, cuda, decode_weights, decode_variant, m):
     w_kn, packed, scales = decode_weights
     x = synth.make_x(m, 4096, seed=m)
     y = session.q4gemm(x, packed, scales, 4096)
@@ -34,7 +41,7 @@ def test_gemv_config2_full(session, oracle, cuda, decode_weights, m):
 
 @pytest.mark.parametrize("m,n,k", [(1, 1, 32), (2, 5, 64), (3, 200, 96), (8, 1000, 64), (5, 37, 4096),
                                    (1, 4096, 8192), (4, 300, 1024), (8, 64, 2048), (6, 129, 160)])
-def test_gemv_ragged_shapes(session, oracle, cuda, m, n, k):
+def test_gemv_ragged_shapes(session, oracle, cuda, decode_variant, m, n, k):
     w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=n + k)
     x = synth.make_x(m, k, seed=m * 7 + 1)
     y = session.q4gemm(x, packed, scales, n)
@@ -44,7 +51,7 @@ def test_gemv_ragged_shapes(session, oracle, cuda, m, n, k):
 
 
 @pytest.mark.parametrize("m", [1, 4, 8])
-def test_gemv_fused_lora(session, oracle, cuda, m):
+def test_gemv_fused_lora(session, oracle, cuda, decode_variant, m):
     k, n, r, alpha = 1024, 768, 16, 32.0
     w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=5)
     x = synth.make_x(m, k, seed=9)
@@ -73,7 +80,7 @@ def test_gemv_device_api_matches_host_api(session, cuda, decode_weights):
     assert session.device_status(0) == 0
 
 
-def test_gemv_is_deterministic(session, cuda, decode_weights):
+def test_gemv_is_deterministic(session, cuda, decode_weights, decode_variant):
     w_kn, packed, scales = decode_weights
     x = synth.make_x(8, 4096, seed=4)
     y1 = session.q4gemm(x, packed, scales, 4096)
