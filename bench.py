@@ -119,56 +119,59 @@ class Dist:
 
 # ------------------------------------------------------------------ clocks --
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms."""
+    """SM clock and clock-event (throttle) reasons, read through NVML every
+    ~0.5 ms by a thread while the timed region runs.  Read-only queries."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, gpu_index: int) -> None:
-        self.proc = None
-        self.gpu = gpu_index
-        self.path = None
+    def __init__(self, torch, device_index: int) -> None:
+        self.handle = None
+        self.samples: list[tuple[int, int, int]] = []
+        self.stop_flag = False
+        self.thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: the line says so
+            self.error = f"{type(e).__name__}: {e}"
+
+    def _run(self) -> None:
+        nv, h = self.nvml, self.handle
+        while not self.stop_flag:
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h),
+                                     nv.nvmlDeviceGetPowerUsage(h)))
+            except Exception:
+                break
+            time.sleep(0.0005)
 
     def start(self) -> None:
-        exe = shutil.which("nvidia-smi")
-        if not exe:
+        if self.handle is None:
             return
-        import tempfile
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
-        self.fh = open(self.path, "w")
-        self.proc = subprocess.Popen([exe, f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits", "-lms", "200"],
-                                     stdout=self.fh, stderr=subprocess.DEVNULL)
+        import threading
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
 
     def stop(self) -> dict | None:
-        if not self.proc:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.fh.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in Path(self.path).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[4:8]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        os.unlink(self.path)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if self.handle is None:
+            return {"unavailable": getattr(self, "error", "no NVML")}
+        self.stop_flag = True
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if not self.samples:
+            return {"unavailable": "no samples"}
+        reasons = sorted({name for _, r, _ in self.samples for name, bit in self.REASONS if r & bit})
+        return {"sm_mhz": statistics.median(c for c, _, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_max": round(max(p for _, _, p in self.samples) / 1000.0, 1),
+                "source": "NVML, every ~0.5 ms during the timed region"}
 
 
 # --------------------------------------------------------- CPU baselines --
@@ -310,8 +313,7 @@ def decode_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     launches_per_step = session.launch_count() - n0
     for _ in range(args.warmup):
         time_graph_replays(torch, stream, graphs, 1)
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dist.local)).split(",")[0])
-                          if os.environ.get("CUDA_VISIBLE_DEVICES", "").isdigit() else dist.local)
+    clocks = ClockSampler(torch, dist.local)
     clocks.start()
     dist.barrier()
     torch.cuda.synchronize(dev)
@@ -364,7 +366,7 @@ def decode_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": avg_launch_bytes,
-                     "peak_source": peaks["source"], "kernel": "q4_gemv_kernel"},
+                     "peak_source": peaks["source"], "kernel": "q4_gemv_tile_kernel"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "spaceslug_q4_weights_run_host (pinned host X/Y, resident weights)"},
     }

@@ -3,29 +3,39 @@
 //
 // The reference has no decode path (q4gemm.comp:36-37 needs M % 64 == 0); the
 // math is its dequant w = float(v) * scale (q4gemm.comp:104-122) and a dot
-// product over K.  Doing that on CUDA cores costs ~2 + M instructions per
-// weight, which is more than the HBM stream allows at M = 8.  Here the
-// weights are the MMA's A operand and the per-group scale is applied after
-// the MMA, so a weight costs ~2 instructions whatever M is:
+// product over K.  On CUDA cores that costs M/2 + ~2.5 fp32-pipe instructions
+// per weight, which at M >= 4 is more than the HBM stream of one small layer
+// leaves time for.  Here the weights are the MMA's A operand and the
+// per-group scale is applied after the MMA, so a weight costs ~1.5
+// instructions whatever M is:
 //
-//   * A = W^T tile: 128 weight columns (TMEM lanes) x 64 k, the int4 values
-//     v themselves as f16 (exact), written by the dequant warps into the
-//     canonical K-major 128B-swizzled layout;
-//   * B = X^T: 16 "rows" = x_hi (8 rows) and x_lo (8 rows), x * 2^e = x_hi +
-//     x_lo split into two f16 with a power-of-two exponent e per (row, K
-//     slice); built once per CTA for its K slice (v is exact, x_hi + x_lo
-//     carries ~22 bits, fp32 accumulation: the product error is ~2^-21);
-//   * one tcgen05.mma pair (K = 16 x 2) per 32-k scale group writes a 128 x 16
-//     fp32 partial into its own TMEM slot; four "scale" warps read the slot
-//     (thread = weight column) and accumulate y[m] += s(n, g) *
-//     (D[m] + D[8 + m]) in registers;
-//   * the K slices of a column block run on the CTAs of a cluster (8 x 512 k
-//     at K = 4096); their partials are summed through distributed shared
-//     memory in fixed rank order, the LoRA term is added and Y is stored.
-//
-// All weight loads are issued before griddepcontrol.wait, so under
-// programmatic dependent launch a launch streams its weights while the
-// previous launch finishes.  No load is shared across CTAs.
+//   * a CTA owns C <= 128 weight columns (the MMA's M rows / TMEM lanes) and a
+//     K slice of <= 1024 (32 scale groups); the S slices of a column block are
+//     the CTAs of one cluster.  N is split evenly over as many column blocks
+//     as clusters fit on the GPU at once, so a launch is one wave;
+//   * at entry one thread issues the TMA loads of the CTA's whole packed slice
+//     (128-byte swizzled boxes of 256 k, so DRAM sees whole 128-byte rows; one
+//     mbarrier per box) and the epilogue threads read
+//     their column's scales: none of it depends on the previous launch, so it
+//     happens before griddepcontrol.wait, as does the dequantisation of the
+//     first A stages;
+//   * 8 dequant warps write A = the int4 values v as f16 (exact) into a ring
+//     of 128-byte-swizzled K-major tiles.  Within each 8-k word the k order is
+//     (0,4,1,5,2,6,3,7): one LOP3 turns two nibbles into (1024 + v + 8) f16
+//     pairs and one HSUB2 gives v; the B tiles use the same order, and a dot
+//     product does not depend on it;
+//   * B = X^T, 16 rows: x_hi (8 rows) and x_lo (8 rows) with x * 2^e = x_hi +
+//     x_lo in f16 for a power-of-two e per (row, K slice), built from a TMA
+//     copy of X after griddepcontrol.wait (v exact, x_hi + x_lo ~22 bits,
+//     fp32 accumulation: ~2^-21 relative error per product);
+//   * each 32-k scale group's two MMAs (K = 16) write their own 128 x 16 fp32
+//     TMEM slot (32 slots = all 512 columns), so MMAs never wait for the
+//     epilogue; four epilogue warps (thread = column) read slot g and
+//     accumulate y[m] += s(n, g) * (D[m] + D[8 + m]);
+//   * the cluster's K-slice partials are summed through distributed shared
+//     memory in fixed rank order, the LoRA term is added and Y stored.
+// Every wait is bounded (status word + abort flag); the CTA drains its copies
+// and MMAs and frees its TMEM before it exits.
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -43,50 +53,66 @@ namespace q4 {
 
 namespace {
 
-constexpr int kCols = 128;          // weight columns per CTA (MMA M, TMEM lanes)
-constexpr int kStageK = 64;         // k per stage (2 scale groups)
-constexpr int kAStages = 3;         // dequantised A tiles in flight
-constexpr int kSlots = 8;           // TMEM partial slots (16 columns each)
-constexpr int kThreads = 320;       // 10 warps
-constexpr int kDqWarp0 = 2;         // dequant warps 2..5
-constexpr int kDqWarps = 4;
-constexpr int kScWarp0 = 6;         // scale warps 6..9 (TMEM lane quarters 2, 3, 0, 1)
-constexpr int kScWarps = 4;
-constexpr int kMaxGroups = 32;      // scale groups per K slice
+constexpr int kRows = 128;          // MMA M = TMEM lanes; rows >= C carry no column
+constexpr int kStageK = 64;         // k per stage: one 128-byte f16 row per column
+constexpr int kAStages = 4;         // dequantised A tiles in flight
+constexpr int kMaxGroups = 32;      // 32 TMEM slots x 16 columns = 512
+constexpr int kSlotCols = 16;       // N of each MMA: x_hi rows 0-7, x_lo rows 8-15
+constexpr int kThreads = 448;       // 14 warps
+constexpr int kDqWarp0 = 2;         // dequant warps 2..9
+constexpr int kDqWarps = 8;
+constexpr int kEpWarp0 = 10;        // epilogue warps 10..13 (TMEM lane quarters 2, 3, 0, 1)
+constexpr int kEpWarps = 4;
+constexpr int kXBox = 256;          // X is copied as rows of 256 floats
+constexpr int kRawBoxK = 256;       // k per packed-weight box: one 128-byte row per column
 
 struct DLayout {
-    int GS;           // scale groups in the slice (even, <= 32)
-    int stages;       // GS / 2
-    int raw_off, a_off, bx_off, part_off, bar_off, misc_off, bytes;
+    int kslice, stages, groups, boxes, raw_box;
+    int a_off, b_off, raw_off, x_off, part_off, bar_off, misc_off, bytes;
 };
 
-__host__ __device__ inline DLayout decode_layout(int K, int S) {
+__host__ __device__ inline DLayout decode_layout(int M, int K, int S, int box_rows) {
     DLayout L;
-    L.GS = K / 32 / S;
-    L.stages = L.GS / 2;
+    L.kslice = K / S;
+    L.stages = L.kslice / kStageK;
+    L.groups = L.kslice / 32;
+    L.boxes = L.kslice / kRawBoxK;
+    L.raw_box = box_rows * 128;                            // box_rows x 32 packed words, swizzled
     L.a_off = 0;                                           // kAStages x 16 KB (1024-aligned)
-    L.bx_off = L.a_off + kAStages * kCols * 128;           // stages x 2 KB (1024-aligned)
-    L.raw_off = L.bx_off + L.stages * 2048;                // stages x 4 KB
-    L.part_off = L.raw_off + L.stages * kCols * 32;        // 128 x 8 floats
-    L.bar_off = L.part_off + kCols * 8 * 4;
-    // raw_full[stages], a_full[3], a_empty[3], d_full[8], d_empty[8]
-    L.misc_off = L.bar_off + (L.stages + 2 * kAStages + 2 * kSlots) * 8;
-    L.bytes = L.misc_off + 16 + 8 * 4;                     // tmem holder, abort flag, row exponents
+    L.b_off = L.a_off + kAStages * kRows * 128;            // stages x 2 KB (1024-aligned)
+    L.raw_off = L.b_off + L.stages * 16 * 128;             // boxes x raw_box (1024-aligned)
+    L.x_off = L.raw_off + L.boxes * L.raw_box;             // [M][kslice] fp32
+    L.part_off = L.x_off + M * L.kslice * 4;               // [128][8] fp32
+    L.bar_off = L.part_off + kRows * 8 * 4;
+    // raw_full[boxes], a_full[4], a_empty[4], d_full[groups], x_full, b_ready, mma_done
+    L.misc_off = L.bar_off + (L.boxes + 2 * kAStages + L.groups + 3) * 8;
+    // tmem holder, abort flag, row exponents [8], row-max scratch [4 warps][8]
+    L.bytes = L.misc_off + 16 + 8 * 4 + kEpWarps * 8 * 4;
     return L;
 }
 
-// 8 int4 values of one packed word as four f16 pairs (k, k+1), exact.
-__device__ __forceinline__ uint4 unpack_word_f16(uint32_t q) {
-    const uint32_t lo = (q ^ 0x88888888u) & 0x0F0F0F0Fu;
-    const uint32_t hi = ((q >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;
-    const float2 nbias = make_float2(-8388616.0f, -8388616.0f);
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+
+// Two nibbles (bits 0-3 and 16-19 of u) as the f16 pair (1024 + v + 8):
+// (nibble ^ 8) = v + 8 goes under the exponent bits of 1024 (0x6400).
+__device__ __forceinline__ uint32_t nibble_pair_f16(uint32_t u) {
+    return ((u ^ 0x00080008u) & 0x000F000Fu) | 0x64006400u;
+}
+
+// The 8 int4 values of one packed word (k = 0..7 at bits 4k) as f16, exact,
+// in the k order (0,4,1,5,2,6,3,7).
+__device__ __forceinline__ uint4 unpack_word_f16_perm(uint32_t q) {
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6408u), __ushort_as_half(0x6408u));  // 1032
     uint32_t out[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const float2 mg = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))),
-                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | static_cast<uint32_t>(b))));
-        const float2 v = __fadd2_rn(mg, nbias);
-        out[b] = pack2<__half>(v.x, v.y);
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t p = nibble_pair_f16(q >> (4 * i));  // (k = i, k = i + 4)
+        __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&p), bias);
+        out[i] = *reinterpret_cast<const uint32_t*>(&h);
     }
     return make_uint4(out[0], out[1], out[2], out[3]);
 }
@@ -101,233 +127,289 @@ __device__ __forceinline__ int row_exponent(float mx) {
     return e < -60 ? -60 : (e > 60 ? 60 : e);
 }
 
-// Byte offset of (row r, k index kk in 0..63) inside one 16-row x 64-k
-// K-major 128B-swizzled tile.
-__device__ __forceinline__ int sw128_offset(int r, int kk) {
-    return r * 128 + ((((kk >> 3) ^ (r & 7))) << 4) + (kk & 7) * 2;
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-    q4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ x,
-                     const float* __restrict__ scales, float* __restrict__ y, int M, int N, int K,
-                     const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank, float lora_scale,
-                     int* __restrict__ status) {
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw_base = smem_u32(smem_raw);
-    const uint32_t base = (raw_base + 1023u) & ~1023u;
-    uint8_t* smem = smem_raw + (base - raw_base);
+// Named barrier over the 128 epilogue threads.
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-    cg::cluster_group cluster = cg::this_cluster();
-    const int S = static_cast<int>(cluster.num_blocks());
-    const int crank = static_cast<int>(cluster.block_rank());
-    const DLayout L = decode_layout(K, S);
-    const int GS = L.GS, NST = L.stages;
-    const int G = K / 32;
-    const int g0 = crank * GS;                  // first group of this K slice
-    const int k0 = g0 * 32;
-    const int n0 = (blockIdx.x / S) * kCols;    // the cluster's column block
+__global__ void __launch_bounds__(kThreads, 1)
+    q4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                     const float* __restrict__ scales, float* __restrict__ y, int M, int N, int K, int G,
+                     int box_rows, const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
+                     float lora_scale, int* __restrict__ status) {
+    extern __shared__ uint8_t smem_raw[];
+    // 128-byte swizzled tiles need 1024-byte alignment in the shared window;
+    // dynamic shared memory of a kernel without static shared memory starts
+    // 1024-aligned.  Anything else is reported, not used.
+    uint8_t* smem = smem_raw;
+    const uint32_t base = smem_u32(smem_raw);
+    if ((base & 1023u) != 0) {
+        if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadLaunch);
+        return;
+    }
+
+    const int S = static_cast<int>(cluster_nctarank());
+    const int crank = static_cast<int>(cluster_ctarank());
+    const DLayout L = decode_layout(M, K, S, box_rows);
+    const int blk = static_cast<int>(blockIdx.x) / S;
+    const int n0 = static_cast<int>(static_cast<long long>(blk) * N / G);
+    const int C = static_cast<int>(static_cast<long long>(blk + 1) * N / G) - n0;  // <= box_rows
+    const int k0 = crank * L.kslice;
+    const int g0 = k0 / 32;
 
     const uint32_t bar = base + L.bar_off;
-    auto raw_full = [&](int st) { return bar + 8u * st; };
-    auto a_full = [&](int i) { return bar + 8u * (NST + i); };
-    auto a_empty = [&](int i) { return bar + 8u * (NST + kAStages + i); };
-    auto d_full = [&](int i) { return bar + 8u * (NST + 2 * kAStages + i); };
-    auto d_empty = [&](int i) { return bar + 8u * (NST + 2 * kAStages + kSlots + i); };
+    auto raw_full = [&](int b) { return bar + 8u * b; };
+    auto a_full = [&](int i) { return bar + 8u * (L.boxes + i); };
+    auto a_empty = [&](int i) { return bar + 8u * (L.boxes + kAStages + i); };
+    auto d_full = [&](int g) { return bar + 8u * (L.boxes + 2 * kAStages + g); };
+    const uint32_t x_full = bar + 8u * (L.boxes + 2 * kAStages + L.groups);
+    const uint32_t b_ready = x_full + 8u;
+    const uint32_t mma_done = x_full + 16u;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
-    int* row_max = reinterpret_cast<int*>(smem + L.misc_off + 16);  // [8] max |x| of each row (float bits)
-    float* part = reinterpret_cast<float*>(smem + L.part_off);      // [128][8]
+    int* row_exp = reinterpret_cast<int*>(smem + L.misc_off + 16);        // [8]
+    float* row_max = reinterpret_cast<float*>(smem + L.misc_off + 48);   // [4 warps][8]
+    float* part = reinterpret_cast<float*>(smem + L.part_off);            // [128][8]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int st = 0; st < NST; ++st) mbar_init(raw_full(st), 1);
+        for (int b = 0; b < L.boxes; ++b) mbar_init(raw_full(b), 1);
         for (int i = 0; i < kAStages; ++i) {
             mbar_init(a_full(i), kDqWarps);
             mbar_init(a_empty(i), 1);
         }
-        for (int i = 0; i < kSlots; ++i) {
-            mbar_init(d_full(i), 1);
-            mbar_init(d_empty(i), kScWarps);
-        }
+        for (int g = 0; g < L.groups; ++g) mbar_init(d_full(g), 1);
+        mbar_init(x_full, 1);
+        mbar_init(b_ready, 1);
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
-        for (int m = 0; m < 8; ++m) row_max[m] = 0;
         fence_mbarrier_init();
+        // The packed slice does not depend on the previous launch; it goes
+        // out first, before the TMEM allocation and the CTA barrier.
+        tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_x);
+        for (int b = 0; b < L.boxes; ++b) {
+            mbar_arrive_expect_tx(raw_full(b), static_cast<uint32_t>(L.raw_box));
+            tma_load_2d(base + L.raw_off + b * L.raw_box, &tmap_w, raw_full(b), (k0 + b * kRawBoxK) / 8, n0);
+        }
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), kSlots * 16);
+        tmem_alloc(smem_u32(tmem_holder), kMaxGroups * kSlotCols);
         tmem_relinquish();
     }
     tc_fence_before_sync();
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_holder;
-
-    // Weights do not depend on the previous launch: the whole slice's packed
-    // W streams in (one 2-D TMA box per 64-k stage) before griddepcontrol.wait.
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmap_w);
-        for (int st = 0; st < NST; ++st) {
-            mbar_arrive_expect_tx(raw_full(st), kCols * 32);
-            tma_load_2d(base + L.raw_off + st * kCols * 32, &tmap_w, raw_full(st), (k0 + st * kStageK) / 8, n0);
-        }
-    }
-    // Scale warps: this thread's column scales for the slice, also before the wait.
+    // Epilogue threads: this column's scales for the slice (also independent).
     float sc[kMaxGroups];
     const int quarter = warp & 3;
-    const int col = quarter * 32 + lane;  // TMEM lane = weight column within the block
-    if (warp >= kScWarp0) {
+    const int col = quarter * 32 + lane;  // TMEM lane = column within the block
+    if (warp >= kEpWarp0) {
         const int n = n0 + col;
-        const float* srow = scales + static_cast<size_t>(n < N ? n : 0) * G + g0;
+        const bool have = col < C && n < N;
+        const float4* srow = reinterpret_cast<const float4*>(scales + static_cast<size_t>(have ? n : 0) * (K / 32) + g0);
 #pragma unroll
-        for (int g = 0; g < kMaxGroups; ++g) sc[g] = (g < GS && n < N) ? __ldg(srow + g) : 0.0f;
-    }
-
-    pdl_wait();  // X and the LoRA projection may come from the previous launch
-
-    // ---------------------------------------------------- B = X^T tile --
-    // Row maxima over the slice (non-negative float bits order like ints).
-    if (warp >= kDqWarp0) {
-        const int t = tid - kDqWarp0 * 32;  // 0..255
-        for (int m = 0; m < M; ++m) {
-            float mx = 0.0f;
-            for (int k = t; k < GS * 32; k += 256) mx = fmaxf(mx, fabsf(x[static_cast<size_t>(m) * K + k0 + k]));
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            if (lane == 0) atomicMax(&row_max[m], __float_as_int(mx));
+        for (int g4 = 0; g4 < kMaxGroups / 4; ++g4) {
+            const float4 v = (have && g4 * 4 < L.groups) ? __ldg(srow + g4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            sc[4 * g4] = v.x;
+            sc[4 * g4 + 1] = v.y;
+            sc[4 * g4 + 2] = v.z;
+            sc[4 * g4 + 3] = v.w;
         }
     }
-    __syncthreads();
-    if (warp >= kDqWarp0) {
-        const int t = tid - kDqWarp0 * 32;
-        // per-row exponent e with max|x * 2^e| in [2^13, 2^14)
-        float rs[8];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) rs[m] = exp2i(row_exponent(__int_as_float(row_max[m])));
-        // units: (row m of 8, 8-k chunk of the slice); writes the hi row m and
-        // the lo row 8 + m of the stage tile
-        const int chunks = GS * 4;
-        for (int u = t; u < 8 * chunks; u += 256) {
-            const int m = u / chunks, c = u % chunks;
-            const int st = c / 8, kk = (c % 8) * 8;
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float a0 = 0.0f, a1 = 0.0f;
-                if (m < M) {
-                    a0 = x[static_cast<size_t>(m) * K + k0 + c * 8 + 2 * i] * rs[m];
-                    a1 = x[static_cast<size_t>(m) * K + k0 + c * 8 + 2 * i + 1] * rs[m];
-                }
-                const __half2 h = __floats2half2_rn(a0, a1);
-                const float2 hf = __half22float2(h);
-                const __half2 l = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
-                hw[i] = *reinterpret_cast<const uint32_t*>(&h);
-                lw[i] = *reinterpret_cast<const uint32_t*>(&l);
-            }
-            uint8_t* tile = smem + L.bx_off + st * 2048;
-            *reinterpret_cast<uint4*>(tile + sw128_offset(m, kk)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(tile + sw128_offset(8 + m, kk)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
-        fence_proxy_async_smem();
-    }
-    __syncthreads();
+    // Dependents may launch now.  Only the X copy and the final Y/LoRA phase
+    // wait for the previous launch; dequantisation runs ahead of it.
     pdl_launch_dependents();
+    if (warp == 0 && lane == 0) {
+        pdl_wait();
+        mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(M * L.kslice * 4));
+        for (int m = 0; m < M; ++m)
+            tma_load_2d(base + L.x_off + m * L.kslice * 4, &tmap_x, x_full, 0, m * (K / kXBox) + k0 / kXBox);
+    }
 
     if (warp == 1) {
         // ------------------------------------------------------------- MMA --
         if (elect_one()) {
-            const uint32_t idesc = umma_idesc_f16(0u, 128u, 16u);
-            bool ok = true;
-            for (int st = 0; st < NST && ok; ++st) {
+            const uint32_t idesc = umma_idesc_f16(0u, static_cast<uint32_t>(kRows), static_cast<uint32_t>(kSlotCols));
+            bool ok = mbar_wait(b_ready, 0u, abort_flag, status, kStatusTimeoutMma);
+            tc_fence_after_sync();
+            for (int st = 0; st < L.stages && ok; ++st) {
                 const int ai = st % kAStages;
                 if (!mbar_wait(a_full(ai), (st / kAStages) & 1u, abort_flag, status, kStatusTimeoutMma)) break;
                 tc_fence_after_sync();
 #pragma unroll
                 for (int g = 0; g < 2; ++g) {
-                    const int gi = st * 2 + g, slot = gi % kSlots;
-                    if (!mbar_wait(d_empty(slot), ((gi / kSlots) & 1u) ^ 1u, abort_flag, status, kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after_sync();
+                    const int gi = st * 2 + g;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int kk = g * 2 + h;  // k16 step within the stage
-                        const uint64_t ad = umma_desc_k_sw128(base + L.a_off + ai * kCols * 128 + kk * 32);
-                        const uint64_t bd = umma_desc_k_sw128(base + L.bx_off + st * 2048 + kk * 32);
-                        umma_f16_ss(tmem_base + static_cast<uint32_t>(slot * 16), ad, bd, idesc, h);
+                        const uint64_t ad = umma_desc_k_sw128(base + L.a_off + ai * kRows * 128 + kk * 32);
+                        const uint64_t bd = umma_desc_k_sw128(base + L.b_off + st * 16 * 128 + kk * 32);
+                        umma_f16_ss(tmem_base + static_cast<uint32_t>(gi * kSlotCols), ad, bd, idesc, h);
                     }
-                    umma_commit(d_full(slot));
+                    umma_commit(d_full(gi));
                 }
                 umma_commit(a_empty(ai));
             }
+            umma_commit(mma_done);  // tracks every MMA issued above
         }
+        __syncwarp();
     } else if (warp >= kDqWarp0 && warp < kDqWarp0 + kDqWarps) {
         // --------------------------------------------------------- dequant --
-        const int dt = tid - kDqWarp0 * 32;  // 0..127, two (column, half) units each
-        for (int st = 0; st < NST; ++st) {
+        // Thread u: column row n = u / 2, k half h = u % 2 of each stage (four
+        // packed words, the 16-byte chunk (st % 4) * 2 + h of the row's
+        // swizzled 128-byte box row -> four 16-byte chunks of the f16 row).
+        const int u = tid - kDqWarp0 * 32;
+        const int n = u >> 1, h = u & 1;
+        for (int st = 0; st < L.stages; ++st) {
             const int ai = st % kAStages;
-            if (!mbar_wait(raw_full(st), 0u, abort_flag, status, kStatusTimeoutDequant)) break;
+            if ((st & 3) == 0 && !mbar_wait(raw_full(st >> 2), 0u, abort_flag, status, kStatusTimeoutDequant)) break;
             if (st >= kAStages &&
                 !mbar_wait(a_empty(ai), ((st / kAStages) - 1) & 1u, abort_flag, status, kStatusTimeoutDequant))
                 break;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int u = dt + i * 128;
-                const int nl = u >> 1, hh = u & 1;
-                const uint4 q = *reinterpret_cast<const uint4*>(smem + L.raw_off + st * kCols * 32 + nl * 32 + hh * 16);
-                uint8_t* arow = smem + L.a_off + ai * kCols * 128 + nl * 128;
+            if (n < box_rows) {  // rows past the box stay stale; their TMEM lanes are never read
+                const int chunk = (((st & 3) * 2 + h) ^ (n & 7));
+                const uint4 q = *reinterpret_cast<const uint4*>(smem + L.raw_off + (st >> 2) * L.raw_box + n * 128 +
+                                                                chunk * 16);
+                const uint32_t row = base + L.a_off + ai * kRows * 128 + n * 128;
                 const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int chunk = (hh * 4 + j) ^ (nl & 7);
-                    *reinterpret_cast<uint4*>(arow + chunk * 16) = unpack_word_f16(words[j]);
-                }
+                for (int j = 0; j < 4; ++j)
+                    sts128(row + ((static_cast<uint32_t>(h * 4 + j) ^ static_cast<uint32_t>(n & 7)) << 4),
+                           unpack_word_f16_perm(words[j]));
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(a_full(ai));
         }
-    } else if (warp >= kScWarp0) {
-        // ----------------------------------------------------------- scale --
+    } else if (warp >= kEpWarp0) {
+        // ------------------------------------------------- B tile, epilogue --
+        const int et = tid - kEpWarp0 * 32;  // 0..127
+        const int ew = warp - kEpWarp0;
+        bool ok = mbar_wait(x_full, 0u, abort_flag, status, kStatusTimeoutEpilogue);
+        const float* xs = reinterpret_cast<const float*>(smem + L.x_off);
+        // items (stage, word): 8 consecutive k of the slice
+        const int items = L.stages * 8;
+        float mx[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) mx[m] = 0.0f;
+        if (ok) {
+            for (int it = et; it < items; it += 128) {
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    if (m < M) {
+                        const float4 a = *reinterpret_cast<const float4*>(xs + m * L.kslice + it * 8);
+                        const float4 b = *reinterpret_cast<const float4*>(xs + m * L.kslice + it * 8 + 4);
+                        mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                        mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], off));
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) row_max[ew * 8 + m] = mx[m];
+        }
+        epilogue_sync();
+        float rs[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const float v = fmaxf(fmaxf(row_max[m], row_max[8 + m]), fmaxf(row_max[16 + m], row_max[24 + m]));
+            const int e = row_exponent(v);
+            rs[m] = exp2i(e);
+            if (et == 0) row_exp[m] = e;
+        }
+        if (ok) {
+            for (int it = et; it < items; it += 128) {
+                const int st = it >> 3, w = it & 7;
+                const uint32_t tile = base + L.b_off + st * 16 * 128;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    float v[8];
+                    if (m < M) {
+                        const float4 a = *reinterpret_cast<const float4*>(xs + m * L.kslice + it * 8);
+                        const float4 b = *reinterpret_cast<const float4*>(xs + m * L.kslice + it * 8 + 4);
+                        v[0] = a.x * rs[m]; v[1] = a.y * rs[m]; v[2] = a.z * rs[m]; v[3] = a.w * rs[m];
+                        v[4] = b.x * rs[m]; v[5] = b.y * rs[m]; v[6] = b.z * rs[m]; v[7] = b.w * rs[m];
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+                    }
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {  // pair (k = i, k = i + 4)
+                        const __half2 hh = __floats2half2_rn(v[i], v[i + 4]);
+                        const float2 hf = __half22float2(hh);
+                        const __half2 ll = __floats2half2_rn(v[i] - hf.x, v[i + 4] - hf.y);
+                        hw[i] = *reinterpret_cast<const uint32_t*>(&hh);
+                        lw[i] = *reinterpret_cast<const uint32_t*>(&ll);
+                    }
+                    // rows m (hi) and 8 + m (lo); chunk w swizzled by row & 7 (= m)
+                    const uint32_t chunk = (static_cast<uint32_t>(w) ^ static_cast<uint32_t>(m)) << 4;
+                    sts128(tile + m * 128 + chunk, make_uint4(hw[0], hw[1], hw[2], hw[3]));
+                    sts128(tile + (8 + m) * 128 + chunk, make_uint4(lw[0], lw[1], lw[2], lw[3]));
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        epilogue_sync();
+        if (et == 0) mbar_arrive(b_ready);
+
         float acc[8];
 #pragma unroll
         for (int m = 0; m < 8; ++m) acc[m] = 0.0f;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-        for (int gi = 0; gi < GS; ++gi) {
-            const int slot = gi % kSlots;
-            if (!mbar_wait(d_full(slot), (gi / kSlots) & 1u, abort_flag, status, kStatusTimeoutEpilogue)) break;
-            tc_fence_after_sync();
-            uint32_t r[16];
-            tmem_ld16(lane_base + static_cast<uint32_t>(slot * 16), r);
-            tmem_ld_wait();
-            // select the group's scale without dynamic register indexing
-            float s = 0.0f;
 #pragma unroll
-            for (int g = 0; g < kMaxGroups; ++g) s = (g == gi) ? sc[g] : s;
+        for (int gi = 0; gi < kMaxGroups; ++gi) {
+            if (gi < L.groups && ok) {
+                if (!mbar_wait(d_full(gi), 0u, abort_flag, status, kStatusTimeoutEpilogue)) {
+                    ok = false;
+                } else {
+                    tc_fence_after_sync();
+                    uint32_t r[16];
+                    tmem_ld16(lane_base + static_cast<uint32_t>(gi * kSlotCols), r);
+                    tmem_ld_wait();
 #pragma unroll
-            for (int m = 0; m < 8; ++m)
-                acc[m] = fmaf(s, __uint_as_float(r[m]) + __uint_as_float(r[8 + m]), acc[m]);
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty(slot));
+                    for (int m = 0; m < 8; ++m)
+                        acc[m] = fmaf(sc[gi], __uint_as_float(r[m]) + __uint_as_float(r[8 + m]), acc[m]);
+                }
+            }
         }
 #pragma unroll
-        for (int m = 0; m < 8; ++m) part[col * 8 + m] = acc[m] * exp2i(-row_exponent(__int_as_float(row_max[m])));
+        for (int m = 0; m < 8; ++m) part[col * 8 + m] = acc[m] * exp2i(-row_exp[m]);
     }
 
     // ------------------------------------- cross-slice sum, LoRA, store --
+    pdl_wait();  // T and Y may be touched by the previous launch (returns at once by now)
     tc_fence_before_sync();
-    cluster.sync();
+    if (S > 1) {
+        cluster_sync_all();
+    } else {
+        __syncthreads();
+    }
     if (*abort_flag == 0) {
-        const int per = kCols / S;  // columns reduced by this CTA
-        for (int idx = tid; idx < per * M; idx += kThreads) {
-            const int cl = crank * per + idx / M, m = idx % M;
+        cg::cluster_group cluster = cg::this_cluster();
+        const int c_lo = C * crank / S, c_hi = C * (crank + 1) / S;  // columns this CTA finishes
+        for (int idx = tid; idx < (c_hi - c_lo) * M; idx += kThreads) {
+            const int cl = c_lo + idx / M, m = idx % M;
             const int n = n0 + cl;
             if (n >= N) continue;
-            float sum = 0.0f;
-            for (int r = 0; r < S; ++r) sum += cluster.map_shared_rank(part, r)[cl * 8 + m];
-            if (lora_t != nullptr) {
+            float v[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) v[r] = r < S ? cluster.map_shared_rank(part, r)[cl * 8 + m] : 0.0f;
+            float sum = v[0];
+#pragma unroll
+            for (int r = 1; r < 8; ++r) sum += v[r];  // fixed rank order; ranks >= S add zero
+            if (lora_b != nullptr) {
                 float d = 0.0f;
                 for (int j = 0; j < rank; ++j) d = fmaf(lora_t[m * rank + j], lora_b[static_cast<size_t>(j) * N + n], d);
                 sum = fmaf(lora_scale, d, sum);
@@ -335,38 +417,75 @@ __global__ void __launch_bounds__(kThreads, 2)
             y[static_cast<size_t>(m) * N + n] = sum;
         }
     } else if (warp == 0 && lane == 0) {
-        for (int st = 0; st < NST; ++st) mbar_drain(raw_full(st), 0u);  // copies in flight land first
+        // copies already issued land before the CTA's shared memory is released
+        for (int b = 0; b < L.boxes; ++b) mbar_drain(raw_full(b), 0u);
+        mbar_drain(x_full, 0u);
     }
-    cluster.sync();  // partials stay alive until every peer has read them
+    if (S > 1) cluster_sync_all();  // partials stay alive until every peer has read them
     if (warp == 1) {
+        mbar_drain(mma_done, 0u);  // no MMA may still write the TMEM being freed
         tc_fence_after_sync();
-        tmem_dealloc(tmem_base, kSlots * 16);
+        tmem_dealloc(tmem_base, kMaxGroups * kSlotCols);
     }
 }
+
+int max_clusters_cache[9][2] = {};  // [S][0] = smem bytes cached for, [S][1] = clusters
 
 }  // namespace
 
-bool decode_supported(int M, int K, int S) {
-    if (M < 1 || M > 8 || S < 1 || S > 8 || K % 32) return false;
-    const int G = K / 32;
-    if (G % S) return false;
-    const int GS = G / S;
-    return GS % 2 == 0 && GS >= 2 && GS <= kMaxGroups;
+size_t decode_smem_bytes(int M, int K, int S, int box_rows) {
+    return static_cast<size_t>(decode_layout(M, K, S, box_rows).bytes);
 }
 
-size_t decode_smem_bytes(int K, int S) { return static_cast<size_t>(decode_layout(K, S).bytes) + 1024; }
+// K split: the smallest S (cluster size) leaving <= 1024 k (32 groups) per CTA;
+// 0 when the shape is not supported.
+int decode_split(int M, int K) {
+    if (M < 1 || M > 8 || K % kXBox != 0) return 0;
+    for (int S = 1; S <= 8; S *= 2)
+        if (K % (S * kRawBoxK) == 0 && K / S <= kMaxGroups * 32) return S;
+    return 0;
+}
 
-int decode_columns_per_cluster() { return kCols; }
+int decode_max_clusters(int M, int K, int S, int box_rows) {
+    const size_t smem = decode_smem_bytes(M, K, S, box_rows);
+    if (smem > 227 * 1024 || S < 1 || S > 8) return 0;
+    int (&c)[2] = max_clusters_cache[S];
+    if (c[0] == static_cast<int>(smem)) return c[1];
+    cudaError_t e = cudaFuncSetAttribute(q4_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(S));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, q4_decode_kernel, &cfg) != cudaSuccess) return 0;
+    c[0] = static_cast<int>(smem);
+    c[1] = n;
+    return n;
+}
 
-int launch_decode(const GemvArgs& a, cudaStream_t stream) {
+int decode_rows() { return kRows; }
+int decode_x_box() { return kXBox; }
+
+int launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     const int S = a.cluster_k;
-    const size_t smem = decode_smem_bytes(a.K, S);
+    if (decode_split(a.M, a.K) != S || a.col_blocks < 1 || a.box_rows < 8 || a.box_rows > kRows ||
+        (a.N + a.col_blocks - 1) / a.col_blocks > a.box_rows)
+        return static_cast<int>(cudaErrorInvalidValue);
+    const size_t smem = decode_smem_bytes(a.M, a.K, S, a.box_rows);
     cudaError_t e =
         cudaFuncSetAttribute(q4_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
-    const int blocks = (a.N + kCols - 1) / kCols;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(S * blocks), 1, 1);
+    cfg.gridDim = dim3(static_cast<unsigned>(S * a.col_blocks), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -379,8 +498,8 @@ int launch_decode(const GemvArgs& a, cudaStream_t stream) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    e = cudaLaunchKernelEx(&cfg, q4_decode_kernel, a.tmap_w, a.x, a.scales, a.y, a.M, a.N, a.K, a.lora_t, a.lora_b,
-                           a.rank, a.lora_scale, a.status);
+    e = cudaLaunchKernelEx(&cfg, q4_decode_kernel, a.tmap_w, a.tmap_x, a.scales, a.y, a.M, a.N, a.K, a.col_blocks,
+                           a.box_rows, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
     return static_cast<int>(e);
 }
 

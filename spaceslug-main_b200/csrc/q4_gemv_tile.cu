@@ -47,19 +47,19 @@ constexpr int kTSlot = 32;       // rows (columns of W) per shared-memory box sl
 constexpr int kTBoxK = 256;      // k per weight box: one 128-byte row (32 words) per column
 constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row per column
 
-// Warps per CTA: 16 for M <= 2 (latency hiding at <= 64 registers, so two
-// CTAs share an SM), 8 above.
+// Warps per CTA: 16 for M <= 4 (latency hiding; at M <= 2 within 64
+// registers, so two CTAs share an SM), 8 above.
 template <int M>
 struct TileCfg {
-    static constexpr int kWarps = M <= 2 ? 16 : 8;
+    static constexpr int kWarps = M <= 4 ? 16 : 8;
     static constexpr int kThreads = kWarps * 32;
 };
 
-__host__ __device__ inline int tile_warps(int M) { return M <= 2 ? 16 : 8; }
+__host__ __device__ inline int tile_warps(int M) { return M <= 4 ? 16 : 8; }
 
 struct TileLayout {
     int kslice, nbox, nsbox;
-    int w_off, s_off, x_off, part_off, cpart_off, bar_off, misc_off, bytes;
+    int w_off, s_off, x_off, x_bytes, part_off, cpart_off, bar_off, misc_off, bytes;
 };
 
 __host__ __device__ inline TileLayout tile_layout(int M, int K, int S) {
@@ -70,8 +70,11 @@ __host__ __device__ inline TileLayout tile_layout(int M, int K, int S) {
     L.w_off = 0;                                       // nbox x [32 rows][128 B], swizzled
     L.s_off = L.w_off + L.nbox * kTSlot * 128;        // nsbox x [32 rows][128 B], swizzled
     L.x_off = L.s_off + L.nsbox * kTSlot * 128;       // [M][kslice] fp32
-    L.part_off = L.x_off + M * L.kslice * 4;          // [warp][M][32] fp32
-    L.cpart_off = L.part_off + tile_warps(M) * kTSlot * M * 4;  // [M][32] fp32 (the CTA's K-slice sum)
+    // the per-warp partials [warp][M][32] reuse the X region once X is consumed
+    const int part_bytes = tile_warps(M) * kTSlot * M * 4;
+    L.x_bytes = M * L.kslice * 4 > part_bytes ? M * L.kslice * 4 : part_bytes;
+    L.part_off = L.x_off;
+    L.cpart_off = L.x_off + L.x_bytes;                 // [M][32] fp32 (the CTA's K-slice sum)
     L.bar_off = L.cpart_off + kTSlot * M * 4;
     L.misc_off = L.bar_off + (L.nbox + 2) * 8;         // wfull[nbox], sfull, xfull
     L.bytes = L.misc_off + 16;                         // abort flag
@@ -150,8 +153,15 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
     constexpr int kThreads = TileCfg<M>::kThreads;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte swizzled TMA destinations need 1024-byte alignment.
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t base = smem_u32(smem);
+    // 128-byte swizzled TMA boxes need 1024-byte alignment in the shared
+    // window; dynamic shared memory of a kernel without static shared memory
+    // starts 1024-aligned.  Anything else is reported, not used.
+    uint8_t* smem = smem_raw;
+    const uint32_t base = smem_u32(smem_raw);
+    if ((base & 1023u) != 0) {
+        if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadLaunch);
+        return;
+    }
     const int S = static_cast<int>(cluster_nctarank());
     const int crank = static_cast<int>(cluster_ctarank());
     const TileLayout L = tile_layout(M, K, S);
@@ -279,6 +289,7 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
     }
 
     // ------------------------------------------------------------- reduce --
+    __syncthreads();  // every warp is done with X: its region takes the partials
     float* part = reinterpret_cast<float*>(smem + L.part_off);  // [warp][M][col]
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -336,7 +347,7 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
 template <int M>
 int launch_tile_m(const GemvTileArgs& a, cudaStream_t stream) {
     const TileLayout L = tile_layout(M, a.K, a.cluster_k);
-    const size_t smem = static_cast<size_t>(L.bytes) + 1024;
+    const size_t smem = static_cast<size_t>(L.bytes);
     auto kern = q4_gemv_tile_kernel<M>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -366,9 +377,7 @@ int launch_tile_m(const GemvTileArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
-size_t gemv_tile_smem_bytes(int M, int K, int S) {
-    return static_cast<size_t>(tile_layout(M, K, S).bytes) + 1024;
-}
+size_t gemv_tile_smem_bytes(int M, int K, int S) { return static_cast<size_t>(tile_layout(M, K, S).bytes); }
 
 bool gemv_tile_supported(int M, int K, int S) {
     if (M < 1 || M > 8 || S < 1 || S > 8 || (S & (S - 1)) != 0) return false;

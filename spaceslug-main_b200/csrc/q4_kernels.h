@@ -29,12 +29,29 @@ struct GemvArgs {
     int* status;             // kernel status word (0 = ok)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t stream);
-// Tensor-core decode (M <= 8): clusters of `cluster_k` CTAs over K, 128
-// columns per cluster; a.tmap_w box = 8 words x 128 columns.
-bool decode_supported(int M, int K, int S);
-size_t decode_smem_bytes(int K, int S);
-int decode_columns_per_cluster();
-int launch_decode(const GemvArgs& a, cudaStream_t stream);
+// Tensor-core decode (M <= 8): col_blocks blocks of <= 128 columns, each a
+// cluster of cluster_k CTAs splitting K into slices of <= 1024.
+struct DecodeArgs {
+    CUtensorMap tmap_w;      // packed uint32 [N][K/8], box 32 words x box_rows, 128B swizzle
+    CUtensorMap tmap_x;      // X fp32 viewed as [M*K/256][256], box 256 x (K/cluster_k/256)
+    const float* scales;     // [N][K/32], 16-byte aligned
+    float* y;                // [M][N]
+    int M, N, K;
+    int cluster_k;           // = decode_split(M, K)
+    int col_blocks;          // G: block g holds columns [g*N/G, (g+1)*N/G)
+    int box_rows;            // multiple of 8, >= ceil(N/G), <= 128
+    const float* lora_t;     // [M][rank] or nullptr
+    const float* lora_b;     // [rank][N] or nullptr
+    int rank;
+    float lora_scale;
+    int* status;
+};
+int decode_split(int M, int K);  // cluster size, 0 = shape not supported
+size_t decode_smem_bytes(int M, int K, int S, int box_rows);
+int decode_max_clusters(int M, int K, int S, int box_rows);  // co-resident clusters (one wave)
+int decode_rows();
+int decode_x_box();
+int launch_decode(const DecodeArgs& a, cudaStream_t stream);
 // Whole-tile GEMV (M <= 8): col_blocks blocks of <= 32 columns x K/S per CTA,
 // every load issued at entry.  Needs K % (256 * S) == 0 and 16-byte aligned x,
 // packed and scales.

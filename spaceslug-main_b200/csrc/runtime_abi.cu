@@ -119,13 +119,16 @@ int current_device() {
     return d;
 }
 
-int decode_split_override() {
-    static const int v = [] {
-        const char* e = std::getenv("SPACESLUG_Q4_DECODE_SPLIT");
-        const int s = e ? std::atoi(e) : 0;
-        return (s == 1 || s == 2 || s == 4 || s == 8) ? s : 0;
-    }();
-    return v;
+// Decode variant; SPACESLUG_Q4_DECODE=auto|gemv|mma|tile sets its initial value.
+std::atomic<int>& decode_variant_init() {
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* e = std::getenv("SPACESLUG_Q4_DECODE");
+        const char* names[4] = {"auto", "gemv", "mma", "tile"};
+        for (int i = 0; e && i < 4; ++i)
+            if (std::strcmp(e, names[i]) == 0) g_decode_variant.store(i);
+    });
+    return g_decode_variant;
 }
 
 q4::Operand16 operand_type() {
@@ -275,7 +278,7 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     // Decode (M <= 8).  Automatic choice: the whole-tile GEMV where the shape
     // allows it, else the streamed-ring GEMV; the tensor-core decode only on
     // request.
-    const int dv = g_decode_variant.load();
+    const int dv = decode_variant_init().load();
     if (p.M <= 8 && (dv == 0 || dv == 3)) {
         const int S = tile_split(p.M, p.K);
         if (S > 0 && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
@@ -302,27 +305,25 @@ void run_problem(const Problem& p, cudaStream_t stream) {
         }
     }
     if (p.M <= 8 && dv == 2) {
-        // K split of the tensor-core decode: the first of 8, 4, 2, 1 that fits;
-        // SPACESLUG_Q4_DECODE_SPLIT overrides (1, 2, 4 or 8).
-        int S = 0;
-        const int order[4] = {8, 4, 2, 1};
-        const int forced = decode_split_override();
-        for (int cand : order) {
-            const int c2 = forced > 0 ? forced : cand;
-            if (q4::decode_supported(p.M, p.K, c2) && q4::decode_smem_bytes(p.K, c2) <= 200 * 1024) {
-                S = c2;
-                break;
-            }
-            if (forced > 0) break;
-        }
-        if (S > 0) {
-            q4::GemvArgs a{};
+        const int S = q4::decode_split(p.M, p.K);
+        const int R = q4::decode_rows();
+        const int waves_cl = S > 0 ? q4::decode_max_clusters(p.M, p.K, S, R) : 0;
+        if (S > 0 && waves_cl > 0 && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
+            // one wave of clusters while blocks stay <= 128 columns (>= 8 each)
+            int G = std::min(waves_cl, std::max(1, p.N / 8));
+            G = std::max(G, (p.N + R - 1) / R);
+            const int rows = ((p.N + G - 1) / G + 7) / 8 * 8;
+            q4::DecodeArgs a{};
             encode_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
-                      static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8,
-                      static_cast<uint32_t>(q4::decode_columns_per_cluster()), CU_TENSOR_MAP_SWIZZLE_NONE);
-            a.x = p.x; a.scales = p.scales; a.y = p.y;
+                      static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 32, static_cast<uint32_t>(rows),
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+            const int bx = q4::decode_x_box();
+            encode_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.x, static_cast<uint64_t>(bx),
+                      static_cast<uint64_t>(p.M) * (p.K / bx), static_cast<uint64_t>(bx) * 4,
+                      static_cast<uint32_t>(bx), static_cast<uint32_t>(p.K / S / bx), CU_TENSOR_MAP_SWIZZLE_NONE);
+            a.scales = p.scales; a.y = p.y;
             a.M = p.M; a.N = p.N; a.K = p.K;
-            a.cluster_k = S;
+            a.cluster_k = S; a.col_blocks = G; a.box_rows = rows;
             a.lora_t = lora_t; a.lora_b = p.rank > 0 ? p.lora_b : nullptr; a.rank = p.rank; a.lora_scale = lscale;
             a.status = c.status;
             check_launch(q4::launch_decode(a, stream), "decode launch");
@@ -744,7 +745,7 @@ int spaceslug_q4_set_operand_type(int type) {
 
 int spaceslug_q4_set_decode_variant(int variant) {
     if (variant < 0 || variant > 3) return -1;
-    return g_decode_variant.exchange(variant);
+    return decode_variant_init().exchange(variant);
 }
 
 int spaceslug_q4_set_gemm_variant(int variant) {
