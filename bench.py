@@ -45,10 +45,11 @@ METRIC = "int4 GEMV HBM GB/s (decode), GEMM TFLOP/s (prefill), % roofline, 1–8
 DECODE_LAYERS = 24
 DECODE_SWEEP = (1, 2, 4, 8)
 
-# ncu DRAM traffic (read + write bytes per launch) of the dominant kernel,
-# from the capture summarised in profiles/ (None until captured).
+# ncu DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# q4_gemv_tile_kernel launch per decode M, from the full capture summarised in
+# profiles/decode_tile_kernel.md.
 NCU_TRAFFIC_PER_LAUNCH = {
-    "decode": None,
+    "decode": {1: 10539520, 2: 10559744, 4: 10598144, 8: 10675456},
 }
 
 
@@ -118,59 +119,85 @@ class Dist:
 
 
 # ------------------------------------------------------------------ clocks --
+_CLOCK_POLLER = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
+print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    t = time.time_ns()
+    try:
+        print(t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), pynvml.nvmlDeviceGetPowerUsage(h), flush=True)
+    except pynvml.NVMLError:
+        break
+    time.sleep(0.0005)
+"""
+
+
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons, read through NVML every
-    ~0.5 ms by a thread while the timed region runs.  Read-only queries."""
+    """SM clock, clock-event (throttle) reasons and power, read through NVML
+    every ~0.5 ms by a separate process (read-only queries); only samples
+    taken between start() and stop() are kept."""
 
     REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
                ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
     def __init__(self, torch, device_index: int) -> None:
-        self.handle = None
-        self.samples: list[tuple[int, int, int]] = []
-        self.stop_flag = False
-        self.thread = None
+        self.proc = None
+        self.error = None
         try:
-            import pynvml
-            pynvml.nvmlInit()
             props = torch.cuda.get_device_properties(device_index)
             bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
-            self.nvml = pynvml
-            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".clocks")
+            self.fh = os.fdopen(fd, "w")
+            self.proc = subprocess.Popen([sys.executable, "-c", _CLOCK_POLLER, bus], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL, text=True)
+            deadline = time.time() + 30
+            first = []
+            while time.time() < deadline and self.proc.poll() is None:
+                first = Path(self.path).read_text().split("\n", 1)[0].split()
+                if first and first[0] == "ready":
+                    break
+                time.sleep(0.02)
+            if not first or first[0] != "ready":
+                raise RuntimeError("NVML poller did not start")
+            self.max_mhz = int(first[1])
         except Exception as e:  # no NVML: the line says so
             self.error = f"{type(e).__name__}: {e}"
+            self._kill()
 
-    def _run(self) -> None:
-        nv, h = self.nvml, self.handle
-        while not self.stop_flag:
-            try:
-                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
-                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h),
-                                     nv.nvmlDeviceGetPowerUsage(h)))
-            except Exception:
-                break
-            time.sleep(0.0005)
+    def _kill(self) -> None:
+        if self.proc is not None:
+            self.proc.kill()
+            self.proc.wait(timeout=5)
+            self.proc = None
 
     def start(self) -> None:
-        if self.handle is None:
-            return
-        import threading
-        self.thread = threading.Thread(target=self._run, daemon=True)
-        self.thread.start()
+        self.t0 = time.time_ns()
 
-    def stop(self) -> dict | None:
-        if self.handle is None:
-            return {"unavailable": getattr(self, "error", "no NVML")}
-        self.stop_flag = True
-        if self.thread is not None:
-            self.thread.join(timeout=5)
-        if not self.samples:
-            return {"unavailable": "no samples"}
-        reasons = sorted({name for _, r, _ in self.samples for name, bit in self.REASONS if r & bit})
-        return {"sm_mhz": statistics.median(c for c, _, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.samples),
-                "power_w_max": round(max(p for _, _, p in self.samples) / 1000.0, 1),
+    def stop(self) -> dict:
+        t1 = time.time_ns()
+        if self.proc is None:
+            return {"unavailable": self.error or "no NVML"}
+        time.sleep(0.005)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.fh.close()
+        out = Path(self.path).read_text()
+        os.unlink(self.path)
+        samples = []
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) == 4 and f[0].isdigit() and self.t0 <= int(f[0]) <= t1:
+                samples.append((int(f[1]), int(f[2]), int(f[3])))
+        if not samples:
+            return {"unavailable": "no samples in the timed region"}
+        reasons = sorted({name for _, r, _ in samples for name, bit in self.REASONS if r & bit})
+        return {"sm_mhz": statistics.median(c for c, _, _ in samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(samples),
+                "power_w_max": round(max(p for _, _, p in samples) / 1000.0, 1),
                 "source": "NVML, every ~0.5 ms during the timed region"}
 
 
@@ -359,7 +386,8 @@ def decode_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     d2h = DECODE_LAYERS * sum(m * cfg.n * 4 for m in DECODE_SWEEP)
     for w in layers:
         w.close()
-    traffic = NCU_TRAFFIC_PER_LAUNCH.get("decode")
+    tr = NCU_TRAFFIC_PER_LAUNCH.get("decode")
+    traffic = (sum(tr[m] for m in DECODE_SWEEP) / len(DECODE_SWEEP)) if tr else None  # bytes per launch, sweep mean
     return {
         "value": value, "ms_per_step": total_ms / args.steps, "clocks": clk, "per_m": per_m,
         "gpu_launches": launches_per_step * args.steps,
