@@ -60,7 +60,7 @@ constexpr int kMaxGroups = 32;      // 32 TMEM slots x 16 columns = 512
 constexpr int kSlotCols = 16;       // N of each MMA: x_hi rows 0-7, x_lo rows 8-15
 constexpr int kThreads = 448;       // 14 warps
 constexpr int kDqWarp0 = 2;         // dequant warps 2..9
-constexpr int kDqWarps = 8;
+constexpr int kDqWarps = 8;         // two per A ring slot: slot p = stages p, p + 4, ...
 constexpr int kEpWarp0 = 10;        // epilogue warps 10..13 (TMEM lane quarters 2, 3, 0, 1)
 constexpr int kEpWarps = 4;
 constexpr int kXBox = 256;          // X is copied as rows of 256 floats
@@ -84,8 +84,8 @@ __host__ __device__ inline DLayout decode_layout(int M, int K, int S, int box_ro
     L.x_off = L.raw_off + L.boxes * L.raw_box;             // [M][kslice] fp32
     L.part_off = L.x_off + M * L.kslice * 4;               // [128][8] fp32
     L.bar_off = L.part_off + kRows * 8 * 4;
-    // raw_full[boxes], a_full[4], a_empty[4], d_full[groups], x_full, b_ready, mma_done
-    L.misc_off = L.bar_off + (L.boxes + 2 * kAStages + L.groups + 3) * 8;
+    // raw_full[boxes], a_full[4], stage_done[stages], x_full, b_ready, mma_done
+    L.misc_off = L.bar_off + (L.boxes + kAStages + L.stages + 3) * 8;
     // tmem holder, abort flag, row exponents [8], row-max scratch [4 warps][8]
     L.bytes = L.misc_off + 16 + 8 * 4 + kEpWarps * 8 * 4;
     return L;
@@ -163,9 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t bar = base + L.bar_off;
     auto raw_full = [&](int b) { return bar + 8u * b; };
     auto a_full = [&](int i) { return bar + 8u * (L.boxes + i); };
-    auto a_empty = [&](int i) { return bar + 8u * (L.boxes + kAStages + i); };
-    auto d_full = [&](int g) { return bar + 8u * (L.boxes + 2 * kAStages + g); };
-    const uint32_t x_full = bar + 8u * (L.boxes + 2 * kAStages + L.groups);
+    // one commit per stage: its A slot is free again and its two groups' TMEM
+    // slots hold their results
+    auto stage_done = [&](int st) { return bar + 8u * (L.boxes + kAStages + st); };
+    const uint32_t x_full = bar + 8u * (L.boxes + kAStages + L.stages);
     const uint32_t b_ready = x_full + 8u;
     const uint32_t mma_done = x_full + 16u;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc_off);
@@ -177,11 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int b = 0; b < L.boxes; ++b) mbar_init(raw_full(b), 1);
-        for (int i = 0; i < kAStages; ++i) {
-            mbar_init(a_full(i), kDqWarps);
-            mbar_init(a_empty(i), 1);
-        }
-        for (int g = 0; g < L.groups; ++g) mbar_init(d_full(g), 1);
+        for (int i = 0; i < kAStages; ++i) mbar_init(a_full(i), kDqWarps / kAStages);
+        for (int st = 0; st < L.stages; ++st) mbar_init(stage_done(st), 1);
         mbar_init(x_full, 1);
         mbar_init(b_ready, 1);
         mbar_init(mma_done, 1);
@@ -251,40 +249,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t bd = umma_desc_k_sw128(base + L.b_off + st * 16 * 128 + kk * 32);
                         umma_f16_ss(tmem_base + static_cast<uint32_t>(gi * kSlotCols), ad, bd, idesc, h);
                     }
-                    umma_commit(d_full(gi));
                 }
-                umma_commit(a_empty(ai));
+                umma_commit(stage_done(st));
             }
             umma_commit(mma_done);  // tracks every MMA issued above
         }
         __syncwarp();
     } else if (warp >= kDqWarp0 && warp < kDqWarp0 + kDqWarps) {
         // --------------------------------------------------------- dequant --
-        // Thread u: column row n = u / 2, k half h = u % 2 of each stage (four
-        // packed words, the 16-byte chunk (st % 4) * 2 + h of the row's
+        // Warps 2p and 2p + 1 own A ring slot p and dequantise stages p, p + 4,
+        // ... (four slots fill in parallel); each takes 64 of the 128 rows.
+        // Lane unit v = lane + 32 i: row n = 64 * half + v / 2, k half h = v % 2
+        // (four packed words, the 16-byte chunk (st % 4) * 2 + h of the row's
         // swizzled 128-byte box row -> four 16-byte chunks of the f16 row).
-        const int u = tid - kDqWarp0 * 32;
-        const int n = u >> 1, h = u & 1;
-        for (int st = 0; st < L.stages; ++st) {
-            const int ai = st % kAStages;
-            if ((st & 3) == 0 && !mbar_wait(raw_full(st >> 2), 0u, abort_flag, status, kStatusTimeoutDequant)) break;
-            if (st >= kAStages &&
-                !mbar_wait(a_empty(ai), ((st / kAStages) - 1) & 1u, abort_flag, status, kStatusTimeoutDequant))
+        const int dw = warp - kDqWarp0;
+        const int slot = dw >> 1, half = dw & 1;
+        for (int st = slot; st < L.stages; st += kAStages) {
+            if (!mbar_wait(raw_full(st >> 2), 0u, abort_flag, status, kStatusTimeoutDequant)) break;
+            if (st >= kAStages && !mbar_wait(stage_done(st - kAStages), 0u, abort_flag, status, kStatusTimeoutDequant))
                 break;
-            if (n < box_rows) {  // rows past the box stay stale; their TMEM lanes are never read
-                const int chunk = (((st & 3) * 2 + h) ^ (n & 7));
-                const uint4 q = *reinterpret_cast<const uint4*>(smem + L.raw_off + (st >> 2) * L.raw_box + n * 128 +
-                                                                chunk * 16);
-                const uint32_t row = base + L.a_off + ai * kRows * 128 + n * 128;
-                const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+            const uint8_t* raw = smem + L.raw_off + (st >> 2) * L.raw_box;
+            const uint32_t atile = base + L.a_off + slot * kRows * 128;
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    sts128(row + ((static_cast<uint32_t>(h * 4 + j) ^ static_cast<uint32_t>(n & 7)) << 4),
-                           unpack_word_f16_perm(words[j]));
+            for (int i = 0; i < 4; ++i) {
+                const int v = lane + 32 * i;
+                const int n = half * 64 + (v >> 1), h = v & 1;
+                if (n < box_rows) {  // rows past the box stay stale; their TMEM lanes are never read
+                    const int chunk = (((st & 3) * 2 + h) ^ (n & 7));
+                    const uint4 q = *reinterpret_cast<const uint4*>(raw + n * 128 + chunk * 16);
+                    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        sts128(atile + n * 128 + ((static_cast<uint32_t>(h * 4 + j) ^ static_cast<uint32_t>(n & 7)) << 4),
+                               unpack_word_f16_perm(words[j]));
+                }
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(a_full(ai));
+            if (lane == 0) mbar_arrive(a_full(slot));
         }
     } else if (warp >= kEpWarp0) {
         // ------------------------------------------------- B tile, epilogue --
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int gi = 0; gi < kMaxGroups; ++gi) {
             if (gi < L.groups && ok) {
-                if (!mbar_wait(d_full(gi), 0u, abort_flag, status, kStatusTimeoutEpilogue)) {
+                if (!mbar_wait(stage_done(gi >> 1), 0u, abort_flag, status, kStatusTimeoutEpilogue)) {
                     ok = false;
                 } else {
                     tc_fence_after_sync();

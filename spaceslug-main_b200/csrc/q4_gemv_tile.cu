@@ -47,15 +47,15 @@ constexpr int kTSlot = 32;       // rows (columns of W) per shared-memory box sl
 constexpr int kTBoxK = 256;      // k per weight box: one 128-byte row (32 words) per column
 constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row per column
 
-// Warps per CTA: 16 for M <= 4 (latency hiding; at M <= 2 within 64
+// Warps per CTA: 16 for M <= 6 (latency hiding; at M <= 2 within 64
 // registers, so two CTAs share an SM), 8 above.
 template <int M>
 struct TileCfg {
-    static constexpr int kWarps = M <= 4 ? 16 : 8;
+    static constexpr int kWarps = M <= 6 ? 16 : 8;
     static constexpr int kThreads = kWarps * 32;
 };
 
-__host__ __device__ inline int tile_warps(int M) { return M <= 4 ? 16 : 8; }
+__host__ __device__ inline int tile_warps(int M) { return M <= 6 ? 16 : 8; }
 
 struct TileLayout {
     int kslice, nbox, nsbox;
@@ -247,21 +247,21 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
         for (int t = 0; t < 8; ++t) {
             const uint32_t wa = wrow | ((static_cast<uint32_t>(t) << 4) ^ cq16);
             const uint32_t sa = (srow | (sx ^ (static_cast<uint32_t>(t >> 2) << 4))) + (t & 3) * 4;
-            float2 xv[M][4];
+            if constexpr (M <= 2) {
+                float2 xv[M][4];
 #pragma unroll
-            for (int m = 0; m < M; ++m) {
-                const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
-                const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
-                xv[m][0] = make_float2(xa.x, xa.y);
-                xv[m][1] = make_float2(xa.z, xa.w);
-                xv[m][2] = make_float2(xc.x, xc.y);
-                xv[m][3] = make_float2(xc.z, xc.w);
-            }
+                for (int m = 0; m < M; ++m) {
+                    const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
+                    const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
+                    xv[m][0] = make_float2(xa.x, xa.y);
+                    xv[m][1] = make_float2(xa.z, xa.w);
+                    xv[m][2] = make_float2(xc.x, xc.y);
+                    xv[m][3] = make_float2(xc.z, xc.w);
+                }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t q = lds_u32(wa + r * 8 * 128);
-                const float s = __uint_as_float(lds_u32(sa + r * 8 * 128));
-                if constexpr (M <= 2) {
+                for (int r = 0; r < 4; ++r) {
+                    const uint32_t q = lds_u32(wa + r * 8 * 128);
+                    const float s = __uint_as_float(lds_u32(sa + r * 8 * 128));
                     // per-word partial sum of v * x, scaled once (fewer fp32 ops)
                     float2 v[4];
                     unpack_word_f32(q, v);
@@ -273,15 +273,26 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
                         p = __ffma2_rn(v[3], xv[m][3], p);
                         acc[r][m].x = fmaf(s, p.x + p.y, acc[r][m].x);
                     }
-                } else {
-                    float2 w[4];
-                    dequant_word_f32(q, s, w);
+                }
+            } else {
+                // the four columns' scaled weights first, then X one row at a
+                // time: 32 + 8 live registers besides the accumulators
+                float2 w[4][4];
 #pragma unroll
-                    for (int m = 0; m < M; ++m) {
-                        acc[r][m] = __ffma2_rn(w[0], xv[m][0], acc[r][m]);
-                        acc[r][m] = __ffma2_rn(w[1], xv[m][1], acc[r][m]);
-                        acc[r][m] = __ffma2_rn(w[2], xv[m][2], acc[r][m]);
-                        acc[r][m] = __ffma2_rn(w[3], xv[m][3], acc[r][m]);
+                for (int r = 0; r < 4; ++r)
+                    dequant_word_f32(lds_u32(wa + r * 8 * 128), __uint_as_float(lds_u32(sa + r * 8 * 128)), w[r]);
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
+                    const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
+                    const float2 x0 = make_float2(xa.x, xa.y), x1 = make_float2(xa.z, xa.w);
+                    const float2 x2 = make_float2(xc.x, xc.y), x3 = make_float2(xc.z, xc.w);
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        acc[r][m] = __ffma2_rn(w[r][0], x0, acc[r][m]);
+                        acc[r][m] = __ffma2_rn(w[r][1], x1, acc[r][m]);
+                        acc[r][m] = __ffma2_rn(w[r][2], x2, acc[r][m]);
+                        acc[r][m] = __ffma2_rn(w[r][3], x3, acc[r][m]);
                     }
                 }
             }
