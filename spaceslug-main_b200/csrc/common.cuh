@@ -70,12 +70,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // when the CTA-wide abort flag is (or becomes) set or the wait times out; on a
-// timeout the flag is raised and `code` is recorded in the status word.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+// timeout the flag is raised and `code` is recorded in the status word.  The
+// fast path is one try_wait; the bounded spin is out of line so that a wait on
+// an already completed phase costs little in the pipelines' inner loops.
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                            int code) {
     const unsigned long long t0 = globaltimer_ns();
 #pragma unroll 1
     while (true) {
@@ -87,6 +86,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             return false;
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, abort_flag, status, code);
 }
 
 // Bounded wait that ignores the abort flag: used on the abort path to let

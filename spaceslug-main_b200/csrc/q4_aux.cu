@@ -138,82 +138,128 @@ __global__ void __launch_bounds__(256) pack_kernel(const int8_t* __restrict__ b_
     packed[static_cast<size_t>(n) * chunks + c] = word;
 }
 
-// T[M][rank] = X[M][K] * A[K][rank], fp32.  CTA (rows 8*blockIdx.x .. +7,
-// rank columns 16*blockIdx.y .. +15, k-chunk blockIdx.z of kXaChunk): threads
-// stride over the chunk's k; each k reads the 8 x values and one 64-byte run
-// of A (coalesced across the warp).  Partials are reduced across lanes with
-// shuffles and across warps in shared memory, then written to T directly
-// (one k-chunk) or to partial[z][M][rank] for lora_xa_reduce_kernel, which
-// sums the chunks in fixed order (deterministic).
-constexpr int kXaRows = 8;
+// T = X * A in fp32 (the LoRA projection, lora.py:21-23 forward).  A block
+// covers 64 rows x 16 ranks x a 256-k chunk: it stages the X tile and the A
+// slice in shared memory (all loads issued at once; rows padded so the reads
+// below are free of bank conflicts), then thread (row group g = t / 16, k lane
+// q = t % 16) accumulates rows 4g..4g+3 x 16 ranks over k = q, q + 16, ...
+// (4 scalar X reads and 4 float4 A reads per 64 FMAs) and the 16 k lanes are
+// summed with a butterfly reduce-scatter.  With one chunk the block writes T;
+// with several it writes partial[z][M][rank] and lora_xa_reduce_kernel sums
+// the chunks in fixed order (deterministic).
+constexpr int kXaRows = 64;
 constexpr int kXaCols = 16;
-constexpr int kXaChunk = 1024;
-constexpr int kXaUnroll = 4;
+constexpr int kXaChunk = 256;
+constexpr int kXaXPitch = kXaChunk + 4;  // floats per staged X row
+constexpr int kXaAPitch = kXaCols + 4;   // floats per staged A row
+constexpr int kXaSmem = (kXaRows * kXaXPitch + kXaChunk * kXaAPitch) * 4;
 __global__ void __launch_bounds__(256) lora_xa_kernel(const float* __restrict__ x, const float* __restrict__ a,
                                                       float* __restrict__ out, int M, int K, int rank, int kchunk) {
-    __shared__ float part[8][kXaRows * kXaCols];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    extern __shared__ float xa_smem[];
+    float* xs = xa_smem;                          // [64][kXaXPitch]
+    float* as = xa_smem + kXaRows * kXaXPitch;    // [256][kXaAPitch]
+    const int tid = threadIdx.x, lane = tid & 31;
     const int m0 = blockIdx.x * kXaRows, j0 = blockIdx.y * kXaCols;
-    const int rows = min(kXaRows, M - m0), cols = min(kXaCols, rank - j0);
-    const int k_begin = blockIdx.z * kchunk, k_end = min(K, k_begin + kchunk);
-    float acc[kXaRows][kXaCols];
+    const int cols = min(kXaCols, rank - j0);
+    float acc[4][kXaCols];
 #pragma unroll
-    for (int r = 0; r < kXaRows; ++r)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int j = 0; j < kXaCols; ++j) acc[r][j] = 0.0f;
-    const bool vec = (rank % 4 == 0) && cols == kXaCols;
-    for (int kb = k_begin; kb < k_end; kb += kXaUnroll * 256) {
-#pragma unroll
-        for (int u = 0; u < kXaUnroll; ++u) {
-            // clamped indices keep every load in bounds, so the unrolled
-            // iterations' loads are independent
-            const int k = kb + u * 256 + static_cast<int>(threadIdx.x);
-            const bool kok = k < k_end;
-            const int kc = kok ? k : k_begin;
+    const int g = tid >> 4, q = tid & 15;
+    for (int kb = blockIdx.z * kchunk; kb < min(K, (blockIdx.z + 1) * kchunk); kb += kXaChunk) {
+        const int kn = min(kXaChunk, K - kb);  // a multiple of 32 (K % 32 == 0)
+        // stage X rows m0.. (zero past M) and A rows kb.. (zero past rank)
+        const bool xvec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;  // else scalar loads
+        for (int i = tid; i < kXaRows * (kXaChunk / 4); i += 256) {
+            const int r = i / (kXaChunk / 4), c4 = (i % (kXaChunk / 4)) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m0 + r < M && c4 < kn) {
+                const float* src = x + static_cast<size_t>(m0 + r) * K + kb + c4;
+                v = xvec ? __ldg(reinterpret_cast<const float4*>(src))
+                         : make_float4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+            }
+            *reinterpret_cast<float4*>(xs + r * kXaXPitch + c4) = v;
+        }
+        for (int i = tid; i < kXaChunk * kXaCols; i += 256) {
+            const int k = i / kXaCols, j = i % kXaCols;
+            as[k * kXaAPitch + j] = (k < kn && j < cols) ? __ldg(a + static_cast<size_t>(kb + k) * rank + j0 + j) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = q; k < kXaChunk; k += 16) {
             float av[kXaCols];
-            const float* arow = a + static_cast<size_t>(kc) * rank + j0;
-            if (vec) {
 #pragma unroll
-                for (int j = 0; j < kXaCols; j += 4) {
-                    const float4 v = __ldg(reinterpret_cast<const float4*>(arow + j));
-                    av[j] = v.x; av[j + 1] = v.y; av[j + 2] = v.z; av[j + 3] = v.w;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kXaCols; ++j) av[j] = __ldg(arow + (j < cols ? j : 0));
+            for (int j = 0; j < kXaCols; j += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(as + k * kXaAPitch + j);
+                av[j] = v.x; av[j + 1] = v.y; av[j + 2] = v.z; av[j + 3] = v.w;
             }
 #pragma unroll
-            for (int r = 0; r < kXaRows; ++r) {
-                const float xv = __ldg(x + static_cast<size_t>(m0 + (r < rows ? r : 0)) * K + kc);
-                const float xm = (kok && r < rows) ? xv : 0.0f;
+            for (int r = 0; r < 4; ++r) {
+                const float xv = xs[(4 * g + r) * kXaXPitch + k];
 #pragma unroll
-                for (int j = 0; j < kXaCols; ++j) acc[r][j] = fmaf(xm, j < cols ? av[j] : 0.0f, acc[r][j]);
+                for (int j = 0; j < kXaCols; ++j) acc[r][j] = fmaf(xv, av[j], acc[r][j]);
             }
         }
+        __syncthreads();
     }
-    // 128 partial sums per thread: four reduce-scatters of 32 values
+    // sum the 16 k lanes: butterfly over lane bits 8, 4, 2, 1 (within each
+    // half warp), 64 values -> 4 per lane
+    float v[64];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        float v32[32];
+    for (int i = 0; i < 64; ++i) v[i] = acc[i / kXaCols][i % kXaCols];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v32[i] = acc[(q * 32 + i) / kXaCols][(q * 32 + i) % kXaCols];
-        const float red = warp_reduce_scatter<32>(v32, lane);
-        part[warp][q * 32 + value_index<32>(lane)] = red;
+    for (int half = 32, bit = 8; half >= 4; half >>= 1, bit >>= 1) {
+        const bool upper = (lane & bit) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+        }
     }
-    __syncthreads();
-    if (threadIdx.x < kXaRows * kXaCols) {
-        const int r = threadIdx.x / kXaCols, j = threadIdx.x % kXaCols;
-        float sum = 0.0f;
+    // lane holds values idx(q) .. idx(q) + 3 of the 64 (row-major 4 x 16)
+    int idx = 0;
+    if (q & 8) idx += 32;
+    if (q & 4) idx += 16;
+    if (q & 2) idx += 8;
+    if (q & 1) idx += 4;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) sum += part[w][threadIdx.x];
-        if (r < rows && j < cols)
-            out[(static_cast<size_t>(blockIdx.z) * M + m0 + r) * rank + j0 + j] = sum;
+    for (int e = 0; e < 4; ++e) {
+        const int r = (idx + e) / kXaCols, j = (idx + e) % kXaCols;
+        const int m = m0 + 4 * g + r;
+        if (m < M && j < cols) out[(static_cast<size_t>(blockIdx.z) * M + m) * rank + j0 + j] = v[e];
     }
 }
 
+// T[m][j] = sum over chunks z (fixed order) of partial[z][m][j].  With tlo
+// != nullptr it also writes the bf16 A operand of the GEMM's LoRA stages:
+// row m holds ceil(rank/16) blocks of 64, block q = [hi(16) | lo(16) | hi(16) |
+// 0(16)] of T[m][16q .. 16q+15] * 2^e_m, e_m = row_exp[m] (0 without), hi + lo
+// carrying ~16 bits.
 __global__ void __launch_bounds__(256) lora_xa_reduce_kernel(const float* __restrict__ partial,
-                                                             float* __restrict__ t, int MR, int chunks) {
+                                                             float* __restrict__ t, int M, int rank, int chunks,
+                                                             const int* __restrict__ row_exp,
+                                                             __nv_bfloat16* __restrict__ tlo) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tlo != nullptr) {
+        // one thread per (row, position) of the bf16 operand
+        const int W = (rank + 15) / 16 * 64;
+        if (i >= M * W) return;
+        const int m = i / W, pq = i % W, p = pq % 64, j = (pq / 64) * 16 + p % 16;
+        float v = 0.0f;
+        if (p < 48 && j < rank) {
+            const int MR = M * rank;
+            for (int z = 0; z < chunks; ++z) v += partial[static_cast<size_t>(z) * MR + m * rank + j];
+            if (p < 16) t[m * rank + j] = v;
+            v *= exp2i(row_exp != nullptr ? row_exp[m] : 0);
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+            v = (p >= 16 && p < 32) ? v - __bfloat162float(hi) : __bfloat162float(hi);
+        }
+        tlo[i] = __float2bfloat16_rn(v);
+        return;
+    }
+    const int MR = M * rank;
     if (i >= MR) return;
     float s = 0.0f;
     for (int z = 0; z < chunks; ++z) s += partial[static_cast<size_t>(z) * MR + i];
@@ -274,15 +320,23 @@ int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t
 int lora_xa_chunks(int K) { return (K + kXaChunk - 1) / kXaChunk; }
 
 int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
-                   float* partial) {
+                   float* partial, const int* row_exp, uint16_t* t_op_bits) {
+    __nv_bfloat16* t_op = reinterpret_cast<__nv_bfloat16*>(t_op_bits);
     const int chunks = partial != nullptr ? lora_xa_chunks(K) : 1;
     const dim3 grid((M + kXaRows - 1) / kXaRows, (rank + kXaCols - 1) / kXaCols, chunks);
-    lora_xa_kernel<<<grid, 256, 0, stream>>>(x, a, chunks > 1 ? partial : t, M, K, rank,
-                                             chunks > 1 ? kXaChunk : K);
+    const cudaError_t attr_ok = cudaFuncSetAttribute(lora_xa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kXaSmem);
+    if (attr_ok != cudaSuccess) return static_cast<int>(attr_ok);
+    lora_xa_kernel<<<grid, 256, kXaSmem, stream>>>(x, a, chunks > 1 ? partial : t, M, K, rank,
+                                                   chunks > 1 ? kXaChunk : K);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || chunks == 1) return static_cast<int>(e);
-    const int mr = M * rank;
-    lora_xa_reduce_kernel<<<(mr + 255) / 256, 256, 0, stream>>>(partial, t, mr, chunks);
+    if (t_op != nullptr) {
+        const int W = (rank + 15) / 16 * 64;
+        lora_xa_reduce_kernel<<<(M * W + 255) / 256, 256, 0, stream>>>(partial, t, M, rank, chunks, row_exp, t_op);
+    } else {
+        lora_xa_reduce_kernel<<<(M * rank + 255) / 256, 256, 0, stream>>>(partial, t, M, rank, chunks, nullptr,
+                                                                          nullptr);
+    }
     return static_cast<int>(cudaGetLastError());
 }
 

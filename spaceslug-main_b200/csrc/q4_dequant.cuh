@@ -47,6 +47,40 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t q, float2 s2) {
     return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
+// Eight weights of one column as four f16 pairs (k, k+1) in f16x2
+// arithmetic: per byte b (nibbles k = 2b, 2b+1), one PRMT puts the byte in
+// both halves, one LOP3 keeps the low nibble in the low half and the high
+// nibble in the high half with the sign bit flipped (u ^ 8 = v + 8) under the
+// f16 exponent of 1024, i.e. (1032 + v0, 1152 + 16 v1); one HFMA2 with
+// (1, 1/16) and (-1032, -72) gives (v0, v1) exactly; one HMUL2 by the group
+// scale s16 (already rounded to f16) gives RN16(v * s16).  16 instructions per
+// word against ~36 for the fp32 path; the scale's f16 rounding adds at most
+// 2^-11 relative error per weight.
+__device__ __forceinline__ uint4 dequant_word_f16x2(uint32_t q, __half2 s2) {
+    const __half2 mul = __halves2half2(__ushort_as_half(0x3C00u), __ushort_as_half(0x2C00u));  // 1, 1/16
+    const __half2 add = __halves2half2(__ushort_as_half(0xE408u), __ushort_as_half(0xD480u));  // -1032, -72
+    uint32_t out[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t both = __byte_perm(q, 0u, 0x4040u | (static_cast<uint32_t>(b) << 8) | static_cast<uint32_t>(b));
+        const uint32_t t = ((both ^ 0x00800008u) & 0x00F0000Fu) | 0x64006400u;
+        const __half2 v = __hfma2(*reinterpret_cast<const __half2*>(&t), mul, add);
+        const __half2 w = __hmul2(v, s2);
+        out[b] = *reinterpret_cast<const uint32_t*>(&w);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// f16 operands take the f16x2 path, bf16 operands the fp32 one.
+template <typename T16>
+__device__ __forceinline__ uint4 dequant_f16x2_or(uint32_t q, float2 s2, __half2 s2h) {
+    if constexpr (std::is_same<T16, __half>::value) {
+        return dequant_word_f16x2(q, s2h);
+    } else {
+        return dequant_word<T16>(q, s2);
+    }
+}
+
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
 
 }  // namespace q4

@@ -18,9 +18,16 @@
 //                 16-bit RN, written straight into the canonical K-major
 //                 128B-swizzled UMMA B tile (packed f32x2 arithmetic);
 //   warps 10..13  epilogue: tcgen05.ld 32 lanes x 16 columns, undo the
-//                 power-of-two operand exponents, add the fused LoRA term
-//                 (alpha/r) * T[m,:] . B[:, n], store fp32 Y; overlaps the
+//                 power-of-two operand exponents, store fp32 Y; overlaps the
 //                 next tile's main loop through the second TMEM buffer.
+//
+// LoRA is ceil(rank/16) more 64-k stages per tile in the same accumulator;
+// stage q covers ranks 16q..16q+15: A = T * 2^e_m as bf16 [hi | lo | hi | 0]
+// (made by the X*A reduction, loaded by TMA like an X tile), B = (alpha/r) *
+// B_lora * 2^f_n as bf16 [hi | hi | lo | 0], built by the dequant warps from
+// fp32 B_lora.  The same power-of-two exponents as the main operands make the
+// epilogue's 2^-(e+f) exact for both; bf16 keeps T * 2^e in range, and
+// hi * hi + lo * hi + hi * lo keeps ~16 bits.
 //
 // With H = 2 every dequantised weight feeds 256 rows of MMA, which keeps the
 // CUDA-core dequant work well under the tensor-core time per k-step.
@@ -74,9 +81,9 @@ struct Cfg {
 template <int H, typename T16>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                   const float* __restrict__ scales, const int* __restrict__ col_exp,
-                   const int* __restrict__ row_exp, float* __restrict__ y, int M, int N, int K,
-                   const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank, float lora_scale,
+                   const __grid_constant__ CUtensorMap tmap_t, const float* __restrict__ scales,
+                   const int* __restrict__ col_exp, const int* __restrict__ row_exp, float* __restrict__ y, int M,
+                   int N, int K, const float* __restrict__ lora_b, int rank, float lora_scale, int lora_stages,
                    int* __restrict__ status) {
     using C = Cfg<H>;
     constexpr int ST = C::kStages;
@@ -104,6 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int NT = (N + kBN - 1) / kBN;
     const int tiles = MT * NT;
     const int KT = (K + kBK - 1) / kBK;
+    const int KS = KT + lora_stages;  // k-steps per tile, the LoRA stages last
     const int G = K / 32;
 
     if (tid == 0) {
@@ -122,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_mbarrier_init();
         tma_prefetch_desc(&tmap_x);
         tma_prefetch_desc(&tmap_w);
+        if (lora_stages) tma_prefetch_desc(&tmap_t);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_holder), C::kTmemCols);
@@ -139,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
                 const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
-                for (int kt = 0; kt < KT; ++kt, ++it) {
+                for (int kt = 0; kt < KS; ++kt, ++it) {
                     const int s = it % ST;
                     const uint32_t ph = (it / ST) & 1u;
                     if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
@@ -147,9 +156,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(full_a(s), C::kABytes);
-                    tma_load_2d(a_s + s * C::kABytes, &tmap_x, full_a(s), kt * kBK, m0);
-                    mbar_arrive_expect_tx(full_r(s), C::kRBytes);
-                    tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
+                    if (kt < KT) {
+                        tma_load_2d(a_s + s * C::kABytes, &tmap_x, full_a(s), kt * kBK, m0);
+                        mbar_arrive_expect_tx(full_r(s), C::kRBytes);
+                        tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
+                    } else {  // LoRA stage: the T operand; no packed weights
+                        tma_load_2d(a_s + s * C::kABytes, &tmap_t, full_a(s), (kt - KT) * kBK, m0);
+                        mbar_arrive(full_r(s));
+                    }
                 }
             }
             if (*abort_flag) {  // let the copies in flight land before exit
@@ -164,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (elect_one()) {
             const uint32_t idesc = umma_idesc_f16(std::is_same<T16, __half>::value ? 0u : 1u, 128u,
                                                   static_cast<uint32_t>(kBN));
+            const uint32_t idesc_lora = umma_idesc_f16(1u, 128u, static_cast<uint32_t>(kBN));  // bf16
             int it = 0, i = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
@@ -172,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(acc_empty(b), (u & 1u) ^ 1u, abort_flag, status, kStatusTimeoutMma)) break;
                 tc_fence_after_sync();
                 const uint32_t d0 = tmem_base + static_cast<uint32_t>(b * H * kBN);
-                for (int kt = 0; kt < KT; ++kt, ++it) {
+                for (int kt = 0; kt < KS; ++kt, ++it) {
                     const int s = it % ST;
                     const uint32_t ph = (it / ST) & 1u;
                     if (!mbar_wait(full_a(s), ph, abort_flag, status, kStatusTimeoutMma) ||
@@ -181,13 +196,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after_sync();
+                    const uint32_t id = kt < KT ? idesc : idesc_lora;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
                         const uint64_t bd = umma_desc_k_sw128(b_s + s * C::kBBytes + kk * 32);
 #pragma unroll
                         for (int h = 0; h < H; ++h) {
                             const uint64_t ad = umma_desc_k_sw128(a_s + s * C::kABytes + h * 16384 + kk * 32);
-                            umma_f16_ss(d0 + static_cast<uint32_t>(h * kBN), ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+                            umma_f16_ss(d0 + static_cast<uint32_t>(h * kBN), ad, bd, id, (kt | kk) != 0 ? 1u : 0u);
                         }
                     }
                     umma_commit(empty(s));
@@ -215,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return (col_ok && g < G) ? __ldg(srow + g) : 0.0f;
             };
             float s0 = scale_at(0), s1 = scale_at(1), s2 = scale_at(2), s3 = scale_at(3);
-            for (int kt = 0; kt < KT; ++kt, ++it) {
+            for (int kt = 0; kt < KS; ++kt, ++it) {
                 const int s = it % ST;
                 const uint32_t ph = (it / ST) & 1u;
                 const float sc = s0;
@@ -227,15 +243,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                const uint4 q = *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
-                const float sv = sc * cs;
-                const float2 s2v = make_float2(sv, sv);
                 uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
-                const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+                if (kt < KT) {
+                    const uint4 q =
+                        *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
+                    const float sv = sc * cs;
+                    const float2 s2v = make_float2(sv, sv);
+                    const __half2 s2h = __float2half2_rn(sv);
+                    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int chunk = (hh * 4 + j) ^ (nl & 7);
-                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_word<T16>(words[j], s2v);
+                    for (int j = 0; j < 4; ++j) {
+                        const int chunk = (hh * 4 + j) ^ (nl & 7);
+                        *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                    }
+                } else {
+                    // LoRA stage q: (alpha/r) * B_lora[16q .. 16q+15, n] * 2^f_n as bf16;
+                    // positions [0,16) hi, [16,32) hi (hh = 0), [32,48) lo, [48,64) 0 (hh = 1)
+                    const int j0 = (kt - KT) * 16;
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2) {
+                        float b0 = 0.0f, b1 = 0.0f;
+                        if (col_ok && j0 + j < rank)
+                            b0 = __ldg(lora_b + static_cast<size_t>(j0 + j) * N + n) * lora_scale * cs;
+                        if (col_ok && j0 + j + 1 < rank)
+                            b1 = __ldg(lora_b + static_cast<size_t>(j0 + j + 1) * N + n) * lora_scale * cs;
+                        const __nv_bfloat162 hi = __floats2bfloat162_rn(b0, b1);
+                        if (hh == 0) {
+                            pk[j / 2] = *reinterpret_cast<const uint32_t*>(&hi);
+                        } else {
+                            const float2 hf = __bfloat1622float2(hi);
+                            const __nv_bfloat162 lo = __floats2bfloat162_rn(b0 - hf.x, b1 - hf.y);
+                            pk[j / 2] = *reinterpret_cast<const uint32_t*>(&lo);
+                        }
+                    }
+                    const uint4 c0 = make_uint4(pk[0], pk[1], pk[2], pk[3]), c1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                    const uint4 v[4] = {c0, c1, hh == 0 ? c0 : z, hh == 0 ? c1 : z};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(brow + (((hh * 4 + j) ^ (nl & 7)) * 16)) = v[j];
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -283,48 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[e] = __uint_as_float(r[e]) * rs * cinv;
                     }
                     if (nb >= N) continue;  // warp-uniform
-                    if (lora_t != nullptr && row_ok) {
-                        // (alpha/r) * T[row, :] . B[:, nb .. nb+15], T row in blocks of 16.  Row
-                        // and column indices are clamped instead of branched on, so every load
-                        // stays in bounds and all of a block's loads can be in flight together.
-                        float d[16];
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) d[e] = 0.0f;
-                        const float* trow = lora_t + static_cast<size_t>(row) * rank;
-                        const bool full16 = nb + 16 <= N && vec_ok;
-                        for (int j0 = 0; j0 < rank; j0 += 16) {
-                            const int jn = min(16, rank - j0);
-                            float tj[16];
-#pragma unroll
-                            for (int jj = 0; jj < 16; ++jj) {
-                                const int j = j0 + jj < rank ? j0 + jj : rank - 1;
-                                tj[jj] = jj < jn ? __ldg(trow + j) : 0.0f;
-                            }
-#pragma unroll
-                            for (int jj = 0; jj < 16; ++jj) {
-                                const int j = j0 + jj < rank ? j0 + jj : rank - 1;
-                                const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
-                                if (full16) {
-#pragma unroll
-                                    for (int e = 0; e < 16; e += 4) {
-                                        const float4 bv = __ldg(reinterpret_cast<const float4*>(brow + e));
-                                        d[e] = fmaf(tj[jj], bv.x, d[e]);
-                                        d[e + 1] = fmaf(tj[jj], bv.y, d[e + 1]);
-                                        d[e + 2] = fmaf(tj[jj], bv.z, d[e + 2]);
-                                        d[e + 3] = fmaf(tj[jj], bv.w, d[e + 3]);
-                                    }
-                                } else {
-#pragma unroll
-                                    for (int e = 0; e < 16; ++e) {
-                                        const int n = nb + e < N ? nb + e : N - 1;
-                                        d[e] = fmaf(tj[jj], __ldg(lora_b + static_cast<size_t>(j) * N + n), d[e]);
-                                    }
-                                }
-                            }
-                        }
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) v[e] = fmaf(lora_scale, d[e], v[e]);
-                    }
                     if (row_ok) {
                         if (vec_ok && nb + 16 <= N) {
 #pragma unroll
@@ -358,8 +362,9 @@ int launch_gemm_t(const GemmArgs& a, int grid, cudaStream_t stream) {
     auto kern = q4_gemm_kernel<H, T16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemAlloc);
     if (e != cudaSuccess) return static_cast<int>(e);
-    kern<<<grid, kThreads, C::kSmemAlloc, stream>>>(a.tmap_x16, a.tmap_w, a.scales, a.col_exp, a.row_exp, a.y, a.M,
-                                                    a.N, a.K, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
+    kern<<<grid, kThreads, C::kSmemAlloc, stream>>>(a.tmap_x16, a.tmap_w, a.tmap_t, a.scales, a.col_exp, a.row_exp,
+                                                    a.y, a.M, a.N, a.K, a.lora_b, a.rank, a.lora_scale,
+                                                    a.lora_stages, a.status);
     return static_cast<int>(cudaGetLastError());
 }
 

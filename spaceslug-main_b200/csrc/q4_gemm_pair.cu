@@ -1,4 +1,6 @@
-// Prefill GEMM on CTA pairs (cta_group::2):  Y = X . dequant(W) (+ LoRA).
+// Prefill GEMM on CTA pairs (cta_group::2):  Y = X . dequant(W).  (With a
+// LoRA term the runtime uses the single-CTA kernel, whose LoRA stages share
+// its accumulator.)
 //
 // Same computation as q4_gemm.cu (the reference's q4gemm.comp:61-175 with
 // w = float(v) * scale, q4gemm.comp:116-122), for large problems.  A cluster
@@ -70,8 +72,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     q4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const float* __restrict__ scales, const int* __restrict__ col_exp,
                         const int* __restrict__ row_exp, float* __restrict__ y, int M, int N, int K,
-                        const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
-                        float lora_scale, int* __restrict__ status) {
+                        int* __restrict__ status) {
     using C = PCfg;
     constexpr int ST = kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -229,12 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint4 q = *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
                 const float sv = sc * cs;
                 const float2 s2v = make_float2(sv, sv);
+                const __half2 s2h = __float2half2_rn(sv);
                 uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
                 const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int chunk = (hh * 4 + j) ^ (nl & 7);
-                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_word<T16>(words[j], s2v);
+                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -279,48 +281,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     v[e] = __uint_as_float(r[e]) * rs * cinv;
                 }
                 if (nb >= N) continue;  // warp-uniform
-                if (lora_t != nullptr && row_ok) {
-                    // (alpha/r) * T[row, :] . B[:, nb .. nb+15], T row in blocks of 16.  Row
-                    // and column indices are clamped instead of branched on, so every load
-                    // stays in bounds and all of a block's loads can be in flight together.
-                    float d[16];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) d[e] = 0.0f;
-                    const float* trow = lora_t + static_cast<size_t>(row) * rank;
-                    const bool full16 = nb + 16 <= N && vec_ok;
-                    for (int j0 = 0; j0 < rank; j0 += 16) {
-                        const int jn = min(16, rank - j0);
-                        float tj[16];
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int j = j0 + jj < rank ? j0 + jj : rank - 1;
-                            tj[jj] = jj < jn ? __ldg(trow + j) : 0.0f;
-                        }
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int j = j0 + jj < rank ? j0 + jj : rank - 1;
-                            const float* brow = lora_b + static_cast<size_t>(j) * N + nb;
-                            if (full16) {
-#pragma unroll
-                                for (int e = 0; e < 16; e += 4) {
-                                    const float4 bv = __ldg(reinterpret_cast<const float4*>(brow + e));
-                                    d[e] = fmaf(tj[jj], bv.x, d[e]);
-                                    d[e + 1] = fmaf(tj[jj], bv.y, d[e + 1]);
-                                    d[e + 2] = fmaf(tj[jj], bv.z, d[e + 2]);
-                                    d[e + 3] = fmaf(tj[jj], bv.w, d[e + 3]);
-                                }
-                            } else {
-#pragma unroll
-                                for (int e = 0; e < 16; ++e) {
-                                    const int n = nb + e < N ? nb + e : N - 1;
-                                    d[e] = fmaf(tj[jj], __ldg(lora_b + static_cast<size_t>(j) * N + n), d[e]);
-                                }
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) v[e] = fmaf(lora_scale, d[e], v[e]);
-                }
                 if (row_ok) {
                     if (vec_ok && nb + 16 <= N) {
 #pragma unroll
@@ -365,7 +325,7 @@ int launch_pair_t(const GemmArgs& a, int pairs, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.scales, a.col_exp, a.row_exp, a.y, a.M, a.N, a.K,
-                           a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
+                           a.status);
     return static_cast<int>(e);
 }
 

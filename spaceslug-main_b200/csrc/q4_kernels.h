@@ -85,6 +85,7 @@ int gemv_max_active_clusters(int M, int K, int cluster_k, int cols_per_cluster);
 struct GemmArgs {
     CUtensorMap tmap_x16;     // [M][K] 16-bit, box 64 x (128 * halves), 128B swizzle
     CUtensorMap tmap_w;       // packed as uint32 [N][K/8], box 8 x 128, no swizzle
+    CUtensorMap tmap_t;       // LoRA-stage A operand, bf16 [M][64*stages], box 64 x (128 * halves), 128B swizzle
     const float* scales;      // [N][K/32]
     const int* col_exp;       // [N] power-of-two exponent applied to the column's scales, or nullptr
     const int* row_exp;       // [M] power-of-two exponent applied to X rows, or nullptr
@@ -97,6 +98,8 @@ struct GemmArgs {
     const float* lora_b;      // [rank][N] fp32
     int rank;
     float lora_scale;
+    int lora_stages;          // single-CTA kernel: ceil(rank/16) bf16 k-stages (0 = no LoRA); the pair kernel
+                              // adds the LoRA term in its epilogue from lora_t
     int* status;              // kernel status word (0 = ok)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
@@ -117,9 +120,12 @@ int launch_dequant(const uint32_t* packed, const float* scales, float* w_kn, int
 int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t stream);
 // T[M][rank] = X[M][K] * A[K][rank] in fp32.  With `partial` (scratch of
 // lora_xa_chunks(K) * M * rank floats) K is split over CTAs and reduced in a
-// second kernel in fixed order; with nullptr one pass per (8 rows, 16 ranks).
+// second kernel in fixed order; with nullptr one pass per (32 rows, 16 ranks).
+// With `partial` and t_op_bits != nullptr, the reduction also writes the GEMM's
+// LoRA-stage operand: bf16 [M][64 * ceil(rank/16)], per 16 ranks a block
+// [hi | lo | hi | 0] of T[m][:] * 2^row_exp[m] (row_exp may be nullptr).
 int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
-                   float* partial = nullptr);
+                   float* partial = nullptr, const int* row_exp = nullptr, uint16_t* t_op_bits = nullptr);
 int lora_xa_chunks(int K);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,

@@ -269,7 +269,9 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     Scratch t_part(p.rank > 0 ? static_cast<size_t>(q4::lora_xa_chunks(p.K)) * p.M * p.rank * sizeof(float) : 0,
                    stream);
     float* lora_t = static_cast<float*>(t_buf.p);
-    if (p.rank > 0)
+    // The decode kernels add (alpha/r) * T * B in their epilogue from fp32 T;
+    // the GEMM computes T after the X cast (it needs the row exponents).
+    if (p.rank > 0 && p.M <= 8)
         check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
                                         static_cast<float*>(t_part.p)),
                      "lora_xa");
@@ -370,7 +372,9 @@ void run_problem(const Problem& p, cudaStream_t stream) {
         pairs = mp;
     }
     const int variant = g_gemm_variant.load();
-    const bool use_pair = pairs > 0 && (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
+    // LoRA runs as extra bf16 k-stages of the single-CTA kernel
+    const bool use_pair = p.rank == 0 && pairs > 0 &&
+                          (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
     g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
     g.sm_count = c.sm_count;
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
@@ -380,8 +384,24 @@ void run_problem(const Problem& p, cudaStream_t stream) {
               static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
     g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
-    g.lora_t = lora_t; g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
+    g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
     g.status = c.status;
+    const int lstages = (p.rank + 15) / 16;
+    Scratch t_op(lstages > 0 ? static_cast<size_t>(p.M) * lstages * 64 * 2 : 0, stream);
+    if (p.rank > 0) {
+        // T = X * A and its bf16 [hi | lo | hi | 0] operand scaled by the row exponents
+        check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
+                                        static_cast<float*>(t_part.p), row_exp, static_cast<uint16_t*>(t_op.p)),
+                     "lora_xa");
+        encode_2d(&g.tmap_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, t_op.p, static_cast<uint64_t>(lstages) * 64,
+                  static_cast<uint64_t>(p.M), static_cast<uint64_t>(lstages) * 128, 64,
+                  static_cast<uint32_t>(128 * g.halves), CU_TENSOR_MAP_SWIZZLE_128B);
+        g.lora_t = lora_t;
+        g.lora_stages = use_pair ? 0 : lstages;
+    } else {
+        g.tmap_t = g.tmap_x16;  // never read
+        g.lora_stages = 0;
+    }
     if (use_pair)
         check_launch(q4::launch_gemm_pair(g, pairs, stream), "gemm (CTA pair) launch");
     else
