@@ -30,11 +30,13 @@
 // each bounded (status word + abort flag).
 #include <cooperative_groups.h>
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 #include "common.cuh"
+#include "q4_dequant.cuh"
 #include "q4_kernels.h"
 
 namespace cg = cooperative_groups;
@@ -47,15 +49,21 @@ constexpr int kTSlot = 32;       // rows (columns of W) per shared-memory box sl
 constexpr int kTBoxK = 256;      // k per weight box: one 128-byte row (32 words) per column
 constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row per column
 
-// Warps per CTA: 16 for M <= 6 (latency hiding; at M <= 2 within 64
-// registers, so two CTAs share an SM), 8 above.
+// 16 warps per CTA (latency hiding; at M <= 2 within 64 registers, so two
+// CTAs share an SM).
 template <int M>
 struct TileCfg {
-    static constexpr int kWarps = M <= 6 ? 16 : 8;
+    // M >= 7 multiplies on the tensor cores with mma.sync (see below): its
+    // cost does not grow with M, but every CTA first converts all of X into
+    // f16 hi/lo planes (~3.8 us at M = 8), so it only breaks even with the
+    // fp32 path (M FMAs per weight) at M = 8 and loses at M = 4.
+    static constexpr bool kMma = M >= 7;
+    static constexpr int kWarps = 16;
     static constexpr int kThreads = kWarps * 32;
 };
 
-__host__ __device__ inline int tile_warps(int M) { return M <= 6 ? 16 : 8; }
+__host__ __device__ inline int tile_warps(int) { return 16; }
+constexpr int kMmaMaxChunksPerThread = 8;  // X conversion: M * kslice / 8 chunks over 512 threads
 
 struct TileLayout {
     int kslice, nbox, nsbox;
@@ -77,7 +85,8 @@ __host__ __device__ inline TileLayout tile_layout(int M, int K, int S) {
     L.cpart_off = L.x_off + L.x_bytes;                 // [M][32] fp32 (the CTA's K-slice sum)
     L.bar_off = L.cpart_off + kTSlot * M * 4;
     L.misc_off = L.bar_off + (L.nbox + 2) * 8;         // wfull[nbox], sfull, xfull
-    L.bytes = L.misc_off + 16;                         // abort flag
+    // abort flag; then (mma path) row-max scratch [16 warps][8] and row exponents [8]
+    L.bytes = L.misc_off + 16 + 16 * 8 * 4 + 8 * 4;
     return L;
 }
 
@@ -214,106 +223,279 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
             tma_load_2d(base + L.x_off + m * L.kslice * 4, &tmap_x, xfull, 0, m * rows_per_m + k0 / kTBoxK);
     }
 
-    // ------------------------------------------------------------ compute --
-    // Lane (cq, j) handles slot rows cq + 8r (r < 4) and word j of each group;
-    // rows >= C (C < 32) hold no column and their sums are never read.  All
-    // four rows of a lane share row & 7 = cq, so in the 128-byte swizzle the
-    // 16-byte chunk of group t is t ^ cq for every r: one LOP3 per group
-    // addresses the four words (and another the four scales), and the eight
-    // lanes cq of a quarter warp hit distinct bank quads.
-    const int cq = lane >> 2, j = lane & 3;
-    const uint32_t cq16 = static_cast<uint32_t>(cq) << 4;
-    float2 acc[4][M];
+    if constexpr (TileCfg<M>::kMma) {
+        // ---------------------------------------------- compute (mma path) --
+        // Warp-level tensor-core MMA (mma.sync m16n8k16, f16 in, fp32
+        // accumulate), issued from registers: no TMEM, no commits.
+        //   A (16 x 16): rows 0-7 = x_hi of rows 0-7, rows 8-15 = x_lo, with
+        //   x * 2^e_m = x_hi + x_lo (f16, e_m per row and K slice);
+        //   B (16 x 8): 8 weight columns, the int4 values v as f16 (exact);
+        //   D[g][n] + D[g + 8][n] = 2^e_g * sum_k x[g][k] v[k][n] over 16 k.
+        // Two MMAs per 32-k scale group into a fresh D, then y += s(n, g) * D
+        // in fp32.  The thread of lane (g = lane / 4, q = lane % 4) owns x-row g
+        // and columns 8o + 2q, 8o + 2q + 1 of each column octet o.
+        bool ok = mbar_wait(sfull, 0u, abort_flag, status, kStatusTimeoutGemv) &&
+                  mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
+        float* rmax = reinterpret_cast<float*>(smem + L.misc_off + 16);             // [16 warps][8]
+        int* rexp = reinterpret_cast<int*>(smem + L.misc_off + 16 + 16 * 8 * 4);    // [8]
+        // X -> per-row exponents and f16 hi/lo planes, in place: chunks of 8 k
+        // are read into registers, the CTA syncs, and the planes are written
+        // with chunk c of row m at position c ^ (m & 7) (conflict-free reads).
+        const int cpr = L.kslice / 8;  // chunks per row
+        const int nch = M * cpr;
+        float xv[kMmaMaxChunksPerThread][8];
+        float mx[8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+        for (int m = 0; m < 8; ++m) mx[m] = 0.0f;
+        const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
 #pragma unroll
-        for (int m = 0; m < M; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
-
-    bool ok = mbar_wait(sfull, 0u, abort_flag, status, kStatusTimeoutGemv) &&
-              mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
-    const uint32_t xs = base + L.x_off + j * 32;  // this lane's 8 x of word j in a group
-#pragma unroll 1
-    for (int b = warp; b < L.nbox && ok; b += kWarps) {
-        if (!mbar_wait(wfull(b), 0u, abort_flag, status, kStatusTimeoutGemv)) {
-            ok = false;
-            break;
+        for (int i = 0; i < kMmaMaxChunksPerThread; ++i) {
+            const int ch = tid + i * kThreads;
+            if (ch < nch && ok) {
+                const float4 a = *reinterpret_cast<const float4*>(xf + ch * 8);
+                const float4 b = *reinterpret_cast<const float4*>(xf + ch * 8 + 4);
+                xv[i][0] = a.x; xv[i][1] = a.y; xv[i][2] = a.z; xv[i][3] = a.w;
+                xv[i][4] = b.x; xv[i][5] = b.y; xv[i][6] = b.z; xv[i][7] = b.w;
+                float cm = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) cm = fmaxf(cm, fabsf(xv[i][e]));
+                const int m = ch / cpr;
+#pragma unroll
+                for (int mm = 0; mm < 8; ++mm) mx[mm] = (mm == m) ? fmaxf(mx[mm], cm) : mx[mm];
+            }
         }
-        // bits 4-6 of both bases are zero, so "| chunk << 4" places the chunk
-        const uint32_t wrow = base + L.w_off + b * kTSlot * 128 + cq * 128 + j * 4;
-        const uint32_t srow = base + L.s_off + (b >> 2) * kTSlot * 128 + cq * 128;
-        const uint32_t sx = (static_cast<uint32_t>((b & 3) * 2) << 4) ^ cq16;  // scale chunk of group 0, swizzled
-        const uint32_t xrow = xs + b * kTBoxK * 4;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const uint32_t wa = wrow | ((static_cast<uint32_t>(t) << 4) ^ cq16);
-            const uint32_t sa = (srow | (sx ^ (static_cast<uint32_t>(t >> 2) << 4))) + (t & 3) * 4;
-            if constexpr (M <= 2) {
-                float2 xv[M][4];
+        for (int m = 0; m < 8; ++m) {
 #pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
-                    const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
-                    xv[m][0] = make_float2(xa.x, xa.y);
-                    xv[m][1] = make_float2(xa.z, xa.w);
-                    xv[m][2] = make_float2(xc.x, xc.y);
-                    xv[m][3] = make_float2(xc.z, xc.w);
+            for (int off = 16; off > 0; off >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], off));
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) rmax[warp * 8 + m] = mx[m];
+        }
+        __syncthreads();  // every chunk is in registers; every warp's row maxima are out
+        if (tid < 8) {
+            float v = 0.0f;
+            for (int w16 = 0; w16 < kWarps; ++w16) v = fmaxf(v, rmax[w16 * 8 + tid]);
+            int e = 0;
+            if (v > 0.0f && isfinite(v)) {
+                int e2;
+                frexpf(v, &e2);
+                e = 14 - e2;  // max|x| * 2^e in [2^13, 2^14)
+                e = e < -60 ? -60 : (e > 60 ? 60 : e);
+            }
+            rexp[tid] = e;
+        }
+        __syncthreads();
+        const uint32_t hi_plane = base + L.x_off, lo_plane = hi_plane + M * L.kslice * 2;
+#pragma unroll
+        for (int i = 0; i < kMmaMaxChunksPerThread; ++i) {
+            const int ch = tid + i * kThreads;
+            if (ch < nch && ok) {
+                const int m = ch / cpr, c = ch % cpr;
+                const float sc = exp2i(rexp[m]);
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a0 = xv[i][2 * e] * sc, a1 = xv[i][2 * e + 1] * sc;
+                    const __half2 hh = __floats2half2_rn(a0, a1);
+                    const float2 hf = __half22float2(hh);
+                    const __half2 ll = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+                    hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
+                    lw[e] = *reinterpret_cast<const uint32_t*>(&ll);
+                }
+                const uint32_t pos = static_cast<uint32_t>(m * cpr + (c ^ (m & 7))) * 16;
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(hi_plane + pos), "r"(hw[0]), "r"(hw[1]),
+                             "r"(hw[2]), "r"(hw[3]) : "memory");
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(lo_plane + pos), "r"(lw[0]), "r"(lw[1]),
+                             "r"(lw[2]), "r"(lw[3]) : "memory");
+            }
+        }
+        __syncthreads();
+
+        const int g = lane >> 2, q = lane & 3;
+        const int mrow = g < M ? g : M - 1;  // A rows past M repeat a row; their D rows are never stored
+        // plain C++ loads (ordered after the mbarrier waits, free to be scheduled)
+        const uint8_t* hi_row = smem + L.x_off + mrow * L.kslice * 2 + q * 4;
+        const uint8_t* lo_row = hi_row + M * L.kslice * 2;
+        const uint32_t msw = static_cast<uint32_t>(mrow & 7);
+        const uint32_t bsel = 0x4040u | (static_cast<uint32_t>(q) << 8) | static_cast<uint32_t>(q);  // byte q, twice
+        const __half2 vmul = __halves2half2(__ushort_as_half(0x3C00u), __ushort_as_half(0x2C00u));  // 1, 1/16
+        const __half2 vadd = __halves2half2(__ushort_as_half(0xE408u), __ushort_as_half(0xD480u));  // -1032, -72
+        float accm[4][2];
+#pragma unroll
+        for (int o = 0; o < 4; ++o) accm[o][0] = accm[o][1] = 0.0f;
+#pragma unroll 1
+        for (int b = warp; b < L.nbox && ok; b += kWarps) {
+            if (!mbar_wait(wfull(b), 0u, abort_flag, status, kStatusTimeoutGemv)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* wcol = smem + L.w_off + b * kTSlot * 128 + g * 128;  // column 8o + g at + o * 1024
+            const uint8_t* sbx = smem + L.s_off + (b >> 2) * kTSlot * 128;
+            const int schunk0 = (b & 3) * 2;
+#pragma unroll 2
+            for (int t = 0; t < 8; ++t) {
+                // A fragments of this 32-k group: chunks c0 .. c0 + 3 of the row
+                const uint32_t c0 = static_cast<uint32_t>(b * 32 + t * 4);
+                uint32_t a[2][4];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t ca = ((c0 + 2 * h) ^ msw) << 4, cb = ((c0 + 2 * h + 1) ^ msw) << 4;
+                    a[h][0] = *reinterpret_cast<const uint32_t*>(hi_row + ca);
+                    a[h][1] = *reinterpret_cast<const uint32_t*>(lo_row + ca);
+                    a[h][2] = *reinterpret_cast<const uint32_t*>(hi_row + cb);
+                    a[h][3] = *reinterpret_cast<const uint32_t*>(lo_row + cb);
                 }
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const uint32_t q = lds_u32(wa + r * 8 * 128);
-                    const float s = __uint_as_float(lds_u32(sa + r * 8 * 128));
-                    // per-word partial sum of v * x, scaled once (fewer fp32 ops)
-                    float2 v[4];
-                    unpack_word_f32(q, v);
+                for (int o = 0; o < 4; ++o) {
+                    // column 8o + g: its 16-byte word of group t (swizzle key g)
+                    const uint4 wq = *reinterpret_cast<const uint4*>(
+                        wcol + o * 1024 + ((static_cast<uint32_t>(t) ^ static_cast<uint32_t>(g)) << 4));
+                    const uint32_t words[4] = {wq.x, wq.y, wq.z, wq.w};
+                    uint32_t bf[4];
 #pragma unroll
-                    for (int m = 0; m < M; ++m) {
-                        float2 p = __fmul2_rn(v[0], xv[m][0]);
-                        p = __ffma2_rn(v[1], xv[m][1], p);
-                        p = __ffma2_rn(v[2], xv[m][2], p);
-                        p = __ffma2_rn(v[3], xv[m][3], p);
-                        acc[r][m].x = fmaf(s, p.x + p.y, acc[r][m].x);
+                    for (int w = 0; w < 4; ++w) {
+                        // byte q of word w: nibbles k = 8w + 2q, 8w + 2q + 1 -> f16 pair (exact)
+                        const uint32_t both = __byte_perm(words[w], 0u, bsel);
+                        const uint32_t tt = ((both ^ 0x00800008u) & 0x00F0000Fu) | 0x64006400u;
+                        const __half2 v = __hfma2(*reinterpret_cast<const __half2*>(&tt), vmul, vadd);
+                        bf[w] = *reinterpret_cast<const uint32_t*>(&v);
                     }
-                }
-            } else {
-                // the four columns' scaled weights first, then X one row at a
-                // time: 32 + 8 live registers besides the accumulators
-                float2 w[4][4];
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    dequant_word_f32(lds_u32(wa + r * 8 * 128), __uint_as_float(lds_u32(sa + r * 8 * 128)), w[r]);
+                    for (int h = 0; h < 2; ++h) {
+                        asm(
+                            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+                            "{%8,%9}, {%0,%1,%2,%3};"
+                            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                            : "r"(a[h][0]), "r"(a[h][1]), "r"(a[h][2]), "r"(a[h][3]), "r"(bf[2 * h]), "r"(bf[2 * h + 1]));
+                    }
+                    // scales of columns 8o + 2q and 8o + 2q + 1 (swizzle key 2q + e)
 #pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
-                    const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
-                    const float2 x0 = make_float2(xa.x, xa.y), x1 = make_float2(xa.z, xa.w);
-                    const float2 x2 = make_float2(xc.x, xc.y), x3 = make_float2(xc.z, xc.w);
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        acc[r][m] = __ffma2_rn(w[r][0], x0, acc[r][m]);
-                        acc[r][m] = __ffma2_rn(w[r][1], x1, acc[r][m]);
-                        acc[r][m] = __ffma2_rn(w[r][2], x2, acc[r][m]);
-                        acc[r][m] = __ffma2_rn(w[r][3], x3, acc[r][m]);
+                    for (int e = 0; e < 2; ++e) {
+                        const uint32_t cc = static_cast<uint32_t>(o * 8 + 2 * q + e);
+                        const float sv = *reinterpret_cast<const float*>(
+                            sbx + cc * 128 + (((static_cast<uint32_t>(schunk0 + (t >> 2))) ^ (cc & 7u)) << 4) + (t & 3) * 4);
+                        accm[o][e] = fmaf(sv, d[e] + d[2 + e], accm[o][e]);
                     }
                 }
             }
         }
-    }
-
-    // ------------------------------------------------------------- reduce --
-    __syncthreads();  // every warp is done with X: its region takes the partials
-    float* part = reinterpret_cast<float*>(smem + L.part_off);  // [warp][M][col]
+        // ------------------------------------------------------------- reduce --
+        __syncthreads();  // every warp is done with X: its region takes the partials
+        float* part = reinterpret_cast<float*>(smem + L.part_off);  // [warp][M][col]
+        if (g < M) {
+            const float unscale = exp2i(-rexp[g]);
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+            for (int o = 0; o < 4; ++o)
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-            float v = acc[r][m].x + acc[r][m].y;
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            if (j == 0) part[(warp * M + m) * kTSlot + cq + 8 * r] = v;
+                for (int e = 0; e < 2; ++e) part[(warp * M + g) * kTSlot + o * 8 + 2 * q + e] = accm[o][e] * unscale;
         }
-    }
-    __syncthreads();
+        __syncthreads();
+    } else {
+        // ------------------------------------------------- compute (fp32 path) --
+        // Lane (cq, j) handles slot rows cq + 8r (r < 4) and word j of each group;
+        // rows >= C (C < 32) hold no column and their sums are never read.  All
+        // four rows of a lane share row & 7 = cq, so in the 128-byte swizzle the
+        // 16-byte chunk of group t is t ^ cq for every r: one LOP3 per group
+        // addresses the four words (and another the four scales), and the eight
+        // lanes cq of a quarter warp hit distinct bank quads.
+        const int cq = lane >> 2, j = lane & 3;
+        const uint32_t cq16 = static_cast<uint32_t>(cq) << 4;
+        float2 acc[4][M];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
 
+        bool ok = mbar_wait(sfull, 0u, abort_flag, status, kStatusTimeoutGemv) &&
+                  mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
+        const uint32_t xs = base + L.x_off + j * 32;  // this lane's 8 x of word j in a group
+#pragma unroll 1
+        for (int b = warp; b < L.nbox && ok; b += kWarps) {
+            if (!mbar_wait(wfull(b), 0u, abort_flag, status, kStatusTimeoutGemv)) {
+                ok = false;
+                break;
+            }
+            // bits 4-6 of both bases are zero, so "| chunk << 4" places the chunk
+            const uint32_t wrow = base + L.w_off + b * kTSlot * 128 + cq * 128 + j * 4;
+            const uint32_t srow = base + L.s_off + (b >> 2) * kTSlot * 128 + cq * 128;
+            const uint32_t sx = (static_cast<uint32_t>((b & 3) * 2) << 4) ^ cq16;  // scale chunk of group 0, swizzled
+            const uint32_t xrow = xs + b * kTBoxK * 4;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const uint32_t wa = wrow | ((static_cast<uint32_t>(t) << 4) ^ cq16);
+                const uint32_t sa = (srow | (sx ^ (static_cast<uint32_t>(t >> 2) << 4))) + (t & 3) * 4;
+                if constexpr (M <= 2) {
+                    float2 xv[M][4];
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
+                        const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
+                        xv[m][0] = make_float2(xa.x, xa.y);
+                        xv[m][1] = make_float2(xa.z, xa.w);
+                        xv[m][2] = make_float2(xc.x, xc.y);
+                        xv[m][3] = make_float2(xc.z, xc.w);
+                    }
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const uint32_t q = lds_u32(wa + r * 8 * 128);
+                        const float s = __uint_as_float(lds_u32(sa + r * 8 * 128));
+                        // per-word partial sum of v * x, scaled once (fewer fp32 ops)
+                        float2 v[4];
+                        unpack_word_f32(q, v);
+#pragma unroll
+                        for (int m = 0; m < M; ++m) {
+                            float2 p = __fmul2_rn(v[0], xv[m][0]);
+                            p = __ffma2_rn(v[1], xv[m][1], p);
+                            p = __ffma2_rn(v[2], xv[m][2], p);
+                            p = __ffma2_rn(v[3], xv[m][3], p);
+                            acc[r][m].x = fmaf(s, p.x + p.y, acc[r][m].x);
+                        }
+                    }
+                } else {
+                    // the four columns' scaled weights first, then X one row at a
+                    // time: 32 + 8 live registers besides the accumulators
+                    float2 w[4][4];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r)
+                        dequant_word_f32(lds_u32(wa + r * 8 * 128), __uint_as_float(lds_u32(sa + r * 8 * 128)), w[r]);
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        const float4 xa = lds_f4(xrow + m * L.kslice * 4 + t * 128);
+                        const float4 xc = lds_f4(xrow + m * L.kslice * 4 + t * 128 + 16);
+                        const float2 x0 = make_float2(xa.x, xa.y), x1 = make_float2(xa.z, xa.w);
+                        const float2 x2 = make_float2(xc.x, xc.y), x3 = make_float2(xc.z, xc.w);
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            acc[r][m] = __ffma2_rn(w[r][0], x0, acc[r][m]);
+                            acc[r][m] = __ffma2_rn(w[r][1], x1, acc[r][m]);
+                            acc[r][m] = __ffma2_rn(w[r][2], x2, acc[r][m]);
+                            acc[r][m] = __ffma2_rn(w[r][3], x3, acc[r][m]);
+                        }
+                    }
+                }
+            }
+        }
+
+        // ------------------------------------------------------------- reduce --
+        __syncthreads();  // every warp is done with X: its region takes the partials
+        float* part = reinterpret_cast<float*>(smem + L.part_off);  // [warp][M][col]
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float v = acc[r][m].x + acc[r][m].y;
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                if (j == 0) part[(warp * M + m) * kTSlot + cq + 8 * r] = v;
+            }
+        }
+        __syncthreads();
+    }
+
+    const float* part = reinterpret_cast<const float*>(smem + L.part_off);  // [warp][M][col]
     float* cpart = reinterpret_cast<float*>(smem + L.cpart_off);  // [M][32]
     for (int idx = tid; idx < kTSlot * M; idx += kThreads) {
         float sum = 0.0f;
@@ -393,6 +575,8 @@ size_t gemv_tile_smem_bytes(int M, int K, int S) { return static_cast<size_t>(ti
 bool gemv_tile_supported(int M, int K, int S) {
     if (M < 1 || M > 8 || S < 1 || S > 8 || (S & (S - 1)) != 0) return false;
     if (K <= 0 || K % (kTBoxK * S) != 0) return false;
+    // the mma path (M >= 7) converts X with at most 8 chunks of 8 k per thread
+    if (M >= 7 && static_cast<long long>(M) * (K / S) > 8LL * kMmaMaxChunksPerThread * 512) return false;
     return gemv_tile_smem_bytes(M, K, S) <= 227 * 1024;
 }
 
