@@ -50,6 +50,8 @@ template <typename T16>
 __global__ void __launch_bounds__(256) cast_x_kernel(const float* __restrict__ x, T16* __restrict__ x16,
                                                      int* __restrict__ row_exp, int K) {
     __shared__ float red[32];
+    // the GEMM that follows may start its prologue (weight loads, dequant)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int m = blockIdx.x;
     const float* row = x + static_cast<size_t>(m) * K;
     float scale = 1.0f;

@@ -146,6 +146,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int it = 0;
             bool ok = true;
+            // The packed weights do not depend on the previous launch (the X
+            // cast, the X*A projection): the first tile's first ST raw stages
+            // go out before griddepcontrol.wait.
+            int pre = 0;
+            if (static_cast<int>(blockIdx.x) < tiles) {
+                const int n00 = (static_cast<int>(blockIdx.x) / MT) * kBN;
+                pre = KT < ST ? KT : ST;
+                for (int kt = 0; kt < pre; ++kt) {
+                    mbar_arrive_expect_tx(full_r(kt), C::kRBytes);
+                    tma_load_2d(r_s + kt * C::kRBytes, &tmap_w, full_r(kt), kt * (kBK / 8), n00);
+                }
+            }
+            pdl_wait();
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
                 const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
                 for (int kt = 0; kt < KS; ++kt, ++it) {
@@ -158,8 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(full_a(s), C::kABytes);
                     if (kt < KT) {
                         tma_load_2d(a_s + s * C::kABytes, &tmap_x, full_a(s), kt * kBK, m0);
-                        mbar_arrive_expect_tx(full_r(s), C::kRBytes);
-                        tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
+                        if (it >= pre) {
+                            mbar_arrive_expect_tx(full_r(s), C::kRBytes);
+                            tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
+                        }
                     } else {  // LoRA stage: the T operand; no packed weights
                         tma_load_2d(a_s + s * C::kABytes, &tmap_t, full_a(s), (kt - KT) * kBK, m0);
                         mbar_arrive(full_r(s));
@@ -290,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------ epilogue --
+        pdl_wait();  // row exponents and Y belong to the previous launch until it completes
         const int quarter = warp & 3;
         const bool vec_ok = (N % 4) == 0;
         int i = 0;
@@ -362,10 +378,19 @@ int launch_gemm_t(const GemmArgs& a, int grid, cudaStream_t stream) {
     auto kern = q4_gemm_kernel<H, T16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemAlloc);
     if (e != cudaSuccess) return static_cast<int>(e);
-    kern<<<grid, kThreads, C::kSmemAlloc, stream>>>(a.tmap_x16, a.tmap_w, a.tmap_t, a.scales, a.col_exp, a.row_exp,
-                                                    a.y, a.M, a.N, a.K, a.lora_b, a.rank, a.lora_scale,
-                                                    a.lora_stages, a.status);
-    return static_cast<int>(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemAlloc;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap the X cast's tail
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.tmap_t, a.scales, a.col_exp, a.row_exp, a.y, a.M, a.N,
+                           a.K, a.lora_b, a.rank, a.lora_scale, a.lora_stages, a.status);
+    return static_cast<int>(e);
 }
 
 }  // namespace

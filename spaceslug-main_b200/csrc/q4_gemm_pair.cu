@@ -137,6 +137,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int it = 0;
             bool ok = true;
+            // The packed weights do not depend on the previous launch (the X
+            // cast): the first tile's first ST raw stages go out before
+            // griddepcontrol.wait, and the dequant warps start on them.
+            int pre = 0;
+            if (pair < tiles) {
+                const int nb0 = (pair / MT) * kPairCols + static_cast<int>(crank) * kHalf;
+                pre = KT < ST ? KT : ST;
+                for (int kt = 0; kt < pre; ++kt) {
+                    mbar_arrive_expect_tx(full_r(kt), C::kRBytes);
+                    tma_load_2d(r_s + kt * C::kRBytes, &tmap_w, full_r(kt), kt * (kBK / 8), nb0);
+                }
+            }
+            pdl_wait();
             for (int t = pair; t < tiles && ok; t += npairs) {
                 const int m0 = (t % MT) * kPairRows + static_cast<int>(crank) * kHalf;
                 const int nb = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf;
@@ -149,8 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (leader) mbar_arrive_expect_tx(full_a(s), 2u * C::kABytes);
                     tma_load_2d_pair(a_s + s * C::kABytes, &tmap_x, leader_addr(full_a(s)), kt * kBK, m0);
-                    mbar_arrive_expect_tx(full_r(s), C::kRBytes);
-                    tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), nb);
+                    if (it >= pre) {
+                        mbar_arrive_expect_tx(full_r(s), C::kRBytes);
+                        tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), nb);
+                    }
                 }
             }
             if (*abort_flag) {  // let this CTA's copies in flight land before exit
@@ -245,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------ epilogue --
+        pdl_wait();  // row exponents and Y belong to the previous launch until it completes
         const int quarter = warp & 3;
         const bool vec_ok = (N % 4) == 0;
         int i = 0;
@@ -317,13 +333,15 @@ int launch_pair_t(const GemmArgs& a, int pairs, cudaStream_t stream) {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = PCfg::kSmemAlloc;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap the X cast's tail
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.scales, a.col_exp, a.row_exp, a.y, a.M, a.N, a.K,
                            a.status);
     return static_cast<int>(e);
