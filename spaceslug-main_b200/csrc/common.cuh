@@ -224,6 +224,15 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
                  : "memory");
 }
+// One commit whose arrival goes to the mbarrier at the same shared-memory
+// offset `bar` (a local address) in every CTA of `cta_mask` (an MMA
+// completion signal, not a data copy).
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"(cta_mask)
+        : "memory");
+}
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f16 (A, B both f16 or both
 // bf16, selected by the instruction descriptor), fp32 accumulate.

@@ -7,22 +7,29 @@
 // of two CTAs on two SMs owns a 256 x 256 output tile:
 //
 //   * each CTA TMA-loads its own 128 rows of the 16-bit X tile and its own
-//     128 columns of packed W per 64-wide k-step, and dequantises those 128
+//     128 columns of packed W per 128-wide k-stage, and dequantises those 128
 //     columns into its own shared memory; the X loads count their bytes on
 //     the leader CTA's barrier, the dequant warps of both CTAs arrive on the
 //     leader's barrier;
 //   * the leader issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16): A rows
 //     and B columns are split between the two CTAs' shared memory at the
 //     same offsets, each CTA's TMEM receives its 128 rows x 256 columns;
-//   * each MMA stage is committed to both CTAs' empty barriers, each finished
-//     accumulator to both CTAs' epilogues (two commits, one per CTA);
+//   * one commit per stage arrives on the empty barriers of both CTAs, one per
+//     tile on both epilogues' accumulator barriers (a commit costs the MMA
+//     thread about as much as four MMAs, so stages are 128 k: 8 MMAs each);
 //   * both CTAs run their epilogue on their own TMEM (double-buffered: 2 x 256
 //     columns) while the pair computes the next tile.
 //
-// Per SM and k-step this moves 20 KB from L2 (16 KB X + 4 KB W) for 128 x 256
-// x 64 MACs: half the bytes per FLOP of the single-CTA 256 x 128 tile, and
-// each dequantised weight still feeds 256 rows.  Every load lands only in the
-// CTA that issued it.
+// A stage is two 64-k sub-blocks in the canonical 128-byte-swizzled K-major
+// layout (16 KB each for X and for the dequantised W).  Its packed W (128
+// columns x 64 B) arrives 64-byte swizzled, so that the dequant warps' 16-byte
+// loads (8 columns per quarter-warp) and their 16-byte stores into the
+// 128-byte-swizzled operand are free of bank conflicts.
+//
+// Per SM and 128-k stage this moves 40 KB from L2 (32 KB X + 8 KB W) for
+// 128 x 256 x 128 MACs: half the bytes per FLOP of the single-CTA 256 x 128
+// tile, and each dequantised weight still feeds 256 rows.  Every load lands
+// only in the CTA that issued it.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -42,17 +49,19 @@ namespace {
 constexpr int kPairRows = 256;  // tile rows of the pair (128 per CTA)
 constexpr int kPairCols = 256;  // tile columns (128 dequantised per CTA)
 constexpr int kHalf = 128;
-constexpr int kBK = 64;
-constexpr int kStages = 6;
+constexpr int kBK = 128;        // k per stage (two 64-k sub-blocks)
+constexpr int kSub = 64;
+constexpr int kStages = 3;
 constexpr int kThreads = 448;   // 14 warps
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarp0 = 10;
 constexpr int kEpiWarps = 4;
 
 struct PCfg {
-    static constexpr int kABytes = kHalf * kBK * 2;  // 16 KB: this CTA's 128 rows of X
-    static constexpr int kBBytes = kHalf * kBK * 2;  // 16 KB: this CTA's 128 dequantised columns
-    static constexpr int kRBytes = kHalf * kBK / 2;  // 4 KB: their packed nibbles
+    static constexpr int kSubBytes = kHalf * kSub * 2;  // 16 KB: one 64-k sub-block of 128 rows
+    static constexpr int kABytes = 2 * kSubBytes;       // 32 KB: this CTA's 128 rows of X
+    static constexpr int kBBytes = 2 * kSubBytes;       // 32 KB: this CTA's 128 dequantised columns
+    static constexpr int kRBytes = kHalf * kBK / 2;     // 8 KB: their packed nibbles (64 B per column)
     static constexpr int kAOff = 0;
     static constexpr int kBOff = kAOff + kStages * kABytes;
     static constexpr int kROff = kBOff + kStages * kBBytes;
@@ -161,7 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     if (leader) mbar_arrive_expect_tx(full_a(s), 2u * C::kABytes);
-                    tma_load_2d_pair(a_s + s * C::kABytes, &tmap_x, leader_addr(full_a(s)), kt * kBK, m0);
+                    const uint32_t fa = leader_addr(full_a(s));
+                    tma_load_2d_pair(a_s + s * C::kABytes, &tmap_x, fa, kt * kBK, m0);
+                    tma_load_2d_pair(a_s + s * C::kABytes + C::kSubBytes, &tmap_x, fa, kt * kBK + kSub, m0);
                     if (it >= pre) {
                         mbar_arrive_expect_tx(full_r(s), C::kRBytes);
                         tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), nb);
@@ -199,25 +210,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after_sync();
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
-                        const uint64_t ad = umma_desc_k_sw128(a_s + s * C::kABytes + kk * 32);
-                        const uint64_t bd = umma_desc_k_sw128(b_s + s * C::kBBytes + kk * 32);
+                        const uint32_t off = static_cast<uint32_t>((kk >> 2) * C::kSubBytes + (kk & 3) * 32);
+                        const uint64_t ad = umma_desc_k_sw128(a_s + s * C::kABytes + off);
+                        const uint64_t bd = umma_desc_k_sw128(b_s + s * C::kBBytes + off);
                         umma_f16_ss_pair(d0, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
                     }
-                    umma_commit_pair(mapa_shared(empty(s), 0));
-                    umma_commit_pair(mapa_shared(empty(s), 1));
+                    umma_commit_pair_both(empty(s), 0x3);
                 }
-                if (ok) {
-                    umma_commit_pair(mapa_shared(acc_full(b), 0));
-                    umma_commit_pair(mapa_shared(acc_full(b), 1));
-                }
+                if (ok) umma_commit_pair_both(acc_full(b), 0x3);
             }
             umma_commit_pair(mapa_shared(done_bar, 0));  // tracks every MMA issued above
             mbar_drain(done_bar, 0u);
         }
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------- dequant --
-        const int dt = tid - 64;
-        const int nl = dt >> 1, hh = dt & 1;  // unit: column nl of this CTA's half, group half hh
+        // Lane l of dequant warp w: column nl = 16 w + (l & 15) of this CTA's
+        // half, k-half hh = l >> 4 of each stage (groups 2 hh and 2 hh + 1,
+        // operand sub-block hh).  A quarter-warp then covers 8 columns of one
+        // k-half: its 16-byte raw loads hit 8 distinct bank groups through the
+        // 64-byte swizzle, its stores through the 128-byte one.
+        const int dw = warp - 2;
+        const int nl = dw * 16 + (lane & 15), hh = lane >> 4;
+        const int rsw = (nl >> 1) & 3;  // 64-byte swizzle key of raw row nl
         int it = 0;
         bool ok = true;
         for (int t = pair; t < tiles && ok; t += npairs) {
@@ -225,33 +239,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool col_ok = n < N;
             const float cs = (col_exp != nullptr && col_ok) ? exp2i(col_exp[n]) : 1.0f;
             const float* srow = scales + static_cast<size_t>(col_ok ? n : 0) * G;
-            auto scale_at = [&](int kt) {
-                const int g = kt * 2 + hh;
+            auto scale_at = [&](int kt, int pq) {
+                const int g = kt * 4 + hh * 2 + pq;
                 return (col_ok && g < G) ? __ldg(srow + g) : 0.0f;
             };
-            float s0 = scale_at(0), s1 = scale_at(1), s2 = scale_at(2), s3 = scale_at(3);
+            float a0 = scale_at(0, 0), b0 = scale_at(0, 1), a1 = scale_at(1, 0), b1 = scale_at(1, 1);
             for (int kt = 0; kt < KT; ++kt, ++it) {
                 const int s = it % ST;
                 const uint32_t ph = (it / ST) & 1u;
-                const float sc = s0;
-                s0 = s1;
-                s1 = s2;
-                s2 = s3;
-                s3 = scale_at(kt + 4);
+                const float sc[2] = {a0 * cs, b0 * cs};
+                a0 = a1;
+                b0 = b1;
+                a1 = scale_at(kt + 2, 0);
+                b1 = scale_at(kt + 2, 1);
                 if (!mbar_wait(full_r(s), ph, abort_flag, status, kStatusTimeoutDequant)) {
                     ok = false;
                     break;
                 }
-                const uint4 q = *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
-                const float sv = sc * cs;
-                const float2 s2v = make_float2(sv, sv);
-                const __half2 s2h = __float2half2_rn(sv);
-                uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
-                const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+                const uint8_t* rrow = smem + C::kROff + s * C::kRBytes + nl * 64;
+                const uint4 q[2] = {*reinterpret_cast<const uint4*>(rrow + (((hh * 2) ^ rsw) << 4)),
+                                    *reinterpret_cast<const uint4*>(rrow + (((hh * 2 + 1) ^ rsw) << 4))};
+                uint8_t* brow = smem + C::kBOff + s * C::kBBytes + hh * C::kSubBytes + nl * 128;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int chunk = (hh * 4 + j) ^ (nl & 7);
-                    *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                for (int pq = 0; pq < 2; ++pq) {
+                    const float2 s2v = make_float2(sc[pq], sc[pq]);
+                    const __half2 s2h = __float2half2_rn(sc[pq]);
+                    const uint32_t words[4] = {q[pq].x, q[pq].y, q[pq].z, q[pq].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int chunk = (pq * 4 + j) ^ (nl & 7);
+                        *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                    }
                 }
                 fence_proxy_async_smem();
                 __syncwarp();

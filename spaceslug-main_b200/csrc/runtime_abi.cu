@@ -380,8 +380,11 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
               static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) * 2, 64,
               static_cast<uint32_t>(128 * g.halves), CU_TENSOR_MAP_SWIZZLE_128B);
+    // packed W: 64-k boxes for the single-CTA kernel, 128-k boxes (64 B per
+    // column, 64-byte swizzled) for the pair kernel
     encode_2d(&g.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
-              static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+              static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, use_pair ? 16 : 8, 128,
+              use_pair ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE);
     g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
     g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
