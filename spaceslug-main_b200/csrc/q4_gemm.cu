@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
             const int b = i & 1;
             const uint32_t u = static_cast<uint32_t>(i >> 1);
-            if (!mbar_wait(acc_full(b), u & 1u, abort_flag, status, kStatusTimeoutEpilogue)) break;
+            if (!mbar_wait_warp(acc_full(b), u & 1u, abort_flag, status, kStatusTimeoutEpilogue)) break;
             tc_fence_after_sync();
             const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
             // 2^-col_exp of the tile's 128 columns: lane l holds columns

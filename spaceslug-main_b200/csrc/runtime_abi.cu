@@ -373,7 +373,9 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     }
     const int variant = g_gemm_variant.load();
     // LoRA runs as extra bf16 k-stages of the single-CTA kernel
-    const bool use_pair = p.rank == 0 && pairs > 0 &&
+    // The pair kernel TMA-stores Y (row stride 4N bytes: N % 4 == 0, 16-byte aligned Y).
+    const bool pair_shape_ok = p.N % 4 == 0 && aligned16(p.y);
+    const bool use_pair = p.rank == 0 && pairs > 0 && pair_shape_ok &&
                           (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
     g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
     g.sm_count = c.sm_count;
@@ -385,6 +387,10 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     encode_2d(&g.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(p.K) / 8,
               static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, use_pair ? 16 : 8, 128,
               use_pair ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (use_pair) {
+        encode_2d(&g.tmap_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.y, static_cast<uint64_t>(p.N),
+                  static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.N) * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    }
     g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
     g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
