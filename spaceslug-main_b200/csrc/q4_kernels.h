@@ -85,7 +85,8 @@ int gemv_max_active_clusters(int M, int K, int cluster_k, int cols_per_cluster);
 struct GemmArgs {
     CUtensorMap tmap_x16;     // [M][K] 16-bit, box 64 x (128 * halves), 128B swizzle
     CUtensorMap tmap_w;       // packed as uint32 [N][K/8]: box 8 x 128 unswizzled (single-CTA), 16 x 128 64B-swizzled (pair)
-    CUtensorMap tmap_y;       // pair kernel: Y fp32 [M][N], box 16 x 32, 64B swizzle (needs N % 4 == 0, 16-byte aligned Y)
+    CUtensorMap tmap_s;       // pair kernel: scales fp32 [N][K/32], box 4 x 128 (needs K % 128 == 0)
+    CUtensorMap tmap_y;       // pair kernel: Y fp32 [M][N], box 32 x 32 (needs N % 4 == 0, 16-byte aligned Y)
     CUtensorMap tmap_t;       // LoRA-stage A operand, bf16 [M][64*stages], box 64 x (128 * halves), 128B swizzle
     const float* scales;      // [N][K/32]
     const int* col_exp;       // [N] power-of-two exponent applied to the column's scales, or nullptr

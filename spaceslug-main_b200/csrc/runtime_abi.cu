@@ -373,8 +373,9 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     }
     const int variant = g_gemm_variant.load();
     // LoRA runs as extra bf16 k-stages of the single-CTA kernel
-    // The pair kernel TMA-stores Y (row stride 4N bytes: N % 4 == 0, 16-byte aligned Y).
-    const bool pair_shape_ok = p.N % 4 == 0 && aligned16(p.y);
+    // The pair kernel TMA-loads the scales (row stride K/8 bytes: K % 128 == 0)
+    // and TMA-stores Y (row stride 4N bytes: N % 4 == 0, 16-byte aligned Y).
+    const bool pair_shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
     const bool use_pair = p.rank == 0 && pairs > 0 && pair_shape_ok &&
                           (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
     g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
@@ -388,8 +389,10 @@ void run_problem(const Problem& p, cudaStream_t stream) {
               static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 2, use_pair ? 16 : 8, 128,
               use_pair ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE);
     if (use_pair) {
+        encode_2d(&g.tmap_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.scales, static_cast<uint64_t>(p.K) / 32,
+                  static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 8, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
         encode_2d(&g.tmap_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.y, static_cast<uint64_t>(p.N),
-                  static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.N) * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+                  static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.N) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     }
     g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;

@@ -136,8 +136,9 @@ def variant(request, session):
     session.set_gemm_variant(prev)
 
 
-# The pair kernel takes N % 4 == 0 (other shapes fall back to the single-CTA
-# kernel); these shapes reach it with ragged row, column and k tiles.
+# The pair kernel takes K % 128 == 0 and N % 4 == 0 (other shapes fall back to
+# the single-CTA kernel): (300, 1000, 1152), (129, 260, 256), (1, 4, 128) and
+# (513, 700, 4096) reach it with ragged row and column tiles.
 @pytest.mark.parametrize("m,n,k", [(9, 8, 32), (300, 1000, 1056), (256, 256, 64), (513, 700, 4096),
                                    (300, 1000, 1152), (129, 260, 256), (1, 4, 128)])
 def test_gemm_variants_ragged(session, oracle, cuda, variant, m, n, k):
@@ -170,7 +171,7 @@ def test_gemm_variants_agree_and_lora(session, oracle, cuda):
 def test_gemm_pair_kernel_on_large_ragged_problem(session, oracle, cuda, n):
     # large enough that the automatic choice is the CTA-pair kernel (n = 4500),
     # or would be but for N % 4 != 0 (n = 4501: the single-CTA kernel)
-    m, k = 1100, 1056
+    m, k = 1100, 1152
     w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=5)
     x = synth.make_x(m, k, seed=6)
     y = session.q4gemm(x, packed, scales, n)
