@@ -87,6 +87,54 @@ __global__ void __launch_bounds__(256) cast_x_kernel(const float* __restrict__ x
     }
 }
 
+template <typename T16>
+__device__ __forceinline__ uint2 pack4_16(float4 v, float scale) {
+    if constexpr (std::is_same<T16, __half>::value) {
+        __half2 a = __floats2half2_rn(v.x * scale, v.y * scale);
+        __half2 b = __floats2half2_rn(v.z * scale, v.w * scale);
+        return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    } else {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x * scale, v.y * scale);
+        __nv_bfloat162 b = __floats2bfloat162_rn(v.z * scale, v.w * scale);
+        return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    }
+}
+
+// The same cast for K <= 1024 R: the row is read once into registers (R
+// float4 per thread, all loads in flight together), reduced, scaled and
+// written; the two-pass kernel above reads it twice.
+template <typename T16, int R>
+__global__ void __launch_bounds__(256) cast_x_reg_kernel(const float* __restrict__ x, T16* __restrict__ x16,
+                                                         int* __restrict__ row_exp, int K) {
+    __shared__ float red[32];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int m = blockIdx.x;
+    const float* row = x + static_cast<size_t>(m) * K;
+    float4 v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int k = (r * 256 + static_cast<int>(threadIdx.x)) * 4;
+        v[r] = k < K ? __ldcs(reinterpret_cast<const float4*>(row + k)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float scale = 1.0f;
+    if (row_exp != nullptr) {
+        float mx = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[r].x), fabsf(v[r].y)), fmaxf(fabsf(v[r].z), fabsf(v[r].w))));
+        mx = block_max(mx, red);
+        const int e = pow2_exponent(mx, 14);
+        if (threadIdx.x == 0) row_exp[m] = e;
+        scale = exp2i(e);
+    }
+    T16* out = x16 + static_cast<size_t>(m) * K;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int k = (r * 256 + static_cast<int>(threadIdx.x)) * 4;
+        if (k < K) *reinterpret_cast<uint2*>(out + k) = pack4_16<T16>(v[r], scale);
+    }
+}
+
 // One warp per column.
 __global__ void __launch_bounds__(256) col_exp_kernel(const float* __restrict__ scales, int* __restrict__ col_exp,
                                                      int N, int G) {
@@ -293,11 +341,23 @@ inline int grid_1d(long long work, int block) { return static_cast<int>((work + 
 
 }  // namespace
 
+namespace {
+template <typename T16>
+void launch_cast_t(const float* x, T16* x16, int* row_exp, int M, int K, cudaStream_t stream) {
+    if (K <= 1024 * 4)
+        cast_x_reg_kernel<T16, 4><<<M, 256, 0, stream>>>(x, x16, row_exp, K);
+    else if (K <= 1024 * 8)
+        cast_x_reg_kernel<T16, 8><<<M, 256, 0, stream>>>(x, x16, row_exp, K);
+    else
+        cast_x_kernel<T16><<<M, 256, 0, stream>>>(x, x16, row_exp, K);
+}
+}  // namespace
+
 int launch_cast_x(const float* x, void* x16, int* row_exp, int M, int K, Operand16 op, cudaStream_t stream) {
     if (op == Operand16::kF16)
-        cast_x_kernel<__half><<<M, 256, 0, stream>>>(x, static_cast<__half*>(x16), row_exp, K);
+        launch_cast_t(x, static_cast<__half*>(x16), row_exp, M, K, stream);
     else
-        cast_x_kernel<__nv_bfloat16><<<M, 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(x16), row_exp, K);
+        launch_cast_t(x, static_cast<__nv_bfloat16*>(x16), row_exp, M, K, stream);
     return static_cast<int>(cudaGetLastError());
 }
 
