@@ -432,6 +432,70 @@ def gemm_gpu(args, dist: Dist, torch, session, synth, peaks, name: str, steps: i
     return out
 
 
+def upload_gpu(args, dist: Dist, torch, session) -> dict:
+    """Model-load path at configs[4]'s weight size (K = 8192, N = 28672: 117 MB
+    packed, 235 MB logical int8): host packing, the staged upload of packed
+    words from pageable memory, and the upload of the logical matrix with
+    packing on the device.  Each figure is the best of three, wall clock
+    around a synchronous C-ABI call."""
+    dev = torch.device("cuda", dist.local)
+    k, n = 8192, 28672
+    rng = np.random.default_rng(7)
+    b = rng.integers(-8, 8, size=(k, n), dtype=np.int8)
+    scales = rng.uniform(0.003, 0.01, size=(n, k // 32)).astype(np.float32)
+    packed_bytes, scale_bytes = k * n // 2, scales.nbytes
+
+    def best(fn, reps=3):
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    out = {"shape": [k, n], "packed_MB": round(packed_bytes / 1e6, 1), "logical_MB": round(b.nbytes / 1e6, 1),
+           "scales_MB": round(scale_bytes / 1e6, 1)}
+    holder = {}
+    t = best(lambda: holder.__setitem__("p", session.q4_pack(b)))
+    packed = holder.pop("p")
+    out["host_pack_ms"] = round(t * 1e3, 1)
+    out["host_pack_threads"] = "several (std::thread, <= 8)"
+    session.weights(packed[:32], scales[:8, :1].copy(), 32, 8).close()  # a first handle sets up the device context
+
+    def create(fn):
+        h = fn()
+        h.close()
+
+    t = best(lambda: create(lambda: session.weights(packed, scales, k, n, device=dist.local)))
+    out["create_packed_ms"] = round(t * 1e3, 2)
+    out["create_packed_GBps"] = round((packed_bytes + scale_bytes) / t / 1e9, 1)
+    t = best(lambda: create(lambda: session.weights_logical(b, scales, k, n, device=dist.local)))
+    out["create_logical_ms"] = round(t * 1e3, 2)
+    out["create_logical_GBps"] = round((b.nbytes + scale_bytes) / t / 1e9, 1)
+    # context: plain H2D copies of the packed words from pageable and pinned memory
+    src = torch.from_numpy(packed.view(np.int32))
+    pin = src.pin_memory()
+    for name, host in (("pageable", src), ("pinned", pin)):
+        def cp(host=host):
+            host.to(dev, non_blocking=False)
+            torch.cuda.synchronize(dev)
+        t = best(cp)
+        out[f"plain_copy_{name}_GBps"] = round(packed_bytes / t / 1e9, 1)
+    del pin
+    if dist.rank == 0:
+        try:  # cpu_baseline leg: the reference's own pack_q4 on one core, a column sample
+            from oracle.oracle import Reference  # test-infra: CPU baseline only
+            if Reference.available():
+                sample = np.ascontiguousarray(b[:, :2048])
+                ref = Reference()
+                t = best(lambda: ref.pack_q4(sample), reps=2)
+                out["cpu_baseline"] = {"kind": "reference", "cores": 1, "sample": "pack_q4 of 8192 x 2048",
+                                       "ref_pack_ms_full_matrix": round(t * (n / 2048) * 1e3, 1)}
+        except Exception as exc:  # report, do not hide
+            out["cpu_baseline"] = {"error": str(exc)}
+    return out
+
+
 def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     """columns of W sharded over the ranks, NCCL all-gather of Y."""
     from spaceslug_b200 import sharding
@@ -521,6 +585,10 @@ def main() -> None:
                     sec[name] = gemm_gpu(args, dist, torch, session, synth, peaks, name, steps=10)
                 except Exception as exc:  # report, do not hide
                     sec[name] = {"error": str(exc)}
+            try:
+                sec["upload"] = upload_gpu(args, dist, torch, session)
+            except Exception as exc:  # report, do not hide
+                sec["upload"] = {"error": str(exc)}
             line["secondary"] = sec
         if dist.rank == 0 and dist.world == 1:
             line["cpu_baseline"] = cpu_reference_decode(args.cpu_seconds, threads=1)

@@ -98,6 +98,9 @@ int spaceslug_q4gemm_device(const float* x, const uint32_t* packed, const float*
 
 /* Device-resident weights (model-load time upload, then many calls), after
  * the persistent-session pattern of vulkan-runtime/src/api/lora_session_api.h:6-14.
+ * Pageable host buffers are uploaded through a per-device ring of pinned
+ * slots filled by several host threads while earlier slots are in flight;
+ * pinned buffers go out as one DMA.
  * The handle keeps columns [col_begin, col_end) of a K x N weight matrix given
  * in the reference layout (host pointers), so a column shard of an N-sharded
  * multi-GPU layer is one contiguous byte range with no repacking.
@@ -105,6 +108,18 @@ int spaceslug_q4gemm_device(const float* x, const uint32_t* packed, const float*
 typedef struct spaceslug_q4_weights spaceslug_q4_weights;
 int spaceslug_q4_weights_create(const uint32_t* packed, const float* scales, uint32_t k, uint32_t n,
                                 uint32_t col_begin, uint32_t col_end, int device, spaceslug_q4_weights** out);
+/* As spaceslug_q4_weights_create, from the logical int4 matrix w_kn[k*n + col]
+ * in [-8, 7] (int8 host buffer, the input of pack_q4 in
+ * vulkan-runtime/tests/test_q4gemm.cpp:84-99) instead of packed words: row
+ * blocks of columns [col_begin, col_end) cross PCIe through pinned staging
+ * slots and are packed on the device into the reference layout.  Values
+ * outside [-8, 7] are stored as (v & 0xF), like the reference packer. */
+int spaceslug_q4_weights_create_logical(const int8_t* w_kn, const float* scales, uint32_t k, uint32_t n,
+                                        uint32_t col_begin, uint32_t col_end, int device, spaceslug_q4_weights** out);
+/* Copies the handle's packed words ((col_end-col_begin) * k/8, reference
+ * layout of those columns) and/or scales ((col_end-col_begin) * k/32) to host
+ * buffers; either output may be NULL.  Synchronous. */
+int spaceslug_q4_weights_export(const spaceslug_q4_weights* w, uint32_t* packed_out, float* scales_out);
 /* Attach (or, with rank 0, detach) a LoRA adapter; lora_b is the full
  * [rank x n] host matrix, the handle keeps its own columns. */
 int spaceslug_q4_weights_set_lora(spaceslug_q4_weights* w, const float* lora_a, const float* lora_b, uint32_t rank,

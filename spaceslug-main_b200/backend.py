@@ -44,6 +44,9 @@ _SIGNATURES = {
                                       ctypes.c_int),
     "spaceslug_q4_weights_create": ([_u32p, _f32p, _u32, _u32, _u32, _u32, ctypes.c_int, ctypes.POINTER(_vp)],
                                     ctypes.c_int),
+    "spaceslug_q4_weights_create_logical": ([_i8p, _f32p, _u32, _u32, _u32, _u32, ctypes.c_int, ctypes.POINTER(_vp)],
+                                            ctypes.c_int),
+    "spaceslug_q4_weights_export": ([_vp, _u32p, _f32p], ctypes.c_int),
     "spaceslug_q4_weights_set_lora": ([_vp, _f32p, _f32p, _u32, ctypes.c_float], ctypes.c_int),
     "spaceslug_q4_weights_run": ([_vp, _vp, _vp, _u32, _vp], ctypes.c_int),
     "spaceslug_q4_weights_run_host": ([_vp, _f32p, _f32p, _u32], ctypes.c_int),
@@ -66,6 +69,7 @@ _CAPABILITIES = {
     "spaceslug_q4gemm_lora": "q4gemm_lora_fused",
     "spaceslug_q4gemm_device": "q4gemm_device",
     "spaceslug_q4_weights_create": "q4_weights_resident",
+    "spaceslug_q4_weights_create_logical": "q4_weights_device_pack",
 }
 
 
@@ -213,20 +217,39 @@ class BackendSession:
                 device: int = 0) -> "Q4Weights":
         return Q4Weights(self, packed, scales, k, n, col_begin, n if col_end is None else col_end, device)
 
+    def weights_logical(self, w_kn, scales, k: int, n: int, col_begin: int = 0, col_end: int | None = None,
+                        device: int = 0) -> "Q4Weights":
+        """Handle from the logical int4 matrix w_kn [k, n] (int8 in [-8, 7]),
+        packed on the device during the upload."""
+        return Q4Weights(self, None, scales, k, n, col_begin, n if col_end is None else col_end, device, w_kn=w_kn)
+
 
 class Q4Weights:
     """Device-resident int4 weights (a handle of the C-ABI)."""
 
     def __init__(self, session: BackendSession, packed, scales, k: int, n: int, col_begin: int, col_end: int,
-                 device: int) -> None:
+                 device: int, w_kn=None) -> None:
         self.session = session
-        pk, sc = _arr(packed, np.uint32), _arr(scales, np.float32)
+        sc = _arr(scales, np.float32)
         self.k, self.n_total, self.col_begin, self.col_end = k, n, col_begin, col_end
         self.n = col_end - col_begin
         h = _vp()
-        session._call("spaceslug_q4_weights_create", _p(pk, _u32p), _p(sc, _f32p), k, n, col_begin, col_end,
-                      device, ctypes.byref(h))
+        if w_kn is None:
+            pk = _arr(packed, np.uint32)
+            session._call("spaceslug_q4_weights_create", _p(pk, _u32p), _p(sc, _f32p), k, n, col_begin, col_end,
+                          device, ctypes.byref(h))
+        else:
+            wk = _arr(w_kn, np.int8)
+            session._call("spaceslug_q4_weights_create_logical", _p(wk, _i8p), _p(sc, _f32p), k, n, col_begin,
+                          col_end, device, ctypes.byref(h))
         self.handle = h
+
+    def export(self) -> tuple[np.ndarray, np.ndarray]:
+        """The handle's packed words [n, k/8] and scales [n, k/32] (its columns)."""
+        pk = np.empty((self.n, self.k // 8), np.uint32)
+        sc = np.empty((self.n, self.k // 32), np.float32)
+        self.session._call("spaceslug_q4_weights_export", self.handle, _p(pk, _u32p), _p(sc, _f32p))
+        return pk, sc
 
     def set_lora(self, lora_a, lora_b, alpha: float) -> None:
         if lora_a is None:

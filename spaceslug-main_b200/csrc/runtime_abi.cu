@@ -24,6 +24,7 @@
 
 #include "../../include/runtime_abi.h"
 #include "q4_kernels.h"
+#include "upload.h"
 
 namespace {
 
@@ -509,21 +510,9 @@ int spaceslug_q4_pack(const int8_t* w_kn, uint32_t k, uint32_t n, uint32_t* pack
     if (!w_kn || !packed_out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
     if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
     return guarded([&] {
-        // Column-major output: for each column n, K/8 words of 8 nibbles each.
-        // Walk k in blocks of 8 rows so each output word is assembled in a
-        // register; the int8 source is read row-block by row-block.
-        const size_t words_per_col = k / 8u;
-        std::vector<uint32_t> acc(n);
-        for (uint32_t c = 0; c < k / 8u; ++c) {
-            std::fill(acc.begin(), acc.end(), 0u);
-            for (uint32_t i = 0; i < 8u; ++i) {
-                const int8_t* row = w_kn + static_cast<size_t>(8u * c + i) * n;
-                const uint32_t shift = 4u * i;
-                for (uint32_t col = 0; col < n; ++col)
-                    acc[col] |= (static_cast<uint32_t>(static_cast<uint8_t>(row[col])) & 0xFu) << shift;
-            }
-            for (uint32_t col = 0; col < n; ++col) packed_out[static_cast<size_t>(col) * words_per_col + c] = acc[col];
-        }
+        // Column-major output: for each column, K/8 words of 8 nibbles each;
+        // the K/8 output chunks are split over host threads.
+        q4up::host_pack(w_kn, k, n, packed_out);
         return SPACESLUG_OK;
     });
 }
@@ -685,8 +674,8 @@ int spaceslug_q4_weights_create(const uint32_t* packed, const float* scales, uin
             check(cudaMalloc(&w->scales, sb), "cudaMalloc scales");
             check(cudaMalloc(&w->col_exp, static_cast<size_t>(w->N) * sizeof(int)), "cudaMalloc col_exp");
             std::lock_guard<std::mutex> lk(c.host_mu);
-            h2d(w->packed, packed + static_cast<size_t>(col_begin) * (k / 8u), pb, c.stream);
-            h2d(w->scales, scales + static_cast<size_t>(col_begin) * G, sb, c.stream);
+            q4up::staged_h2d(device, w->packed, packed + static_cast<size_t>(col_begin) * (k / 8u), pb, c.stream);
+            q4up::staged_h2d(device, w->scales, scales + static_cast<size_t>(col_begin) * G, sb, c.stream);
             check_launch(q4::launch_col_exp(w->scales, w->col_exp, w->N, w->K, c.stream), "col_exp");
             check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         } catch (...) {
@@ -694,6 +683,54 @@ int spaceslug_q4_weights_create(const uint32_t* packed, const float* scales, uin
             throw;
         }
         *out = w;
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_create_logical(const int8_t* w_kn, const float* scales, uint32_t k, uint32_t n,
+                                        uint32_t col_begin, uint32_t col_end, int device, spaceslug_q4_weights** out) {
+    if (!w_kn || !scales || !out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (k == 0 || n == 0 || k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "k must be a positive multiple of 32, n > 0");
+    if (col_begin >= col_end || col_end > n) return fail(SPACESLUG_INVALID_ARGUMENT, "bad column range");
+    *out = nullptr;
+    return guarded([&] {
+        check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceCtx& c = ctx_for(device);
+        auto* w = new spaceslug_q4_weights();
+        w->device = device;
+        w->K = static_cast<int>(k);
+        w->N = static_cast<int>(col_end - col_begin);
+        w->col_begin = col_begin;
+        w->n_total = n;
+        const size_t G = k / 32u;
+        const size_t pb = static_cast<size_t>(w->N) * k / 2, sb = static_cast<size_t>(w->N) * G * 4;
+        try {
+            check(cudaMalloc(&w->packed, pb), "cudaMalloc packed");
+            check(cudaMalloc(&w->scales, sb), "cudaMalloc scales");
+            check(cudaMalloc(&w->col_exp, static_cast<size_t>(w->N) * sizeof(int)), "cudaMalloc col_exp");
+            std::lock_guard<std::mutex> lk(c.host_mu);
+            q4up::staged_pack_logical(device, w->packed, w_kn, k, n, col_begin, static_cast<uint32_t>(w->N), c.stream);
+            q4up::staged_h2d(device, w->scales, scales + static_cast<size_t>(col_begin) * G, sb, c.stream);
+            check_launch(q4::launch_col_exp(w->scales, w->col_exp, w->N, w->K, c.stream), "col_exp");
+            check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        } catch (...) {
+            spaceslug_q4_weights_destroy(w);
+            throw;
+        }
+        *out = w;
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_export(const spaceslug_q4_weights* w, uint32_t* packed_out, float* scales_out) {
+    if (!w || (!packed_out && !scales_out)) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        DeviceCtx& c = ctx_for(w->device);
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        if (packed_out) d2h(packed_out, w->packed, static_cast<size_t>(w->N) * w->K / 2, c.stream);
+        if (scales_out) d2h(scales_out, w->scales, static_cast<size_t>(w->N) * (w->K / 32) * 4, c.stream);
+        check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         return SPACESLUG_OK;
     });
 }

@@ -47,7 +47,10 @@ def test_vector_add_million(session):
     assert out[0] == 3.0 and out[-1] == 3.0
 
 
-@pytest.mark.parametrize("k,n", [(32, 1), (64, 256), (96, 37), (4096, 64)])
+# the host packer splits the k/8 output chunks over threads: 1 chunk, chunk
+# counts that do not divide evenly, and a large matrix
+@pytest.mark.parametrize("k,n", [(32, 1), (64, 256), (96, 37), (4096, 64), (1000 // 8 * 8 // 32 * 32, 3),
+                                 (2080, 777), (8192, 513)])
 def test_host_pack_matches_oracle(session, oracle, k, n):
     b = synth.lcg_int4(k * n, 7 * k + n).reshape(k, n)
     assert np.array_equal(session.q4_pack(b), oracle.pack(b))
@@ -96,6 +99,11 @@ def test_invalid_arguments_return_1_before_device_work(session):
     h = ctypes.c_void_p()
     assert wc(_u(p), _f(s), 64, 64, 10, 5, 0, ctypes.byref(h)) == 1  # empty column range
     assert wc(_u(p), _f(s), 64, 64, 0, 65, 0, ctypes.byref(h)) == 1  # beyond n
+    wl = session.raw("spaceslug_q4_weights_create_logical")
+    assert wl(None, _f(s), 64, 64, 0, 64, 0, ctypes.byref(h)) == 1
+    assert wl(w.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), _f(s), 48, 4, 0, 4, 0, ctypes.byref(h)) == 1  # K % 32
+    assert wl(w.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), _f(s), 32, 4, 3, 3, 0, ctypes.byref(h)) == 1
+    assert session.raw("spaceslug_q4_weights_export")(None, _u(p), _f(s)) == 1
     assert session.raw("spaceslug_q4_weights_run")(None, 16, 16, 1, None) == 1
     assert session.raw("spaceslug_q4_weights_destroy")(None) == 1
     assert session.raw("spaceslug_q4_set_operand_type")(7) == -1
