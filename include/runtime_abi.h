@@ -175,6 +175,54 @@ uint64_t spaceslug_q4_launch_count(void);
 /* Human-readable description of the last non-zero return code on this thread. */
 const char* spaceslug_last_error(void);
 
+/* ---- CQ4 (Cactus-Quants) ------------------------------------------------
+ * C[M x N] = A'[M x K] * W'^T in fp16 storage with fp32 accumulation, where
+ * A' is the activation transformed into the code basis and
+ * W'[n][k] = norm(n, k / group_size) * codebook[idx(n, k)]: the reference's
+ * cactus_quant_matmul (vulkan-runtime/src/cactus/cactus_x86.cpp:384-397),
+ * which its GPU path runs as transform_act -> dequant_w -> sgemm_f16_am
+ * (bench/bench_cq4gemm.cpp).  The matrix description is field for field the
+ * reference's CactusQuantMatrixBridge (src/cactus/cactus_x86_bridge.h), so a
+ * pointer to one can be passed as is; fp16 values are IEEE binary16 bits.
+ * Supported: bits == 4; K % 32 == 0; Hadamard mode with a power-of-two
+ * group_size in [32, 256] and K == group_size * num_groups, or the
+ * orthogonal mode (one group spanning K, dense rotation [K][K]);
+ * INTERLEAVED_4ROW panels need N % 4 == 0.  The product runs on the tcgen05
+ * GEMM with the codebook applied while the weights are dequantised. */
+#define SPACESLUG_CQ4_FLAG_ORTHOGONAL 4u       /* CACTUS_BRIDGE_QUANT_FLAG_ORTHOGONAL */
+#define SPACESLUG_CQ4_FLAG_INTERLEAVED_4ROW 8u /* CACTUS_BRIDGE_QUANT_FLAG_INTERLEAVED_4ROW */
+typedef struct spaceslug_cq4_matrix {
+    uint32_t bits;
+    uint32_t k;
+    uint32_t n;
+    uint32_t group_size;
+    uint32_t num_groups;
+    uint32_t flags;
+    const uint16_t* codebook;          /* [2^bits] fp16 */
+    const uint16_t* input_scale;       /* [K] fp16 or NULL */
+    const uint16_t* input_scale_recip; /* [K] fp16 or NULL (takes precedence) */
+    const uint16_t* norms;             /* [N * num_groups] fp16, stored layout (panel-major when interleaved) */
+    const uint8_t* packed_indices;     /* LSB-first 4-bit indices, or 4-row interleaved panels */
+    const int8_t* left_signs;          /* [group_size] +-1 or NULL */
+    const int8_t* right_signs;         /* [group_size] +-1 or NULL */
+    const uint32_t* permutation;       /* [group_size] or NULL */
+    const uint16_t* rotation;          /* [K * K] fp16, orthogonal mode only */
+    const int8_t* expanded;            /* unused */
+    const float* norm_f32;             /* unused */
+} spaceslug_cq4_matrix;
+typedef struct spaceslug_cq4_weights spaceslug_cq4_weights;
+/* Uploads a CQ4 matrix (host pointers) to `device`. */
+int spaceslug_cq4_weights_create(const spaceslug_cq4_matrix* m, int device, spaceslug_cq4_weights** out);
+/* C = cactus_quant_matmul(W, A): a [m x K] and c [m x N] fp16 device
+ * pointers, asynchronous on `stream`. */
+int spaceslug_cq4_matmul(spaceslug_cq4_weights* w, const uint16_t* a, uint16_t* c, uint32_t m, void* stream);
+/* Same with host pointers, synchronous. */
+int spaceslug_cq4_matmul_host(spaceslug_cq4_weights* w, const uint16_t* a, uint16_t* c, uint32_t m);
+/* The code-basis activations alone (fp16, [m x K]), host pointers: the
+ * reference's transform_act output (shaders/transform_act.comp). */
+int spaceslug_cq4_transform_host(spaceslug_cq4_weights* w, const uint16_t* a, uint16_t* a_out, uint32_t m);
+int spaceslug_cq4_weights_destroy(spaceslug_cq4_weights* w);
+
 #ifdef __cplusplus
 }
 #endif

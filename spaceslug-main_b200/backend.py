@@ -57,6 +57,11 @@ _SIGNATURES = {
     "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
     "spaceslug_last_error": ([], ctypes.c_char_p),
+    "spaceslug_cq4_weights_create": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
+    "spaceslug_cq4_matmul": ([_vp, _vp, _vp, _u32, _vp], ctypes.c_int),
+    "spaceslug_cq4_matmul_host": ([_vp, _vp, _vp, _u32], ctypes.c_int),
+    "spaceslug_cq4_transform_host": ([_vp, _vp, _vp, _u32], ctypes.c_int),
+    "spaceslug_cq4_weights_destroy": ([_vp], ctypes.c_int),
 }
 
 # symbol -> capability name reported by capabilities()
@@ -70,7 +75,18 @@ _CAPABILITIES = {
     "spaceslug_q4gemm_device": "q4gemm_device",
     "spaceslug_q4_weights_create": "q4_weights_resident",
     "spaceslug_q4_weights_create_logical": "q4_weights_device_pack",
+    "spaceslug_cq4_matmul": "cq4_quant_matmul",
 }
+
+
+class CQ4Matrix(ctypes.Structure):
+    """spaceslug_cq4_matrix (include/runtime_abi.h), field for field the
+    reference's CactusQuantMatrixBridge."""
+    _fields_ = [("bits", ctypes.c_uint32), ("k", ctypes.c_uint32), ("n", ctypes.c_uint32),
+                ("group_size", ctypes.c_uint32), ("num_groups", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+                ("codebook", _vp), ("input_scale", _vp), ("input_scale_recip", _vp), ("norms", _vp),
+                ("packed_indices", _vp), ("left_signs", _vp), ("right_signs", _vp), ("permutation", _vp),
+                ("rotation", _vp), ("expanded", _vp), ("norm_f32", _vp)]
 
 
 class BackendError(RuntimeError):
@@ -217,6 +233,15 @@ class BackendSession:
                 device: int = 0) -> "Q4Weights":
         return Q4Weights(self, packed, scales, k, n, col_begin, n if col_end is None else col_end, device)
 
+    def cq4_weights(self, *, k: int, n: int, group_size: int, num_groups: int, flags: int, codebook, norms, packed,
+                    input_scale=None, input_scale_recip=None, left_signs=None, right_signs=None, permutation=None,
+                    rotation=None, bits: int = 4, device: int = 0) -> "CQ4Weights":
+        """A CQ4 matrix (fp16 arrays as uint16 bits) resident on `device`."""
+        return CQ4Weights(self, dict(bits=bits, k=k, n=n, group_size=group_size, num_groups=num_groups, flags=flags,
+                                     codebook=codebook, input_scale=input_scale, input_scale_recip=input_scale_recip,
+                                     norms=norms, packed=packed, left_signs=left_signs, right_signs=right_signs,
+                                     permutation=permutation, rotation=rotation), device)
+
     def weights_logical(self, w_kn, scales, k: int, n: int, col_begin: int = 0, col_end: int | None = None,
                         device: int = 0) -> "Q4Weights":
         """Handle from the logical int4 matrix w_kn [k, n] (int8 in [-8, 7]),
@@ -272,6 +297,57 @@ class Q4Weights:
     def close(self) -> None:
         if self.handle:
             self.session._call("spaceslug_q4_weights_destroy", self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class CQ4Weights:
+    """Device-resident CQ4 matrix (a handle of the C-ABI)."""
+
+    def __init__(self, session: BackendSession, d: dict, device: int) -> None:
+        self.session = session
+        self.k, self.n = d["k"], d["n"]
+        keep = {
+            "codebook": _arr(d["codebook"], np.uint16), "norms": _arr(d["norms"], np.uint16),
+            "packed_indices": _arr(d["packed"], np.uint8),
+            "input_scale": None if d["input_scale"] is None else _arr(d["input_scale"], np.uint16),
+            "input_scale_recip": None if d["input_scale_recip"] is None else _arr(d["input_scale_recip"], np.uint16),
+            "left_signs": None if d["left_signs"] is None else _arr(d["left_signs"], np.int8),
+            "right_signs": None if d["right_signs"] is None else _arr(d["right_signs"], np.int8),
+            "permutation": None if d["permutation"] is None else _arr(d["permutation"], np.uint32),
+            "rotation": None if d["rotation"] is None else _arr(d["rotation"], np.uint16),
+        }
+        m = CQ4Matrix(d["bits"], d["k"], d["n"], d["group_size"], d["num_groups"], d["flags"])
+        for name, arr in keep.items():
+            setattr(m, name, None if arr is None else arr.ctypes.data)
+        h = _vp()
+        session._call("spaceslug_cq4_weights_create", ctypes.addressof(m), device, ctypes.byref(h))
+        self.handle = h
+
+    def matmul_host(self, a_bits) -> np.ndarray:
+        """C (fp16 bits [m, n]) = cactus_quant_matmul(W, A) for A fp16 bits [m, k]."""
+        a = _arr(a_bits, np.uint16).reshape(-1, self.k)
+        c = np.empty((a.shape[0], self.n), np.uint16)
+        self.session._call("spaceslug_cq4_matmul_host", self.handle, a.ctypes.data, c.ctypes.data, a.shape[0])
+        return c
+
+    def matmul(self, a_dev: int, c_dev: int, m: int, stream: int = 0) -> None:
+        self.session._call("spaceslug_cq4_matmul", self.handle, a_dev, c_dev, m, stream or None)
+
+    def transform_host(self, a_bits) -> np.ndarray:
+        a = _arr(a_bits, np.uint16).reshape(-1, self.k)
+        out = np.empty_like(a)
+        self.session._call("spaceslug_cq4_transform_host", self.handle, a.ctypes.data, out.ctypes.data, a.shape[0])
+        return out
+
+    def close(self) -> None:
+        if self.handle:
+            self.session._call("spaceslug_cq4_weights_destroy", self.handle)
             self.handle = None
 
     def __enter__(self):

@@ -71,7 +71,8 @@ struct Cfg {
     static constexpr int kBarOff = kROff + kStages * kRBytes;
     static constexpr int kNumBars = 4 * kStages + 2 + 2 + 1;  // ring, acc_full[2], acc_empty[2], done
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kBytes = kMiscOff + 16;
+    static constexpr int kLutOff = kMiscOff + 16;     // CQ4: 256 f16 pairs (codebook[b & 15], codebook[b >> 4])
+    static constexpr int kBytes = kLutOff + 1024;
     static constexpr int kSmemAlloc = kBytes + 1024;  // slack for 1024-byte alignment
     static constexpr int kTmemCols = 2 * H * kBN;     // 256 or 512
     static_assert(kSmemAlloc <= 232448, "shared memory budget");
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmap_t, const float* __restrict__ scales,
                    const int* __restrict__ col_exp, const int* __restrict__ row_exp, float* __restrict__ y, int M,
                    int N, int K, const float* __restrict__ lora_b, int rank, float lora_scale, int lora_stages,
-                   int* __restrict__ status) {
+                   const uint32_t* __restrict__ lut, int* __restrict__ status) {
     using C = Cfg<H>;
     constexpr int ST = C::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -136,6 +137,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(smem_u32(tmem_holder), C::kTmemCols);
         tmem_relinquish();
     }
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem + C::kLutOff);
+    if (lut != nullptr && tid < 256) lut_s[tid] = __ldg(lut + tid);
     tc_fence_before_sync();
     __syncthreads();
     tc_fence_after_sync();
@@ -266,10 +269,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float2 s2v = make_float2(sv, sv);
                     const __half2 s2h = __float2half2_rn(sv);
                     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+                    if (lut == nullptr) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int chunk = (hh * 4 + j) ^ (nl & 7);
-                        *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                        for (int j = 0; j < 4; ++j) {
+                            const int chunk = (hh * 4 + j) ^ (nl & 7);
+                            *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                        }
+                    } else {
+                        // CQ4: pair (k, k+1) = RN16(codebook[idx] * norm), idx from byte b of the word
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int b = 0; b < 4; ++b) {
+                                const uint32_t e = lut_s[(words[j] >> (8 * b)) & 0xFFu];
+                                const __half2 w = __hmul2(*reinterpret_cast<const __half2*>(&e), s2h);
+                                o[b] = *reinterpret_cast<const uint32_t*>(&w);
+                            }
+                            const int chunk = (hh * 4 + j) ^ (nl & 7);
+                            *reinterpret_cast<uint4*>(brow + chunk * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
                     }
                 } else {
                     // LoRA stage q: (alpha/r) * B_lora[16q .. 16q+15, n] * 2^f_n as bf16;
@@ -389,7 +408,7 @@ int launch_gemm_t(const GemmArgs& a, int grid, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.tmap_t, a.scales, a.col_exp, a.row_exp, a.y, a.M, a.N,
-                           a.K, a.lora_b, a.rank, a.lora_scale, a.lora_stages, a.status);
+                           a.K, a.lora_b, a.rank, a.lora_scale, a.lora_stages, a.lut, a.status);
     return static_cast<int>(e);
 }
 

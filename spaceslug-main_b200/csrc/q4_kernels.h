@@ -102,6 +102,8 @@ struct GemmArgs {
     float lora_scale;
     int lora_stages;          // single-CTA kernel: ceil(rank/16) bf16 k-stages (0 = no LoRA); the pair kernel
                               // adds the LoRA term in its epilogue from lora_t
+    const uint32_t* lut = nullptr;  // single-CTA kernel, f16 only: CQ4 codebook pairs (256 words); the
+                                    // scales are then the norms and W = RN16(codebook[idx] * norm)
     int* status;              // kernel status word (0 = ok)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
@@ -129,6 +131,14 @@ int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t
 int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
                    float* partial = nullptr, const int* row_exp = nullptr, uint16_t* t_op_bits = nullptr);
 int lora_xa_chunks(int K);
+// CQ4 activation transform into the code basis, fp16 [M][K] -> fp16 [M][K]:
+// Hadamard groups of gs in {32, 64, 128, 256} (rotation == nullptr) or the
+// dense orthogonal rotation [K][K] fp16.  lsign / rsign ([gs], +-1) and perm
+// ([gs]) may be nullptr.
+int launch_cq4_transform(const void* a, void* a_out, const float* recip, const float* lsign, const float* rsign,
+                         const uint32_t* perm, const void* rotation, int M, int K, int gs, float inv_sqrt,
+                         cudaStream_t stream);
+int launch_f32_to_f16(const float* y, void* c, long long count, cudaStream_t stream);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream);

@@ -498,6 +498,106 @@ struct spaceslug_q4_weights {
     float alpha = 0.0f;
 };
 
+// CQ4 (Cactus-Quants) matrix on one device: the indices repacked to the q4
+// nibble order ([N][K/2] bytes), the norms expanded to one value per 32-k
+// block ([N][K/32], the GEMM's scale grid), the codebook as 256 f16 pairs
+// (codebook[b & 15], codebook[b >> 4]) for byte b of packed indices, and the
+// activation-transform parameters.
+struct spaceslug_cq4_weights {
+    int device = 0;
+    int K = 0, N = 0, gs = 0;
+    bool orthogonal = false;
+    float inv_sqrt = 1.0f;
+    uint32_t* packed = nullptr;
+    float* scales = nullptr;
+    uint32_t* lut = nullptr;
+    float* recip = nullptr;
+    float* lsign = nullptr;
+    float* rsign = nullptr;
+    uint32_t* perm = nullptr;
+    uint16_t* rotation = nullptr;
+};
+
+namespace {
+
+// IEEE binary16 bits -> float (exact).
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+    const uint32_t exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {  // subnormal: normalise
+            int e = -1;
+            uint32_t m = man;
+            do {
+                ++e;
+                m <<= 1;
+            } while ((m & 0x400u) == 0);
+            bits = sign | (static_cast<uint32_t>(127 - 15 - e) << 23) | ((m & 0x3FFu) << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// Codebook index of (n, k) in the stored layout (cactus_x86.cpp:25-53 and
+// dequant_w.comp:45-97: LSB-first per (n, group), or 4-row interleaved panels).
+uint32_t cq4_index(const spaceslug_cq4_matrix& m, bool orth, uint32_t n, uint32_t k) {
+    const uint32_t gs = orth ? m.k : m.group_size, ng = orth ? 1u : m.num_groups;
+    const uint32_t g = k / gs, kk = k % gs, pgb = gs / 2u;
+    if (m.flags & SPACESLUG_CQ4_FLAG_INTERLEAVED_4ROW) {
+        const uint8_t* panel = m.packed_indices + (static_cast<size_t>(n / 4u) * ng + g) * (4u * pgb);
+        const uint8_t b = panel[(kk / 8u) * 16u + (n & 3u) * 4u + (kk & 3u)];
+        return (kk & 4u) ? (b >> 4) : (b & 0xFu);
+    }
+    const uint8_t b = m.packed_indices[(static_cast<size_t>(n) * ng + g) * pgb + kk / 2u];
+    return (b >> ((kk & 1u) * 4u)) & 0xFu;
+}
+
+float cq4_norm(const spaceslug_cq4_matrix& m, bool orth, uint32_t n, uint32_t g) {
+    const bool il = (m.flags & SPACESLUG_CQ4_FLAG_INTERLEAVED_4ROW) != 0;
+    size_t i;
+    if (orth) i = il ? (n / 4u) * 4u + (n & 3u) : n;
+    else i = il ? (static_cast<size_t>(n / 4u) * m.num_groups + g) * 4u + (n & 3u) : static_cast<size_t>(n) * m.num_groups + g;
+    return half_bits_to_float(m.norms[i]);
+}
+
+void run_cq4(const spaceslug_cq4_weights& w, const void* a, void* c, int M, cudaStream_t stream) {
+    DeviceCtx& ctx = ctx_for(current_device());
+    const int K = w.K, N = w.N;
+    Scratch a1(static_cast<size_t>(M) * K * 2, stream);
+    Scratch yf(static_cast<size_t>(M) * N * 4, stream);
+    check_launch(q4::launch_cq4_transform(a, a1.p, w.recip, w.lsign, w.rsign, w.perm, w.rotation, M, K, w.gs,
+                                          w.inv_sqrt, stream),
+                 "cq4 transform");
+    q4::GemmArgs g{};
+    g.halves = q4::gemm_tiles(M, N, 2) >= ctx.sm_count ? 2 : 1;
+    g.sm_count = ctx.sm_count;
+    encode_2d(&g.tmap_x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a1.p, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+              static_cast<uint64_t>(K) * 2, 64, static_cast<uint32_t>(128 * g.halves), CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w.packed, static_cast<uint64_t>(K) / 8,
+              static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    g.tmap_t = g.tmap_x16;  // never read
+    g.scales = w.scales;
+    g.y = static_cast<float*>(yf.p);
+    g.M = M; g.N = N; g.K = K;
+    g.op = q4::Operand16::kF16;
+    g.lut = w.lut;
+    g.status = ctx.status;
+    check_launch(q4::launch_gemm(g, stream), "cq4 gemm launch");
+    check_launch(q4::launch_f32_to_f16(static_cast<const float*>(yf.p), c, static_cast<long long>(M) * N, stream),
+                 "cq4 output cast");
+}
+
+}  // namespace
+
 extern "C" {
 
 int spaceslug_vector_add(const float* left, const float* right, float* output, size_t count) {
@@ -837,5 +937,147 @@ int spaceslug_q4_device_status(int device) {
 uint64_t spaceslug_q4_launch_count(void) { return g_launches.load(); }
 
 const char* spaceslug_last_error(void) { return g_last_error.c_str(); }
+
+int spaceslug_cq4_weights_create(const spaceslug_cq4_matrix* m, int device, spaceslug_cq4_weights** out) {
+    if (!m || !out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (m->bits != 4) return fail(SPACESLUG_INVALID_ARGUMENT, "only 4-bit CQ4 indices are supported");
+    if (!m->codebook || !m->norms || !m->packed_indices) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (m->k == 0 || m->n == 0 || m->k % 32u) return fail(SPACESLUG_INVALID_ARGUMENT, "K must be a positive multiple of 32");
+    const bool orth = (m->flags & SPACESLUG_CQ4_FLAG_ORTHOGONAL) != 0;
+    const bool il = (m->flags & SPACESLUG_CQ4_FLAG_INTERLEAVED_4ROW) != 0;
+    if (il && m->n % 4u) return fail(SPACESLUG_INVALID_ARGUMENT, "INTERLEAVED_4ROW needs N % 4 == 0");
+    if (orth) {
+        if (!m->rotation) return fail(SPACESLUG_INVALID_ARGUMENT, "orthogonal mode needs the rotation");
+    } else {
+        const uint32_t gs = m->group_size;
+        if (gs < 32 || gs > 256 || (gs & (gs - 1))) return fail(SPACESLUG_INVALID_ARGUMENT, "group_size must be 32, 64, 128 or 256");
+        if (m->num_groups == 0 || gs * m->num_groups != m->k) return fail(SPACESLUG_INVALID_ARGUMENT, "K != group_size * num_groups");
+        if (m->permutation)
+            for (uint32_t j = 0; j < gs; ++j)
+                if (m->permutation[j] >= gs) return fail(SPACESLUG_INVALID_ARGUMENT, "permutation entry out of range");
+    }
+    return guarded([&] {
+        check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceCtx& c = ctx_for(device);
+        const uint32_t K = m->k, N = m->n, gs = orth ? K : m->group_size;
+        // host preparation
+        std::vector<uint8_t> packed(static_cast<size_t>(N) * K / 2, 0);
+        if (il) {
+            for (uint32_t n = 0; n < N; ++n)
+                for (uint32_t k = 0; k < K; k += 2)
+                    packed[static_cast<size_t>(n) * K / 2 + k / 2] =
+                        static_cast<uint8_t>(cq4_index(*m, orth, n, k) | (cq4_index(*m, orth, n, k + 1) << 4));
+        } else {
+            std::memcpy(packed.data(), m->packed_indices, packed.size());  // already [N][K/2], low nibble = even k
+        }
+        std::vector<float> scales(static_cast<size_t>(N) * (K / 32));
+        for (uint32_t n = 0; n < N; ++n)
+            for (uint32_t j = 0; j < K / 32; ++j)
+                scales[static_cast<size_t>(n) * (K / 32) + j] = cq4_norm(*m, orth, n, orth ? 0u : (32u * j) / gs);
+        std::vector<uint32_t> lut(256);
+        for (uint32_t b = 0; b < 256; ++b)
+            lut[b] = static_cast<uint32_t>(m->codebook[b & 15u]) | (static_cast<uint32_t>(m->codebook[b >> 4]) << 16);
+        std::vector<float> recip(K, 1.0f);
+        for (uint32_t k = 0; k < K; ++k) {
+            if (m->input_scale_recip) recip[k] = half_bits_to_float(m->input_scale_recip[k]);
+            else if (m->input_scale) recip[k] = 1.0f / half_bits_to_float(m->input_scale[k]);
+        }
+        auto* w = new spaceslug_cq4_weights();
+        w->device = device;
+        w->K = static_cast<int>(K);
+        w->N = static_cast<int>(N);
+        w->gs = static_cast<int>(gs);
+        w->orthogonal = orth;
+        w->inv_sqrt = 1.0f / std::sqrt(static_cast<float>(gs));
+        try {
+            std::lock_guard<std::mutex> lk(c.host_mu);
+            auto upload = [&](auto** dst, const void* src, size_t bytes) {
+                check(cudaMalloc(reinterpret_cast<void**>(dst), bytes), "cudaMalloc cq4");
+                q4up::staged_h2d(device, *dst, src, bytes, c.stream);
+            };
+            upload(&w->packed, packed.data(), packed.size());
+            upload(&w->scales, scales.data(), scales.size() * 4);
+            upload(&w->lut, lut.data(), lut.size() * 4);
+            upload(&w->recip, recip.data(), recip.size() * 4);
+            if (!orth) {
+                std::vector<float> sg(gs);
+                if (m->left_signs) {
+                    for (uint32_t j = 0; j < gs; ++j) sg[j] = static_cast<float>(m->left_signs[j]);
+                    upload(&w->lsign, sg.data(), gs * 4);
+                }
+                if (m->right_signs) {
+                    for (uint32_t j = 0; j < gs; ++j) sg[j] = static_cast<float>(m->right_signs[j]);
+                    upload(&w->rsign, sg.data(), gs * 4);
+                }
+                if (m->permutation) upload(&w->perm, m->permutation, gs * 4);
+            } else {
+                upload(&w->rotation, m->rotation, static_cast<size_t>(K) * K * 2);
+            }
+            check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        } catch (...) {
+            spaceslug_cq4_weights_destroy(w);
+            throw;
+        }
+        *out = w;
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_cq4_matmul(spaceslug_cq4_weights* w, const uint16_t* a, uint16_t* c, uint32_t m, void* stream) {
+    if (!w || !a || !c || m == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer or m == 0");
+    if (m > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "m too large");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        run_cq4(*w, a, c, static_cast<int>(m), static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_cq4_matmul_host(spaceslug_cq4_weights* w, const uint16_t* a, uint16_t* c, uint32_t m) {
+    if (!w || !a || !c || m == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer or m == 0");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        DeviceCtx& ctx = ctx_for(w->device);
+        std::lock_guard<std::mutex> lk(ctx.host_mu);
+        const size_t ab = static_cast<size_t>(m) * w->K * 2, cb = static_cast<size_t>(m) * w->N * 2;
+        Scratch da(ab, ctx.stream), dc(cb, ctx.stream);
+        h2d(da.p, a, ab, ctx.stream);
+        run_cq4(*w, da.p, dc.p, static_cast<int>(m), ctx.stream);
+        d2h(c, dc.p, cb, ctx.stream);
+        check(cudaStreamSynchronize(ctx.stream), "cudaStreamSynchronize");
+        if (take_status(ctx, ctx.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_cq4_transform_host(spaceslug_cq4_weights* w, const uint16_t* a, uint16_t* a_out, uint32_t m) {
+    if (!w || !a || !a_out || m == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer or m == 0");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        DeviceCtx& ctx = ctx_for(w->device);
+        std::lock_guard<std::mutex> lk(ctx.host_mu);
+        const size_t ab = static_cast<size_t>(m) * w->K * 2;
+        Scratch da(ab, ctx.stream), dout(ab, ctx.stream);
+        h2d(da.p, a, ab, ctx.stream);
+        check_launch(q4::launch_cq4_transform(da.p, dout.p, w->recip, w->lsign, w->rsign, w->perm, w->rotation,
+                                              static_cast<int>(m), w->K, w->gs, w->inv_sqrt, ctx.stream),
+                     "cq4 transform");
+        d2h(a_out, dout.p, ab, ctx.stream);
+        check(cudaStreamSynchronize(ctx.stream), "cudaStreamSynchronize");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_cq4_weights_destroy(spaceslug_cq4_weights* w) {
+    if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
+    cudaSetDevice(w->device);
+    for (void* p : {static_cast<void*>(w->packed), static_cast<void*>(w->scales), static_cast<void*>(w->lut),
+                    static_cast<void*>(w->recip), static_cast<void*>(w->lsign), static_cast<void*>(w->rsign),
+                    static_cast<void*>(w->perm), static_cast<void*>(w->rotation)})
+        cudaFree(p);
+    delete w;
+    return SPACESLUG_OK;
+}
 
 }  // extern "C"
