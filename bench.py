@@ -496,6 +496,44 @@ def upload_gpu(args, dist: Dist, torch, session) -> dict:
     return out
 
 
+def cq4_gpu(args, dist: Dist, torch, session, peaks) -> dict:
+    """CQ4 chain (activation transform + codebook-dequant GEMM + fp16 output)
+    at the reference bench's sizes (bench/bench_cq4gemm.cpp:51-55, group size
+    128, 4-bit, interleaved panels with signs and permutation): device time of
+    one call per step from a CUDA graph, L2 flushed before each step."""
+    dev = torch.device("cuda", dist.local)
+    rng = np.random.default_rng(5)
+    f16 = lambda a: np.asarray(a, np.float32).astype(np.float16).view(np.uint16)  # noqa: E731
+    stream = torch.cuda.Stream(device=dev)
+    flush = l2_flush_buffer(torch, dev)
+    out = {}
+    for (M, N, K) in ((1024, 1024, 1024), (1, 512, 512), (1024, 512, 512)):
+        # any byte string is a valid set of 4-bit index panels
+        h = session.cq4_weights(k=K, n=N, group_size=128, num_groups=K // 128, flags=8,
+                                codebook=f16(rng.uniform(-1, 1, 16)), norms=f16(rng.uniform(0.5, 1.5, N * K // 128)),
+                                packed=rng.integers(0, 256, N * K // 2, dtype=np.uint8),
+                                input_scale_recip=f16(rng.uniform(0.5, 1.5, K)),
+                                left_signs=rng.choice(np.array([-1, 1], np.int8), 128),
+                                right_signs=rng.choice(np.array([-1, 1], np.int8), 128),
+                                permutation=rng.permutation(128).astype(np.uint32), device=dist.local)
+        a = (torch.rand((M, K), device=dev) * 2 - 1).to(torch.float16)
+        c = torch.empty((M, N), dtype=torch.float16, device=dev)
+        fn = lambda: h.matmul(a.data_ptr(), c.data_ptr(), M, stream.cuda_stream)  # noqa: E731
+        fn()
+        stream.synchronize()
+        g = capture(torch, stream, fn)
+        time_graph_replays(torch, stream, [g], 5, flush)
+        ms = time_graph_replays(torch, stream, [g], 20, flush)[0] / 20
+        flops = 2.0 * M * N * K
+        out[f"{M}x{N}x{K}"] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2)}
+        del g
+        h.close()
+    out["reference_RX580_1024^3_TFLOPs"] = 1.19
+    out["note"] = "includes the activation transform and the fp16 output cast; L2 flushed before each step"
+    del flush
+    return out
+
+
 def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     """columns of W sharded over the ranks, NCCL all-gather of Y."""
     from spaceslug_b200 import sharding
@@ -589,6 +627,10 @@ def main() -> None:
                 sec["upload"] = upload_gpu(args, dist, torch, session)
             except Exception as exc:  # report, do not hide
                 sec["upload"] = {"error": str(exc)}
+            try:
+                sec["cq4"] = cq4_gpu(args, dist, torch, session, peaks)
+            except Exception as exc:  # report, do not hide
+                sec["cq4"] = {"error": str(exc)}
             line["secondary"] = sec
         if dist.rank == 0 and dist.world == 1:
             line["cpu_baseline"] = cpu_reference_decode(args.cpu_seconds, threads=1)

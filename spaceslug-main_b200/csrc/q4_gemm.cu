@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmap_t, const float* __restrict__ scales,
                    const int* __restrict__ col_exp, const int* __restrict__ row_exp, float* __restrict__ y, int M,
                    int N, int K, const float* __restrict__ lora_b, int rank, float lora_scale, int lora_stages,
-                   const uint32_t* __restrict__ lut, int* __restrict__ status) {
+                   const uint32_t* __restrict__ lut, __half* __restrict__ y16, int* __restrict__ status) {
     using C = Cfg<H>;
     constexpr int ST = C::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -364,7 +364,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[e] = __uint_as_float(r[e]) * rs * cinv;
                     }
                     if (nb >= N) continue;  // warp-uniform
-                    if (row_ok) {
+                    if (row_ok && y16 != nullptr) {
+                        // fp16 output (CQ4): round once, 16 consecutive columns
+                        __half* hrow = y16 + static_cast<size_t>(row) * N;
+                        if ((N % 8) == 0 && nb + 16 <= N) {
+                            uint32_t hp[8];
+#pragma unroll
+                            for (int e = 0; e < 16; e += 2) {
+                                const __half2 h2 = __floats2half2_rn(v[e], v[e + 1]);
+                                hp[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+                            }
+                            *reinterpret_cast<uint4*>(hrow + nb) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+                            *reinterpret_cast<uint4*>(hrow + nb + 8) = make_uint4(hp[4], hp[5], hp[6], hp[7]);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e)
+                                if (nb + e < N) hrow[nb + e] = __float2half_rn(v[e]);
+                        }
+                    } else if (row_ok) {
                         if (vec_ok && nb + 16 <= N) {
 #pragma unroll
                             for (int e = 0; e < 16; e += 4)
@@ -408,7 +425,8 @@ int launch_gemm_t(const GemmArgs& a, int grid, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.tmap_t, a.scales, a.col_exp, a.row_exp, a.y, a.M, a.N,
-                           a.K, a.lora_b, a.rank, a.lora_scale, a.lora_stages, a.lut, a.status);
+                           a.K, a.lora_b, a.rank, a.lora_scale, a.lora_stages, a.lut,
+                           static_cast<__half*>(a.y16), a.status);
     return static_cast<int>(e);
 }
 

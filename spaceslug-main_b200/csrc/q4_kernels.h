@@ -104,6 +104,7 @@ struct GemmArgs {
                               // adds the LoRA term in its epilogue from lora_t
     const uint32_t* lut = nullptr;  // single-CTA kernel, f16 only: CQ4 codebook pairs (256 words); the
                                     // scales are then the norms and W = RN16(codebook[idx] * norm)
+    void* y16 = nullptr;            // single-CTA kernel: fp16 [M][N] output instead of y
     int* status;              // kernel status word (0 = ok)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
@@ -139,6 +140,26 @@ int launch_cq4_transform(const void* a, void* a_out, const float* recip, const f
                          const uint32_t* perm, const void* rotation, int M, int K, int gs, float inv_sqrt,
                          cudaStream_t stream);
 int launch_f32_to_f16(const float* y, void* c, long long count, cudaStream_t stream);
+// CQ4 decode (1 <= M <= 8, M * K * 2 <= 192 KB): C fp16 [M][N] from the
+// indices [N][K/8 words], the expanded norms [N][K/32] and the codebook cbf
+// [16] (fp32).  fused_gs = 0: `a` holds the transformed activations A';
+// fused_gs = group size (32..256): `a` holds the raw activations and every
+// CTA applies the Hadamard transform itself.
+struct Cq4GemvArgs {
+    const void* a;
+    const uint32_t* packed;
+    const float* scales;
+    const float* cbf;
+    const float* recip;
+    const float* lsign;
+    const float* rsign;
+    const uint32_t* perm;
+    float inv_sqrt;
+    int fused_gs;
+    void* c;
+    int M, N, K;
+};
+int launch_cq4_gemv(const Cq4GemvArgs& g, cudaStream_t stream);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream);

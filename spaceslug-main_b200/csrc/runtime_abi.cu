@@ -511,6 +511,7 @@ struct spaceslug_cq4_weights {
     uint32_t* packed = nullptr;
     float* scales = nullptr;
     uint32_t* lut = nullptr;
+    float* cbf = nullptr;  // codebook as fp32 [16] (decode rows)
     float* recip = nullptr;
     float* lsign = nullptr;
     float* rsign = nullptr;
@@ -572,11 +573,22 @@ float cq4_norm(const spaceslug_cq4_matrix& m, bool orth, uint32_t n, uint32_t g)
 void run_cq4(const spaceslug_cq4_weights& w, const void* a, void* c, int M, cudaStream_t stream) {
     DeviceCtx& ctx = ctx_for(current_device());
     const int K = w.K, N = w.N;
+    q4::Cq4GemvArgs dv{a, w.packed, w.scales, w.cbf, w.recip, w.lsign, w.rsign, w.perm, w.inv_sqrt, 0, c, M, N, K};
+    if (M <= 8 && static_cast<long long>(M) * K * 2 <= 192 * 1024 && !w.orthogonal) {
+        // decode rows, Hadamard mode: one kernel (transform per CTA, then one warp per column), fp16 out
+        dv.fused_gs = w.gs;
+        check_launch(q4::launch_cq4_gemv(dv, stream), "cq4 gemv");
+        return;
+    }
     Scratch a1(static_cast<size_t>(M) * K * 2, stream);
-    Scratch yf(static_cast<size_t>(M) * N * 4, stream);
     check_launch(q4::launch_cq4_transform(a, a1.p, w.recip, w.lsign, w.rsign, w.perm, w.rotation, M, K, w.gs,
                                           w.inv_sqrt, stream),
                  "cq4 transform");
+    if (M <= 8 && static_cast<long long>(M) * K * 2 <= 192 * 1024) {
+        dv.a = a1.p;  // orthogonal: the rotation ran as its own kernel
+        check_launch(q4::launch_cq4_gemv(dv, stream), "cq4 gemv");
+        return;
+    }
     q4::GemmArgs g{};
     g.halves = q4::gemm_tiles(M, N, 2) >= ctx.sm_count ? 2 : 1;
     g.sm_count = ctx.sm_count;
@@ -586,14 +598,13 @@ void run_cq4(const spaceslug_cq4_weights& w, const void* a, void* c, int M, cuda
               static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
     g.tmap_t = g.tmap_x16;  // never read
     g.scales = w.scales;
-    g.y = static_cast<float*>(yf.p);
+    g.y = nullptr;
     g.M = M; g.N = N; g.K = K;
     g.op = q4::Operand16::kF16;
     g.lut = w.lut;
+    g.y16 = c;  // fp16 straight from the epilogue
     g.status = ctx.status;
     check_launch(q4::launch_gemm(g, stream), "cq4 gemm launch");
-    check_launch(q4::launch_f32_to_f16(static_cast<const float*>(yf.p), c, static_cast<long long>(M) * N, stream),
-                 "cq4 output cast");
 }
 
 }  // namespace
@@ -999,6 +1010,9 @@ int spaceslug_cq4_weights_create(const spaceslug_cq4_matrix* m, int device, spac
             upload(&w->packed, packed.data(), packed.size());
             upload(&w->scales, scales.data(), scales.size() * 4);
             upload(&w->lut, lut.data(), lut.size() * 4);
+            float cbf[16];
+            for (int i = 0; i < 16; ++i) cbf[i] = half_bits_to_float(m->codebook[i]);
+            upload(&w->cbf, cbf, sizeof(cbf));
             upload(&w->recip, recip.data(), recip.size() * 4);
             if (!orth) {
                 std::vector<float> sg(gs);
@@ -1073,6 +1087,7 @@ int spaceslug_cq4_weights_destroy(spaceslug_cq4_weights* w) {
     if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
     cudaSetDevice(w->device);
     for (void* p : {static_cast<void*>(w->packed), static_cast<void*>(w->scales), static_cast<void*>(w->lut),
+                    static_cast<void*>(w->cbf),
                     static_cast<void*>(w->recip), static_cast<void*>(w->lsign), static_cast<void*>(w->rsign),
                     static_cast<void*>(w->perm), static_cast<void*>(w->rotation)})
         cudaFree(p);

@@ -49,6 +49,9 @@ def test_reference_fixtures(session, cuda, spec):
     (37, 96, 32, 8, False, True, False),      # smallest group
     (130, 132, 256, 2, True, True, False),    # largest group
     (96, 128, 256, 1, True, False, True),     # orthogonal, interleaved lm_head layout
+    (8, 200, 128, 4, False, True, False),     # decode kernel, 8 rows, ragged column block
+    (5, 64, 256, 2, True, False, False),      # decode kernel, 5 rows
+    (1, 64, 256, 1, False, False, True),      # decode kernel after the orthogonal transform
 ])
 def test_random_shapes_match_the_oracle(session, cuda, M, N, gs, ng, il, sp, orth):
     fx = cq4.random_fixture(M, N, gs, ng, il, sp, orth, seed=M + N + gs)
