@@ -130,6 +130,40 @@ int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, 
 int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m);
 int spaceslug_q4_weights_destroy(spaceslug_q4_weights* w);
 
+/* LoRA training on the handle's adapter, for the fused forward
+ *   Y = X * dequant(W) + s * (X * A) * B,  s = alpha / rank, W frozen:
+ *   dB = s * (X A)^T dY  [rank x (col_end-col_begin)],  dA = s * X^T (dY B^T)  [k x rank],
+ * the reference's lora_gradients (vulkan-runtime/src/api/lora_gradients_api.h:4-6,
+ * s = 1 there) for any k, n and rank <= 64.  x [m x k] and dy [m x (col_end -
+ * col_begin)] are device pointers; asynchronous on `stream`.  For a column
+ * shard, dA is this shard's partial sum: the caller all-reduces it over the
+ * shards.  The gradients stay in the handle until the next backward. */
+int spaceslug_q4_weights_lora_backward(spaceslug_q4_weights* w, const float* x, const float* dy, uint32_t m,
+                                       void* stream);
+/* A -= lr * dA, B -= lr * dB (lora_sgd_api.h:4-6), in place on the device. */
+int spaceslug_q4_weights_lora_sgd(spaceslug_q4_weights* w, float learning_rate, void* stream);
+/* AdamW with decoupled weight decay and bias-corrected moments (kept in the
+ * handle; set_lora resets them):  m = b1 m + (1-b1) g,  v = b2 v + (1-b2) g^2,
+ * p -= lr * ((m / (1-b1^t)) / (sqrt(v / (1-b2^t)) + eps) + wd * p). */
+int spaceslug_q4_weights_lora_adamw(spaceslug_q4_weights* w, float learning_rate, float beta1, float beta2, float eps,
+                                    float weight_decay, void* stream);
+/* Host copies of the adapter and its last gradients (any output may be NULL);
+ * synchronises the device. */
+int spaceslug_q4_weights_get_lora(const spaceslug_q4_weights* w, float* a_out, float* b_out, float* da_out,
+                                  float* db_out);
+
+/* The reference's hidden-64 training ABI, same contracts and return codes:
+ * dA = X^T dY B^T and dB = (X A)^T dY for X/dY [m x 64], A [64 x rank],
+ * B [rank x 64], 1 <= m <= 128, 1 <= rank <= 8 (lora_gradients_api.h:4-6);
+ * A -= lr dA, B -= lr dB (lora_sgd_api.h:4-6); and one training step: delta
+ * forward into y, gradients at the old A/B, SGD (lora_train_api.h:4-10).
+ * Host pointers, synchronous. */
+int spaceslug_lora_gradients(const float* x, const float* dy, const float* a, const float* b, float* da, float* db,
+                             uint32_t m, uint32_t rank);
+int spaceslug_lora_sgd(float* a, float* b, const float* da, const float* db, float learning_rate, uint32_t rank);
+int spaceslug_lora_train_step(const float* x, const float* dy, float* a, float* b, float* y, float learning_rate,
+                              uint32_t m, uint32_t rank);
+
 /* No counterpart in the reference.  The decode GEMV with the fused LoRA term
  * (device pointers, asynchronous on `stream`, same result as
  * spaceslug_q4gemm_device with the same arguments) for callers that cannot

@@ -57,6 +57,14 @@ _SIGNATURES = {
     "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
     "spaceslug_last_error": ([], ctypes.c_char_p),
+    "spaceslug_lora_gradients": ([_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32], ctypes.c_int),
+    "spaceslug_lora_sgd": ([_f32p, _f32p, _f32p, _f32p, ctypes.c_float, _u32], ctypes.c_int),
+    "spaceslug_lora_train_step": ([_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float, _u32, _u32], ctypes.c_int),
+    "spaceslug_q4_weights_lora_backward": ([_vp, _vp, _vp, _u32, _vp], ctypes.c_int),
+    "spaceslug_q4_weights_lora_sgd": ([_vp, ctypes.c_float, _vp], ctypes.c_int),
+    "spaceslug_q4_weights_lora_adamw": ([_vp, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                         ctypes.c_float, _vp], ctypes.c_int),
+    "spaceslug_q4_weights_get_lora": ([_vp, _f32p, _f32p, _f32p, _f32p], ctypes.c_int),
     "spaceslug_cq4_weights_create": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
     "spaceslug_cq4_matmul": ([_vp, _vp, _vp, _u32, _vp], ctypes.c_int),
     "spaceslug_cq4_matmul_host": ([_vp, _vp, _vp, _u32], ctypes.c_int),
@@ -76,6 +84,8 @@ _CAPABILITIES = {
     "spaceslug_q4_weights_create": "q4_weights_resident",
     "spaceslug_q4_weights_create_logical": "q4_weights_device_pack",
     "spaceslug_cq4_matmul": "cq4_quant_matmul",
+    "spaceslug_lora_train_step": "lora_train_step_abi",
+    "spaceslug_q4_weights_lora_backward": "lora_training",
 }
 
 
@@ -233,6 +243,30 @@ class BackendSession:
                 device: int = 0) -> "Q4Weights":
         return Q4Weights(self, packed, scales, k, n, col_begin, n if col_end is None else col_end, device)
 
+    def lora_gradients(self, x, dy, a, b, m: int, rank: int):
+        """The reference's hidden-64 spaceslug_lora_gradients: (dA [64, r], dB [r, 64])."""
+        xx, yy, aa, bb = (_arr(v, np.float32) for v in (x, dy, a, b))
+        da, db = np.empty(64 * rank, np.float32), np.empty(rank * 64, np.float32)
+        self._call("spaceslug_lora_gradients", _p(xx, _f32p), _p(yy, _f32p), _p(aa, _f32p), _p(bb, _f32p),
+                   _p(da, _f32p), _p(db, _f32p), m, rank)
+        return da.reshape(64, rank), db.reshape(rank, 64)
+
+    def lora_sgd(self, a, b, da, db, learning_rate: float, rank: int):
+        aa, bb = _arr(a, np.float32).copy(), _arr(b, np.float32).copy()
+        ga, gb = _arr(da, np.float32), _arr(db, np.float32)
+        self._call("spaceslug_lora_sgd", _p(aa, _f32p), _p(bb, _f32p), _p(ga, _f32p), _p(gb, _f32p),
+                   float(learning_rate), rank)
+        return aa, bb
+
+    def lora_train_step(self, x, dy, a, b, learning_rate: float, m: int, rank: int):
+        """(y [m, 64], new A, new B) of the reference's spaceslug_lora_train_step."""
+        xx, yy = _arr(x, np.float32), _arr(dy, np.float32)
+        aa, bb = _arr(a, np.float32).copy(), _arr(b, np.float32).copy()
+        y = np.empty(m * 64, np.float32)
+        self._call("spaceslug_lora_train_step", _p(xx, _f32p), _p(yy, _f32p), _p(aa, _f32p), _p(bb, _f32p),
+                   _p(y, _f32p), float(learning_rate), m, rank)
+        return y.reshape(m, 64), aa, bb
+
     def cq4_weights(self, *, k: int, n: int, group_size: int, num_groups: int, flags: int, codebook, norms, packed,
                     input_scale=None, input_scale_recip=None, left_signs=None, right_signs=None, permutation=None,
                     rotation=None, bits: int = 4, device: int = 0) -> "CQ4Weights":
@@ -286,6 +320,28 @@ class Q4Weights:
 
     def run(self, x: int, y: int, m: int, stream: int = 0) -> None:
         self.session._call("spaceslug_q4_weights_run", self.handle, x, y, m, stream or None)
+
+    # ---- LoRA training (device pointers, asynchronous) ----
+    def lora_backward(self, x: int, dy: int, m: int, stream: int = 0) -> None:
+        self.session._call("spaceslug_q4_weights_lora_backward", self.handle, x, dy, m, stream or None)
+
+    def lora_sgd(self, learning_rate: float, stream: int = 0) -> None:
+        self.session._call("spaceslug_q4_weights_lora_sgd", self.handle, float(learning_rate), stream or None)
+
+    def lora_adamw(self, learning_rate: float, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
+                   weight_decay: float = 0.0, stream: int = 0) -> None:
+        self.session._call("spaceslug_q4_weights_lora_adamw", self.handle, float(learning_rate), float(beta1),
+                           float(beta2), float(eps), float(weight_decay), stream or None)
+
+    def get_lora(self, rank: int, grads: bool = False):
+        """(A [k, r], B [r, n]) and, with grads, (dA, dB) as well."""
+        a = np.empty((self.k, rank), np.float32)
+        b = np.empty((rank, self.n), np.float32)
+        da = np.empty_like(a) if grads else None
+        db = np.empty_like(b) if grads else None
+        self.session._call("spaceslug_q4_weights_get_lora", self.handle, _p(a, _f32p), _p(b, _f32p),
+                           None if da is None else _p(da, _f32p), None if db is None else _p(db, _f32p))
+        return (a, b, da, db) if grads else (a, b)
 
     def run_host(self, x) -> np.ndarray:
         xx = _arr(x, np.float32)

@@ -160,6 +160,24 @@ struct Cq4GemvArgs {
     int M, N, K;
 };
 int launch_cq4_gemv(const Cq4GemvArgs& g, cudaStream_t stream);
+// LoRA training (lora_train.cu): dB = s T^T dY, dA = s X^T (dY B^T) with
+// T = X A, for X [M][K], dY [M][N], A [K][r], B [r][N] (device, fp32).
+struct LoraBackwardArgs {
+    const float* x;
+    const float* dy;
+    const float* lora_a;
+    const float* lora_b;
+    float* da;       // [K][r]
+    float* db;       // [r][N]
+    float* scratch;  // lora_backward_scratch_floats(M, K, N, r) floats
+    int M, K, N, rank;
+    float scale;
+};
+size_t lora_backward_scratch_floats(int M, int K, int N, int rank);
+int launch_lora_backward(const LoraBackwardArgs& a, cudaStream_t stream);
+int launch_sgd(float* p, const float* g, float lr, long long count, cudaStream_t stream);
+int launch_adamw(float* p, const float* g, float* m1, float* m2, float lr, float beta1, float beta2, float eps,
+                 float wd, int step, long long count, cudaStream_t stream);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream);

@@ -496,6 +496,11 @@ struct spaceslug_q4_weights {
     float* lora_b = nullptr;
     int rank = 0;
     float alpha = 0.0f;
+    // training state (allocated on first use, reset by set_lora)
+    float* lora_da = nullptr;
+    float* lora_db = nullptr;
+    float* adam = nullptr;  // first and second moments of A then of B: 2 * (K*r + r*N)
+    int adam_step = 0;
 };
 
 // CQ4 (Cactus-Quants) matrix on one device: the indices repacked to the q4
@@ -856,7 +861,11 @@ int spaceslug_q4_weights_set_lora(spaceslug_q4_weights* w, const float* lora_a, 
         check(cudaSetDevice(w->device), "cudaSetDevice");
         cudaFree(w->lora_a);
         cudaFree(w->lora_b);
-        w->lora_a = w->lora_b = nullptr;
+        cudaFree(w->lora_da);
+        cudaFree(w->lora_db);
+        cudaFree(w->adam);
+        w->lora_a = w->lora_b = w->lora_da = w->lora_db = w->adam = nullptr;
+        w->adam_step = 0;
         w->rank = 0;
         if (rank == 0) return SPACESLUG_OK;
         // lora_b is the full [rank x n_total] matrix; keep the handle's columns.
@@ -913,8 +922,175 @@ int spaceslug_q4_weights_destroy(spaceslug_q4_weights* w) {
     cudaFree(w->col_exp);
     cudaFree(w->lora_a);
     cudaFree(w->lora_b);
+    cudaFree(w->lora_da);
+    cudaFree(w->lora_db);
+    cudaFree(w->adam);
     delete w;
     return SPACESLUG_OK;
+}
+
+int spaceslug_lora_gradients(const float* x, const float* dy, const float* a, const float* b, float* da, float* db,
+                             uint32_t m, uint32_t rank) {
+    // Same checks as vulkan-runtime/src/api/lora_gradients_api.cpp:23.
+    if (!x || !dy || !a || !b || !da || !db || m == 0 || m > 128 || rank == 0 || rank > 8)
+        return fail(SPACESLUG_INVALID_ARGUMENT, "invalid arguments (need 1<=m<=128, 1<=rank<=8, non-null)");
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const int M = static_cast<int>(m), r = static_cast<int>(rank);
+        const size_t xb = static_cast<size_t>(M) * 64 * 4, pb = 64u * rank * 4;
+        Scratch dx(xb, c.stream), ddy(xb, c.stream), dA(pb, c.stream), dB(pb, c.stream), gA(pb, c.stream),
+            gB(pb, c.stream), sc(q4::lora_backward_scratch_floats(M, 64, 64, r) * 4, c.stream);
+        h2d(dx.p, x, xb, c.stream);
+        h2d(ddy.p, dy, xb, c.stream);
+        h2d(dA.p, a, pb, c.stream);
+        h2d(dB.p, b, pb, c.stream);
+        q4::LoraBackwardArgs g{static_cast<float*>(dx.p), static_cast<float*>(ddy.p), static_cast<float*>(dA.p),
+                               static_cast<float*>(dB.p), static_cast<float*>(gA.p), static_cast<float*>(gB.p),
+                               static_cast<float*>(sc.p), M, 64, 64, r, 1.0f};
+        check_launch(q4::launch_lora_backward(g, c.stream), "lora backward");
+        d2h(da, gA.p, pb, c.stream);
+        d2h(db, gB.p, pb, c.stream);
+        check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_lora_sgd(float* a, float* b, const float* da, const float* db, float learning_rate, uint32_t rank) {
+    // Same checks as vulkan-runtime/src/api/lora_sgd_api.cpp:23.
+    if (!a || !b || !da || !db || !(learning_rate > 0.0f) || rank == 0 || rank > 8)
+        return fail(SPACESLUG_INVALID_ARGUMENT, "invalid arguments (need learning_rate > 0, 1<=rank<=8, non-null)");
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const size_t pb = 64u * rank * 4;
+        Scratch dA(pb, c.stream), dB(pb, c.stream), gA(pb, c.stream), gB(pb, c.stream);
+        h2d(dA.p, a, pb, c.stream);
+        h2d(dB.p, b, pb, c.stream);
+        h2d(gA.p, da, pb, c.stream);
+        h2d(gB.p, db, pb, c.stream);
+        check_launch(q4::launch_sgd(static_cast<float*>(dA.p), static_cast<float*>(gA.p), learning_rate, 64 * rank,
+                                    c.stream),
+                     "sgd A");
+        check_launch(q4::launch_sgd(static_cast<float*>(dB.p), static_cast<float*>(gB.p), learning_rate, 64 * rank,
+                                    c.stream),
+                     "sgd B");
+        d2h(a, dA.p, pb, c.stream);
+        d2h(b, dB.p, pb, c.stream);
+        check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_lora_train_step(const float* x, const float* dy, float* a, float* b, float* y, float learning_rate,
+                              uint32_t m, uint32_t rank) {
+    // Same checks as vulkan-runtime/src/api/lora_train_api.cpp:10; the same
+    // sequence (delta forward, gradients at the old A/B, SGD) on the device.
+    if (!x || !dy || !a || !b || !y || !(learning_rate > 0.0f) || m == 0 || m > 128 || rank == 0 || rank > 8)
+        return fail(SPACESLUG_INVALID_ARGUMENT, "invalid arguments (need learning_rate > 0, 1<=m<=128, 1<=rank<=8)");
+    return guarded([&] {
+        DeviceCtx& c = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        const int M = static_cast<int>(m), r = static_cast<int>(rank);
+        const size_t xb = static_cast<size_t>(M) * 64 * 4, pb = 64u * rank * 4;
+        Scratch dx(xb, c.stream), ddy(xb, c.stream), dyo(xb, c.stream), dA(pb, c.stream), dB(pb, c.stream),
+            gA(pb, c.stream), gB(pb, c.stream), sc(q4::lora_backward_scratch_floats(M, 64, 64, r) * 4, c.stream);
+        h2d(dx.p, x, xb, c.stream);
+        h2d(ddy.p, dy, xb, c.stream);
+        h2d(dA.p, a, pb, c.stream);
+        h2d(dB.p, b, pb, c.stream);
+        check_launch(q4::launch_lora_delta64(static_cast<float*>(dx.p), static_cast<float*>(dA.p),
+                                             static_cast<float*>(dB.p), static_cast<float*>(dyo.p), M, r, c.stream),
+                     "lora_delta launch");
+        q4::LoraBackwardArgs g{static_cast<float*>(dx.p), static_cast<float*>(ddy.p), static_cast<float*>(dA.p),
+                               static_cast<float*>(dB.p), static_cast<float*>(gA.p), static_cast<float*>(gB.p),
+                               static_cast<float*>(sc.p), M, 64, 64, r, 1.0f};
+        check_launch(q4::launch_lora_backward(g, c.stream), "lora backward");
+        check_launch(q4::launch_sgd(static_cast<float*>(dA.p), static_cast<float*>(gA.p), learning_rate, 64 * r, c.stream),
+                     "sgd A");
+        check_launch(q4::launch_sgd(static_cast<float*>(dB.p), static_cast<float*>(gB.p), learning_rate, 64 * r, c.stream),
+                     "sgd B");
+        d2h(y, dyo.p, xb, c.stream);
+        d2h(a, dA.p, pb, c.stream);
+        d2h(b, dB.p, pb, c.stream);
+        check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_lora_backward(spaceslug_q4_weights* w, const float* x, const float* dy, uint32_t m,
+                                       void* stream) {
+    if (!w || !x || !dy || m == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer or m == 0");
+    if (w->rank == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "no LoRA adapter attached");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const size_t pa = static_cast<size_t>(w->K) * w->rank * 4, pbb = static_cast<size_t>(w->rank) * w->N * 4;
+        if (!w->lora_da) check(cudaMalloc(&w->lora_da, pa), "cudaMalloc dA");
+        if (!w->lora_db) check(cudaMalloc(&w->lora_db, pbb), "cudaMalloc dB");
+        Scratch sc(q4::lora_backward_scratch_floats(static_cast<int>(m), w->K, w->N, w->rank) * 4, s);
+        q4::LoraBackwardArgs g{x, dy, w->lora_a, w->lora_b, w->lora_da, w->lora_db, static_cast<float*>(sc.p),
+                               static_cast<int>(m), w->K, w->N, w->rank, w->alpha / static_cast<float>(w->rank)};
+        check_launch(q4::launch_lora_backward(g, s), "lora backward");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_lora_sgd(spaceslug_q4_weights* w, float learning_rate, void* stream) {
+    if (!w || !(learning_rate > 0.0f)) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle or learning_rate <= 0");
+    if (!w->lora_da || !w->lora_db) return fail(SPACESLUG_INVALID_ARGUMENT, "no gradients: run the backward first");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        check_launch(q4::launch_sgd(w->lora_a, w->lora_da, learning_rate, static_cast<long long>(w->K) * w->rank, s),
+                     "sgd A");
+        check_launch(q4::launch_sgd(w->lora_b, w->lora_db, learning_rate, static_cast<long long>(w->rank) * w->N, s),
+                     "sgd B");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_lora_adamw(spaceslug_q4_weights* w, float learning_rate, float beta1, float beta2, float eps,
+                                    float weight_decay, void* stream) {
+    if (!w || !(learning_rate > 0.0f) || !(beta1 >= 0.0f && beta1 < 1.0f) || !(beta2 >= 0.0f && beta2 < 1.0f) ||
+        !(eps > 0.0f) || !(weight_decay >= 0.0f))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "bad AdamW hyper-parameters");
+    if (!w->lora_da || !w->lora_db) return fail(SPACESLUG_INVALID_ARGUMENT, "no gradients: run the backward first");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const long long na = static_cast<long long>(w->K) * w->rank, nb = static_cast<long long>(w->rank) * w->N;
+        if (!w->adam) {
+            check(cudaMalloc(&w->adam, static_cast<size_t>(2 * (na + nb)) * 4), "cudaMalloc AdamW moments");
+            check(cudaMemsetAsync(w->adam, 0, static_cast<size_t>(2 * (na + nb)) * 4, s), "cudaMemset moments");
+        }
+        ++w->adam_step;
+        check_launch(q4::launch_adamw(w->lora_a, w->lora_da, w->adam, w->adam + na, learning_rate, beta1, beta2, eps,
+                                      weight_decay, w->adam_step, na, s),
+                     "adamw A");
+        check_launch(q4::launch_adamw(w->lora_b, w->lora_db, w->adam + 2 * na, w->adam + 2 * na + nb, learning_rate,
+                                      beta1, beta2, eps, weight_decay, w->adam_step, nb, s),
+                     "adamw B");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_get_lora(const spaceslug_q4_weights* w, float* a_out, float* b_out, float* da_out,
+                                  float* db_out) {
+    if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
+    if (w->rank == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "no LoRA adapter attached");
+    if ((da_out || db_out) && (!w->lora_da || !w->lora_db))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "no gradients: run the backward first");
+    return guarded([&] {
+        check(cudaSetDevice(w->device), "cudaSetDevice");
+        check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        const size_t pa = static_cast<size_t>(w->K) * w->rank * 4, pbb = static_cast<size_t>(w->rank) * w->N * 4;
+        if (a_out) check(cudaMemcpy(a_out, w->lora_a, pa, cudaMemcpyDeviceToHost), "D2H A");
+        if (b_out) check(cudaMemcpy(b_out, w->lora_b, pbb, cudaMemcpyDeviceToHost), "D2H B");
+        if (da_out) check(cudaMemcpy(da_out, w->lora_da, pa, cudaMemcpyDeviceToHost), "D2H dA");
+        if (db_out) check(cudaMemcpy(db_out, w->lora_db, pbb, cudaMemcpyDeviceToHost), "D2H dB");
+        return SPACESLUG_OK;
+    });
 }
 
 int spaceslug_q4_set_operand_type(int type) {
