@@ -534,6 +534,29 @@ def cq4_gpu(args, dist: Dist, torch, session, peaks) -> dict:
     return out
 
 
+def sgemm_gpu(args, dist: Dist, torch, session) -> dict:
+    """spaceslug_sgemm_device (cuBLAS fp32 FMA) at the reference bench's 1024^3
+    (bench/bench_cq4gemm.cpp:39: 3.21 TFLOP/s fp32 baseline on the RX580)."""
+    dev = torch.device("cuda", dist.local)
+    stream = torch.cuda.Stream(device=dev)
+    out = {}
+    for n in (1024, 4096):
+        a = torch.randn((n, n), device=dev)
+        b = torch.randn((n, n), device=dev)
+        c = torch.empty((n, n), device=dev)
+        fn = lambda: session.sgemm_device(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, n, n, stream.cuda_stream)  # noqa: E731
+        fn()
+        stream.synchronize()
+        g = capture(torch, stream, fn)
+        flush = l2_flush_buffer(torch, dev)
+        time_graph_replays(torch, stream, [g], 3, flush)
+        ms = time_graph_replays(torch, stream, [g], 10, flush)[0] / 10
+        out[f"{n}^3"] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(2.0 * n ** 3 / (ms * 1e-3) / 1e12, 2)}
+        del g, flush
+    out["reference_RX580_1024^3_TFLOPs"] = 3.21
+    return out
+
+
 def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     """columns of W sharded over the ranks, NCCL all-gather of Y."""
     from spaceslug_b200 import sharding
@@ -631,6 +654,10 @@ def main() -> None:
                 sec["cq4"] = cq4_gpu(args, dist, torch, session, peaks)
             except Exception as exc:  # report, do not hide
                 sec["cq4"] = {"error": str(exc)}
+            try:
+                sec["sgemm"] = sgemm_gpu(args, dist, torch, session)
+            except Exception as exc:  # report, do not hide
+                sec["sgemm"] = {"error": str(exc)}
             line["secondary"] = sec
         if dist.rank == 0 and dist.world == 1:
             line["cpu_baseline"] = cpu_reference_decode(args.cpu_seconds, threads=1)

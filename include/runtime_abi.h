@@ -209,6 +209,16 @@ uint64_t spaceslug_q4_launch_count(void);
 /* Human-readable description of the last non-zero return code on this thread. */
 const char* spaceslug_last_error(void);
 
+/* fp32 row-major C[m x n] = A[m x k] * B[k x n], host pointers, synchronous:
+ * the reference's spaceslug_sgemm (vulkan-runtime/src/api/sgemm_api.h:5-9), same
+ * checks (M, N % 64 == 0, K % 32 == 0) and codes; *max_relative_error is set
+ * to 0 as the reference does.  A plain library GEMM: cuBLAS SGEMM with fp32
+ * FMA (no TF32), cuBLAS loaded on first use. */
+int spaceslug_sgemm(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
+                    float* max_relative_error);
+/* Same product for device pointers, any positive m, n, k, asynchronous on `stream`. */
+int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, void* stream);
+
 /* ---- CQ4 (Cactus-Quants) ------------------------------------------------
  * C[M x N] = A'[M x K] * W'^T in fp16 storage with fp32 accumulation, where
  * A' is the activation transformed into the code basis and

@@ -57,6 +57,8 @@ _SIGNATURES = {
     "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
     "spaceslug_last_error": ([], ctypes.c_char_p),
+    "spaceslug_sgemm": ([_f32p, _f32p, _f32p, _u32, _u32, _u32, _f32p], ctypes.c_int),
+    "spaceslug_sgemm_device": ([_vp, _vp, _vp, _u32, _u32, _u32, _vp], ctypes.c_int),
     "spaceslug_lora_gradients": ([_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32], ctypes.c_int),
     "spaceslug_lora_sgd": ([_f32p, _f32p, _f32p, _f32p, ctypes.c_float, _u32], ctypes.c_int),
     "spaceslug_lora_train_step": ([_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float, _u32, _u32], ctypes.c_int),
@@ -85,6 +87,7 @@ _CAPABILITIES = {
     "spaceslug_q4_weights_create_logical": "q4_weights_device_pack",
     "spaceslug_cq4_matmul": "cq4_quant_matmul",
     "spaceslug_lora_train_step": "lora_train_step_abi",
+    "spaceslug_sgemm": "sgemm",
     "spaceslug_q4_weights_lora_backward": "lora_training",
 }
 
@@ -242,6 +245,19 @@ class BackendSession:
     def weights(self, packed, scales, k: int, n: int, col_begin: int = 0, col_end: int | None = None,
                 device: int = 0) -> "Q4Weights":
         return Q4Weights(self, packed, scales, k, n, col_begin, n if col_end is None else col_end, device)
+
+    def sgemm(self, a, b) -> np.ndarray:
+        """The reference's spaceslug_sgemm: fp32 C = A B (M, N % 64, K % 32), host arrays."""
+        aa, bb = _arr(a, np.float32), _arr(b, np.float32)
+        m, k = aa.shape
+        n = bb.shape[1]
+        c = np.empty((m, n), np.float32)
+        err = ctypes.c_float(-1.0)
+        self._call("spaceslug_sgemm", _p(aa, _f32p), _p(bb, _f32p), _p(c, _f32p), m, n, k, ctypes.byref(err))
+        return c
+
+    def sgemm_device(self, a: int, b: int, c: int, m: int, n: int, k: int, stream: int = 0) -> None:
+        self._call("spaceslug_sgemm_device", a, b, c, m, n, k, stream or None)
 
     def lora_gradients(self, x, dy, a, b, m: int, rank: int):
         """The reference's hidden-64 spaceslug_lora_gradients: (dA [64, r], dB [r, 64])."""

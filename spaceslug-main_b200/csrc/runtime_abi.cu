@@ -6,8 +6,10 @@
 // Error behaviour mirrors vulkan-runtime/src/api/lora_delta_api.cpp:42-85:
 // arguments are checked first (return 1), every device failure returns 2, and
 // nothing throws across the ABI (catch (...) -> 2).
+#include <cublas_v2.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 
 #include <algorithm>
 #include <array>
@@ -63,6 +65,8 @@ struct DeviceCtx {
     std::mutex host_mu;             // serialises use of `stream` by host entry points
     int max_pairs[2] = {-1, -1};    // co-resident CTA pairs of the pair GEMM, per operand type
     std::mutex pair_mu;
+    cublasHandle_t blas = nullptr;  // spaceslug_sgemm (created on first use)
+    std::mutex blas_mu;
 };
 
 constexpr int kMaxDevices = 64;
@@ -139,6 +143,45 @@ q4::Operand16 operand_type() {
         if (e && std::strcmp(e, "f16") == 0) g_operand.store(static_cast<int>(q4::Operand16::kF16));
     });
     return static_cast<q4::Operand16>(g_operand.load());
+}
+
+// cuBLAS for the plain fp32 GEMM (spaceslug_sgemm), loaded on first use so the
+// library has no link-time dependency on it.
+struct BlasApi {
+    decltype(&cublasCreate_v2) create = nullptr;
+    decltype(&cublasSetStream_v2) set_stream = nullptr;
+    decltype(&cublasSetMathMode) set_math = nullptr;
+    decltype(&cublasSgemm_v2) sgemm = nullptr;
+};
+const BlasApi& blas_api() {
+    static BlasApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_LOCAL);
+        if (!h) return;
+        api.create = reinterpret_cast<decltype(api.create)>(dlsym(h, "cublasCreate_v2"));
+        api.set_stream = reinterpret_cast<decltype(api.set_stream)>(dlsym(h, "cublasSetStream_v2"));
+        api.set_math = reinterpret_cast<decltype(api.set_math)>(dlsym(h, "cublasSetMathMode"));
+        api.sgemm = reinterpret_cast<decltype(api.sgemm)>(dlsym(h, "cublasSgemm_v2"));
+    });
+    if (!api.create || !api.set_stream || !api.set_math || !api.sgemm) throw CudaError("libcublas.so.12 is unavailable");
+    return api;
+}
+
+// C[m x n] = A[m x k] B[k x n], fp32 row-major, on `stream`: the column-major
+// product C^T = B^T A^T, fp32 FMA (no TF32).
+void run_sgemm(DeviceCtx& c, const float* a, const float* b, float* cm, int m, int n, int k, cudaStream_t stream) {
+    const BlasApi& api = blas_api();
+    std::lock_guard<std::mutex> lk(c.blas_mu);
+    if (!c.blas) {
+        if (api.create(&c.blas) != CUBLAS_STATUS_SUCCESS) throw CudaError("cublasCreate failed");
+        api.set_math(c.blas, CUBLAS_DEFAULT_MATH);
+    }
+    if (api.set_stream(c.blas, stream) != CUBLAS_STATUS_SUCCESS) throw CudaError("cublasSetStream failed");
+    const float one = 1.0f, zero = 0.0f;
+    if (api.sgemm(c.blas, CUBLAS_OP_N, CUBLAS_OP_N, n, m, k, &one, b, n, a, k, &zero, cm, n) != CUBLAS_STATUS_SUCCESS)
+        throw CudaError("cublasSgemm failed");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 // Stream-ordered scratch buffer released on the same stream at scope exit.
@@ -1124,6 +1167,39 @@ int spaceslug_q4_device_status(int device) {
 uint64_t spaceslug_q4_launch_count(void) { return g_launches.load(); }
 
 const char* spaceslug_last_error(void) { return g_last_error.c_str(); }
+
+int spaceslug_sgemm(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
+                    float* max_relative_error) {
+    // Same checks as vulkan-runtime/src/api/sgemm_api.cpp:25.
+    if (!a || !b || !c || !max_relative_error || m == 0 || n == 0 || k == 0 || m % 64 || n % 64 || k % 32)
+        return fail(SPACESLUG_INVALID_ARGUMENT, "need non-null pointers, M, N % 64 == 0 and K % 32 == 0");
+    return guarded([&] {
+        DeviceCtx& ctx = ctx_for(current_device());
+        std::lock_guard<std::mutex> lk(ctx.host_mu);
+        const size_t ab = static_cast<size_t>(m) * k * 4, bb = static_cast<size_t>(k) * n * 4,
+                     cb = static_cast<size_t>(m) * n * 4;
+        Scratch da(ab, ctx.stream), db(bb, ctx.stream), dc(cb, ctx.stream);
+        q4up::staged_h2d(current_device(), da.p, a, ab, ctx.stream);
+        q4up::staged_h2d(current_device(), db.p, b, bb, ctx.stream);
+        run_sgemm(ctx, static_cast<float*>(da.p), static_cast<float*>(db.p), static_cast<float*>(dc.p),
+                  static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), ctx.stream);
+        d2h(c, dc.p, cb, ctx.stream);
+        check(cudaStreamSynchronize(ctx.stream), "cudaStreamSynchronize");
+        *max_relative_error = 0.0f;  // the reference reports 0 as well (sgemm_api.cpp:54)
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, void* stream) {
+    if (!a || !b || !c || m == 0 || n == 0 || k == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer or zero dimension");
+    if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "dimension too large");
+    return guarded([&] {
+        DeviceCtx& ctx = ctx_for(current_device());
+        run_sgemm(ctx, a, b, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                  static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
 
 int spaceslug_cq4_weights_create(const spaceslug_cq4_matrix* m, int device, spaceslug_cq4_weights** out) {
     if (!m || !out) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");

@@ -104,6 +104,12 @@ def test_invalid_arguments_return_1_before_device_work(session):
     assert wl(w.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), _f(s), 48, 4, 0, 4, 0, ctypes.byref(h)) == 1  # K % 32
     assert wl(w.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), _f(s), 32, 4, 3, 3, 0, ctypes.byref(h)) == 1
     assert session.raw("spaceslug_q4_weights_export")(None, _u(p), _f(s)) == 1
+    sg = session.raw("spaceslug_sgemm")
+    e = ctypes.c_float()
+    assert sg(_f(x), _f(x), _f(y), 64, 64, 48, ctypes.byref(e)) == 1   # K % 32 (sgemm_api.cpp:25)
+    assert sg(_f(x), _f(x), _f(y), 32, 64, 32, ctypes.byref(e)) == 1   # M % 64
+    assert sg(_f(x), _f(x), _f(y), 64, 64, 32, None) == 1
+    assert session.raw("spaceslug_sgemm_device")(None, None, None, 1, 1, 1, None) == 1
     assert session.raw("spaceslug_q4_weights_run")(None, 16, 16, 1, None) == 1
     assert session.raw("spaceslug_q4_weights_destroy")(None) == 1
     assert session.raw("spaceslug_q4_set_operand_type")(7) == -1

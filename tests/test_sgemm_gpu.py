@@ -1,0 +1,56 @@
+"""GPU: spaceslug_sgemm, the reference's fp32 GEMM ABI
+(vulkan-runtime/src/api/sgemm_api.h:5-9), at its own test case
+(tests/test_sgemm.cpp: 256^3, LCG inputs, |gpu - ref| <= 1e-3 * max(1, |ref|))."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from spaceslug_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(c, a, b, tol=1e-3):
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    err = np.abs(c - ref) / np.maximum(1.0, np.abs(ref))
+    assert float(err.max()) <= tol, float(err.max())
+
+
+def test_reference_case(session, cuda):
+    a = synth.lcg_floats(256 * 256, 0x12345678, -1.0, 1.0).reshape(256, 256)
+    b = synth.lcg_floats(256 * 256, 0x9ABCDEF0, -1.0, 1.0).reshape(256, 256)
+    _check(session.sgemm(a, b), a, b)
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 64, 32), (128, 192, 96), (1024, 1024, 1024), (64, 4096, 512)])
+def test_shapes(session, cuda, m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    _check(session.sgemm(a, b), a, b, 1e-4)
+
+
+def test_device_entry_any_shape(session, cuda):
+    import torch
+    rng = np.random.default_rng(1)
+    a = rng.standard_normal((37, 100)).astype(np.float32)
+    b = rng.standard_normal((100, 51)).astype(np.float32)
+    da, db = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    dc = torch.empty((37, 51), device=cuda)
+    session.sgemm_device(da.data_ptr(), db.data_ptr(), dc.data_ptr(), 37, 51, 100,
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    _check(dc.cpu().numpy(), a, b, 1e-4)
+
+
+def test_reports_zero_error_like_the_reference(session, cuda):
+    a = np.ones((64, 32), np.float32)
+    b = np.ones((32, 64), np.float32)
+    c = np.empty((64, 64), np.float32)
+    err = ctypes.c_float(-1.0)
+    f = lambda x: x.ctypes.data_as(ctypes.POINTER(ctypes.c_float))  # noqa: E731
+    assert session.raw("spaceslug_sgemm")(f(a), f(b), f(c), 64, 64, 32, ctypes.byref(err)) == 0
+    assert err.value == 0.0 and np.all(c == 32.0)
