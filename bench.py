@@ -18,7 +18,8 @@ path is "replicas only"; scaling "weak").
 Other workloads (secondary figures, also attached to the default line at N=1):
 prefill = configs[2] (2048 x 4096 x 11008), lora = configs[3] (512 x 4096 x
 4096, r=16, alpha=32), tiny = configs[0]; mlp70b = configs[4] N-sharded over
-the ranks with an NCCL all-gather of Y (run it under torchrun).
+the ranks with an NCCL all-gather of Y (run it under torchrun; at N > 1 the
+default run attaches it as a secondary figure).
 
 --impl reference times the reference's own CPU implementation
 (cpu_reference of vulkan-runtime/tests/test_q4gemm.cpp:102-119, compiled from
@@ -558,7 +559,16 @@ def sgemm_gpu(args, dist: Dist, torch, session) -> dict:
 
 
 def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
-    """columns of W sharded over the ranks, NCCL all-gather of Y."""
+    """columns of W sharded over the ranks; Y all-gathered over NVLink.
+
+    Timed per step (L2 flushed before each), for 1, 2 and 4 row bands, both
+    exchanges of the sharding module: ShardedGemm (GEMM of row band b+1 on the
+    compute stream while band b is all-gathered by NCCL and re-laid out into
+    row-major Y) and ShardedGemmPush (GEMM writes into a row-major Y every
+    peer has mapped; copy engines push each finished band to the peers).  The
+    value is the fastest of the six; the GEMM alone, the NCCL all-gather of the
+    whole Y alone and the re-layout alone are timed the same way for the
+    breakdown."""
     from spaceslug_b200 import sharding
     dev = torch.device("cuda", dist.local)
     cfg = synth.CONFIGS["mlp70b"]
@@ -566,36 +576,96 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     del w_kn
     c0, c1 = sharding.shard_columns(cfg.n, dist.world, dist.rank)
     h = session.weights(packed, scales, cfg.k, cfg.n, c0, c1, device=dist.local)
+    del packed, scales
     x = torch.from_numpy(synth.make_x(cfg.m, cfg.k, 0)).to(dev)
-    ys = torch.empty((cfg.m, c1 - c0), dtype=torch.float32, device=dev)
+    y = torch.empty((cfg.m, cfg.n), dtype=torch.float32, device=dev)
+    ysh = torch.empty((cfg.m, c1 - c0), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(device=dev)
-    gemm = lambda: h.run(x.data_ptr(), ys.data_ptr(), cfg.m, stream.cuda_stream)  # noqa: E731
-    gemm()
-    stream.synchronize()
     flush = l2_flush_buffer(torch, dev)
-    steps = args.steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(steps + args.warmup)]
-    dist.barrier()
-    for i in range(steps + args.warmup):
-        with torch.cuda.stream(stream):
-            flush.zero_()
-            ev[i][0].record(stream)
-            gemm()
-            ev[i][1].record(stream)
-            y = sharding.allgather_columns(ys, cfg.n, dist.pg, stream=stream) if dist.world > 1 else ys
-            ev[i][2].record(stream)
-    torch.cuda.synchronize(dev)
-    dist.barrier()
-    g_ms = sum(ev[i][0].elapsed_time(ev[i][1]) for i in range(args.warmup, steps + args.warmup)) / steps
-    t_ms = sum(ev[i][0].elapsed_time(ev[i][2]) for i in range(args.warmup, steps + args.warmup)) / steps
-    g_ms, t_ms = dist.max(g_ms), dist.max(t_ms)
     flops = 2.0 * cfg.m * cfg.n * cfg.k
+
+    def timed(fn, steps):
+        evs = []
+        for _ in range(args.warmup + steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                evs.append((a, b))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        return dist.max(sum(a.elapsed_time(b) for a, b in evs[args.warmup:]) / steps)
+
+    steps = args.steps
+    n0 = session.launch_count()
+    h.run(x.data_ptr(), ysh.data_ptr(), cfg.m, stream.cuda_stream)
+    gemm_launches = session.launch_count() - n0
+    stream.synchronize()
+    dist.barrier()
+    g_ms = timed(lambda: h.run(x.data_ptr(), ysh.data_ptr(), cfg.m, stream.cuda_stream), steps)
+    detail = {"gemm_ms": g_ms, "gemm_only_tflops": flops / (g_ms * 1e-3) / 1e12,
+              "per_gpu_frac_gemm": flops / dist.world / (g_ms * 1e-3) / 1e12 / peaks["bf16_tflops"]}
+    if dist.world == 1:
+        h.close()
+        detail.update({"ms_per_step": g_ms, "exchange": "none (one GPU)"})
+        return {"value": detail["gemm_only_tflops"], "ms_per_step": g_ms, "detail": detail,
+                "gpu_launches": gemm_launches * steps}
+    p = dist.world
+    width = sharding.shard_width(cfg.n, p)
+    recv = (p - 1) * cfg.m * width * 4
+    best = None
+    for bands in (1, 2, 4):
+        piped = sharding.ShardedGemm(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands)
+        n0 = session.launch_count()
+        piped.run(x, y, stream)
+        launches = session.launch_count() - n0
+        stream.synchronize()
+        dist.barrier()
+        t_ms = timed(lambda: piped.run(x, y, stream), steps)
+        detail[f"bands{bands}_ms"] = t_ms
+        if best is None or t_ms < best[1]:
+            best = (bands, t_ms, launches)
+        if bands == 1:
+            g = piped.gathered.view(p * cfg.m, width)
+            ag = timed(lambda: dist.pg.all_gather_into_tensor(g, piped.ys), steps)
+            rl = timed(lambda: session.shards_relayout(g.data_ptr(), y.data_ptr(), p, cfg.m, width, cfg.n, cfg.n,
+                                                       stream.cuda_stream), steps)
+            algbw = p * cfg.m * width * 4 / (ag * 1e-3) / 1e9
+            detail.update({"nccl_allgather_ms": ag, "allgather_algbw_GBs": algbw,
+                           "allgather_busbw_GBs": algbw * (p - 1) / p,
+                           "allgather_recv_bytes_per_gpu": recv, "relayout_ms": rl,
+                           "relayout_GBs": 2 * cfg.m * cfg.n * 4 / (rl * 1e-3) / 1e9})
+        del piped
+        torch.cuda.empty_cache()
+    best = (best[0], best[1], best[2], "nccl")
+    del y
+    torch.cuda.empty_cache()
+    for bands in (1, 2, 4):
+        push = sharding.ShardedGemmPush(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands)
+        n0 = session.launch_count()
+        push.run(x, stream)
+        launches = session.launch_count() - n0
+        stream.synchronize()
+        dist.barrier()
+        t_ms = timed(lambda: push.run(x, stream), steps)
+        detail[f"push_bands{bands}_ms"] = t_ms
+        if t_ms < best[1]:
+            best = (bands, t_ms, launches, "push")
+        push.close()
+        del push
+        torch.cuda.empty_cache()
+    bands, t_ms, launches, exchange = best
+    target_ms = max(flops / p / (peaks["bf16_tflops"] * 1e12), recv / 770e9) * 1e3
+    detail.update({"bands": bands, "exchange": exchange, "ms_per_step": t_ms,
+                   "roofline": {"target_ms": target_ms, "frac": target_ms / t_ms,
+                                "bound": "max(GEMM/P at the measured bf16 peak, all-gather receive bytes at "
+                                         "770 GB/s per direction)"},
+                   "y_shape": [cfg.m, cfg.n]})
     h.close()
-    return {"value": flops / (t_ms * 1e-3) / 1e12, "gemm_only_tflops": flops / (g_ms * 1e-3) / 1e12,
-            "ms_per_step": t_ms, "gemm_ms": g_ms, "allgather_ms": t_ms - g_ms,
-            "per_gpu_frac_gemm": flops / dist.world / (g_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
-            "y_shape": list(y.shape)}
+    return {"value": flops / (t_ms * 1e-3) / 1e12, "ms_per_step": t_ms, "detail": detail,
+            "gpu_launches": launches * steps}
 
 
 def main() -> None:
@@ -659,16 +729,26 @@ def main() -> None:
             except Exception as exc:  # report, do not hide
                 sec["sgemm"] = {"error": str(exc)}
             line["secondary"] = sec
+        if dist.world > 1 and not args.no_secondary:
+            # the N-sharded config at this world size, beside the decode replicas
+            try:
+                r = mlp70b_gpu(args, dist, torch, session, synth, peaks)
+                line["secondary"] = {"mlp70b": {"TFLOP/s": r["value"], "ms_per_step": r["ms_per_step"],
+                                                "parallelism": f"N-shard x{dist.world}", **r["detail"]}}
+            except Exception as exc:  # report, do not hide
+                line["secondary"] = {"mlp70b": {"error": str(exc)}}
         if dist.rank == 0 and dist.world == 1:
             line["cpu_baseline"] = cpu_reference_decode(args.cpu_seconds, threads=1)
     elif args.workload == "mlp70b":
         r = mlp70b_gpu(args, dist, torch, session, synth, peaks)
         line.update({"value": r["value"], "unit": "TFLOP/s", "ms_per_step": r["ms_per_step"], "scaling": "strong",
-                     "dtype": "f16 MMA / f32 accumulate",
+                     "dtype": "f16 MMA / f32 accumulate", "gpu_launches": r["gpu_launches"],
                      "config": {"workload": "70B MLP int4 GEMM 4096x8192x28672, N-sharded + NCCL all-gather "
                                             "(BASELINE configs[4])", "parallelism": f"N-shard x{dist.world}",
+                                "bands": r["detail"].get("bands", 1),
+                                "exchange": r["detail"].get("exchange", "none"),
                                 "l2": "L2 flushed (256 MB write) before every step"},
-                     "detail": r})
+                     "detail": r["detail"]})
     else:
         r = gemm_gpu(args, dist, torch, session, synth, peaks, args.workload)
         line.update({"value": r["TFLOP/s"], "unit": "TFLOP/s", "ms_per_step": r["ms"], "scaling": "weak",

@@ -219,6 +219,35 @@ int spaceslug_sgemm(const float* a, const float* b, float* c, uint32_t m, uint32
 /* Same product for device pointers, any positive m, n, k, asynchronous on `stream`. */
 int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, void* stream);
 
+/* spaceslug_q4_weights_run with a row pitch: Y[i][j] at y[i * ld_y + j] for
+ * j < the handle's column count; other columns of the pitched rows are not
+ * written (a rank's column shard straight into the full row-major Y).  x
+ * 16-byte aligned, y 4-byte aligned, ld_y >= the handle's column count. */
+int spaceslug_q4_weights_run_strided(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, uint64_t ld_y,
+                                     void* stream);
+
+/* CUDA IPC between the ranks of one node (no reference counterpart).
+ * export: 64-byte handle of the device allocation holding `ptr` and the byte
+ * offset of ptr inside it.  open: maps a peer's allocation on `device`
+ * (peer access enabled on first use); *ptr = mapped base + offset, *base is
+ * what close takes. */
+int spaceslug_ipc_export(const void* ptr, void* handle64, uint64_t* offset);
+int spaceslug_ipc_open(const void* handle64, uint64_t offset, int device, void** ptr, void** base);
+int spaceslug_ipc_close(void* base);
+/* Pitched copy of `rows` rows of width_bytes between any two device (or
+ * peer-mapped) addresses, asynchronous on `stream` (a copy engine, no SMs). */
+int spaceslug_copy_2d(void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width_bytes,
+                      uint64_t rows, void* stream);
+
+/* N-sharded GEMM exchange (no reference counterpart: the reference runs on one
+ * device).  After an all-gather of equal-width column shards of Y, the
+ * gathered buffer is rank-major [parts][rows][width]; this writes it into
+ * rows [rows][ld_y] of row-major Y, columns [0, n_total) (n_total <=
+ * parts * width; the last shard's padding columns are dropped).  Device
+ * pointers, asynchronous on `stream`. */
+int spaceslug_shards_relayout(const float* gathered, float* y, uint32_t parts, uint32_t rows, uint32_t width,
+                              uint32_t n_total, uint64_t ld_y, void* stream);
+
 /* ---- CQ4 (Cactus-Quants) ------------------------------------------------
  * C[M x N] = A'[M x K] * W'^T in fp16 storage with fp32 accumulation, where
  * A' is the activation transformed into the code basis and

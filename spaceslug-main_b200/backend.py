@@ -59,6 +59,14 @@ _SIGNATURES = {
     "spaceslug_last_error": ([], ctypes.c_char_p),
     "spaceslug_sgemm": ([_f32p, _f32p, _f32p, _u32, _u32, _u32, _f32p], ctypes.c_int),
     "spaceslug_sgemm_device": ([_vp, _vp, _vp, _u32, _u32, _u32, _vp], ctypes.c_int),
+    "spaceslug_shards_relayout": ([_vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, _vp], ctypes.c_int),
+    "spaceslug_q4_weights_run_strided": ([_vp, _vp, _vp, _u32, ctypes.c_uint64, _vp], ctypes.c_int),
+    "spaceslug_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "spaceslug_ipc_open": ([_vp, ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)],
+                           ctypes.c_int),
+    "spaceslug_ipc_close": ([_vp], ctypes.c_int),
+    "spaceslug_copy_2d": ([_vp, ctypes.c_uint64, _vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _vp],
+                          ctypes.c_int),
     "spaceslug_lora_gradients": ([_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32], ctypes.c_int),
     "spaceslug_lora_sgd": ([_f32p, _f32p, _f32p, _f32p, ctypes.c_float, _u32], ctypes.c_int),
     "spaceslug_lora_train_step": ([_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float, _u32, _u32], ctypes.c_int),
@@ -259,6 +267,34 @@ class BackendSession:
     def sgemm_device(self, a: int, b: int, c: int, m: int, n: int, k: int, stream: int = 0) -> None:
         self._call("spaceslug_sgemm_device", a, b, c, m, n, k, stream or None)
 
+    def shards_relayout(self, gathered: int, y: int, parts: int, rows: int, width: int, n_total: int, ld_y: int,
+                        stream: int = 0) -> None:
+        """Device pointers: rank-major gathered shards [parts][rows][width] -> Y rows [rows][ld_y]."""
+        self._call("spaceslug_shards_relayout", gathered, y, parts, rows, width, n_total, ld_y, stream or None)
+
+    def ipc_export(self, ptr: int) -> tuple[bytes, int]:
+        """(64-byte CUDA IPC handle of the allocation holding ptr, byte offset of ptr in it)."""
+        h = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64()
+        self._call("spaceslug_ipc_export", ptr, h, ctypes.byref(off))
+        return h.raw, int(off.value)
+
+    def ipc_open(self, handle: bytes, offset: int, device: int) -> tuple[int, int]:
+        """Maps a peer's allocation on `device`: (pointer, base to pass to ipc_close)."""
+        if len(handle) != 64:
+            raise ValueError("an IPC handle has 64 bytes")
+        ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+        self._call("spaceslug_ipc_open", ctypes.create_string_buffer(handle, 64), offset, device,
+                   ctypes.byref(ptr), ctypes.byref(base))
+        return int(ptr.value), int(base.value)
+
+    def ipc_close(self, base: int) -> None:
+        self._call("spaceslug_ipc_close", base)
+
+    def copy_2d(self, dst: int, dpitch: int, src: int, spitch: int, width_bytes: int, rows: int,
+                stream: int = 0) -> None:
+        self._call("spaceslug_copy_2d", dst, dpitch, src, spitch, width_bytes, rows, stream or None)
+
     def lora_gradients(self, x, dy, a, b, m: int, rank: int):
         """The reference's hidden-64 spaceslug_lora_gradients: (dA [64, r], dB [r, 64])."""
         xx, yy, aa, bb = (_arr(v, np.float32) for v in (x, dy, a, b))
@@ -336,6 +372,10 @@ class Q4Weights:
 
     def run(self, x: int, y: int, m: int, stream: int = 0) -> None:
         self.session._call("spaceslug_q4_weights_run", self.handle, x, y, m, stream or None)
+
+    def run_strided(self, x: int, y: int, m: int, ld_y: int, stream: int = 0) -> None:
+        """Y rows with pitch ld_y floats (this handle's columns only)."""
+        self.session._call("spaceslug_q4_weights_run_strided", self.handle, x, y, m, ld_y, stream or None)
 
     # ---- LoRA training (device pointers, asynchronous) ----
     def lora_backward(self, x: int, dy: int, m: int, stream: int = 0) -> None:

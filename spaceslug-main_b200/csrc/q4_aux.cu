@@ -1,7 +1,8 @@
 // Auxiliary sm_100a kernels of the int4 path: bit-exact dequant (debug
 // export), device-side packer, the fp32 -> 16-bit operand cast with per-row
 // power-of-two exponents, per-column scale exponents, the LoRA projection
-// T = X*A, and the legacy hidden-64 LoRA delta kernel.
+// T = X*A, the legacy hidden-64 LoRA delta kernel, and the re-layout of
+// all-gathered column shards into row-major Y.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -399,6 +400,65 @@ int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int r
         lora_xa_reduce_kernel<<<(M * rank + 255) / 256, 256, 0, stream>>>(partial, t, M, rank, chunks, nullptr,
                                                                           nullptr);
     }
+    return static_cast<int>(cudaGetLastError());
+}
+
+namespace {
+
+// Gathered column shards [P][rows][w] (rank-major, as an all-gather of the
+// per-rank Y shards leaves them) -> Y rows [rows][ld], columns [0, n_total).
+// Source index order: consecutive threads read consecutive elements of one
+// shard row and write consecutive columns of one Y row, so both sides
+// coalesce.  V = 4 moves float4 (every address and extent 16-byte aligned),
+// V = 1 single floats.
+template <int V>
+__global__ void __launch_bounds__(256) shards_relayout_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                                              int rows, int wv, int nv, long long ldv,
+                                                              long long total) {
+    using T = typename std::conditional<V == 4, float4, float>::type;
+    const T* s = reinterpret_cast<const T*>(src);
+    T* d = reinterpret_cast<T*>(dst);
+    const long long per_part = static_cast<long long>(rows) * wv;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(i / per_part);
+        const long long rem = i - p * per_part;
+        const int r = static_cast<int>(rem / wv);
+        const int j = static_cast<int>(rem - static_cast<long long>(r) * wv);
+        const int col = p * wv + j;
+        if (col >= nv) continue;
+        T v;
+        if constexpr (V == 4) {
+            const uint4 u = ldg_stream_v4(s + i);
+            v = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+        } else {
+            v = __ldg(s + i);
+        }
+        d[r * ldv + col] = v;
+    }
+}
+
+}  // namespace
+
+int launch_shards_relayout(const float* gathered, float* y, int parts, int rows, int width, int n_total,
+                           long long ld_y, cudaStream_t stream) {
+    if (parts < 1 || rows < 0 || width < 1 || n_total < 1 || n_total > static_cast<long long>(parts) * width ||
+        ld_y < n_total)
+        return static_cast<int>(cudaErrorInvalidValue);
+    if (rows == 0) return 0;
+    const bool v4 = width % 4 == 0 && n_total % 4 == 0 && ld_y % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(gathered) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+    const int v = v4 ? 4 : 1;
+    const long long total = static_cast<long long>(parts) * rows * (width / v);
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long want = (total + 255) / 256;
+    const unsigned grid = static_cast<unsigned>(want < 8LL * sms ? want : 8LL * sms);
+    if (v4)
+        shards_relayout_kernel<4><<<grid, 256, 0, stream>>>(gathered, y, rows, width / 4, n_total / 4, ld_y / 4, total);
+    else
+        shards_relayout_kernel<1><<<grid, 256, 0, stream>>>(gathered, y, rows, width, n_total, ld_y, total);
     return static_cast<int>(cudaGetLastError());
 }
 

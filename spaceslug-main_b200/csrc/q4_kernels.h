@@ -132,6 +132,11 @@ int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t
 int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
                    float* partial = nullptr, const int* row_exp = nullptr, uint16_t* t_op_bits = nullptr);
 int lora_xa_chunks(int K);
+// All-gathered column shards [parts][rows][width] (rank-major) -> rows
+// [rows][ld_y] of row-major Y, columns [0, n_total) (the last shard may be
+// partly padding).  HBM-bound copy; float4 when every address is aligned.
+int launch_shards_relayout(const float* gathered, float* y, int parts, int rows, int width, int n_total,
+                           long long ld_y, cudaStream_t stream);
 // CQ4 activation transform into the code basis, fp16 [M][K] -> fp16 [M][K]:
 // Hadamard groups of gs in {32, 64, 128, 256} (rotation == nullptr) or the
 // dense orthogonal rotation [K][K] fp16.  lsign / rsign ([gs], +-1) and perm

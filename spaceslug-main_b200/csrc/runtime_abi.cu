@@ -226,6 +226,7 @@ struct Problem {
     float alpha;
     float* y;
     int M, N, K;
+    long long ld_y = 0;  // row pitch of Y in floats (0: N)
 };
 
 // GEMV launch geometry.  K is split over a cluster of S CTAs (S | G, slice
@@ -307,8 +308,47 @@ void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
     if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
 }
 
+// Co-resident CTA pairs of the pair kernel for operand type `op` (cached).
+int pair_capacity(DeviceCtx& c, q4::Operand16 op) {
+    std::lock_guard<std::mutex> lk(c.pair_mu);
+    int& mp = c.max_pairs[static_cast<int>(op)];
+    if (mp < 0) mp = q4::gemm_pair_max_active(op);
+    return mp;
+}
+
+// The GEMM takes the CTA-pair kernel (256 x 256 tiles, half the
+// operand bytes per FLOP) when it still fills every co-resident pair and the
+// shape suits its TMA maps: scales loaded with row stride K/8 bytes (K % 128
+// == 0), Y stored with row stride 4 ld bytes (N % 4 == 0, ld % 4 == 0,
+// 16-byte aligned Y).  LoRA runs as extra bf16 k-stages of the single-CTA
+// kernel.
+bool use_pair_kernel(DeviceCtx& c, const Problem& p, q4::Operand16 op, int* pairs_out) {
+    const long long ld = p.ld_y ? p.ld_y : p.N;
+    const int pairs = pair_capacity(c, op);
+    if (pairs_out) *pairs_out = pairs;
+    const int variant = g_gemm_variant.load();
+    const bool shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && ld % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
+    return p.rank == 0 && pairs > 0 && shape_ok &&
+           (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
+}
+
 void run_problem(const Problem& p, cudaStream_t stream) {
     DeviceCtx& c = ctx_for(current_device());
+    if (p.ld_y != 0 && p.ld_y != p.N && !(p.M > 8 && use_pair_kernel(c, p, operand_type(), nullptr))) {
+        // Only the pair kernel (reached for M > 8) stores Y with an arbitrary
+        // row pitch: elsewhere the product lands in scratch and one strided
+        // copy places it.
+        Scratch ys(static_cast<size_t>(p.M) * p.N * sizeof(float), stream);
+        Problem q = p;
+        q.y = static_cast<float*>(ys.p);
+        q.ld_y = 0;
+        run_problem(q, stream);
+        check(cudaMemcpy2DAsync(p.y, static_cast<size_t>(p.ld_y) * 4, ys.p, static_cast<size_t>(p.N) * 4,
+                                static_cast<size_t>(p.N) * 4, static_cast<size_t>(p.M), cudaMemcpyDeviceToDevice,
+                                stream),
+              "cudaMemcpy2DAsync (strided Y)");
+        return;
+    }
     Scratch t_buf(p.rank > 0 ? static_cast<size_t>(p.M) * p.rank * sizeof(float) : 0, stream);
     Scratch t_part(p.rank > 0 ? static_cast<size_t>(q4::lora_xa_chunks(p.K)) * p.M * p.rank * sizeof(float) : 0,
                    stream);
@@ -409,19 +449,10 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     // single-CTA kernel with 256-row tiles when they fill every SM; else
     // 128-row tiles.
     int pairs = 0;
-    {
-        std::lock_guard<std::mutex> lk(c.pair_mu);
-        int& mp = c.max_pairs[static_cast<int>(op)];
-        if (mp < 0) mp = q4::gemm_pair_max_active(op);
-        pairs = mp;
-    }
     const int variant = g_gemm_variant.load();
-    // LoRA runs as extra bf16 k-stages of the single-CTA kernel
-    // The pair kernel TMA-loads the scales (row stride K/8 bytes: K % 128 == 0)
-    // and TMA-stores Y (row stride 4N bytes: N % 4 == 0, 16-byte aligned Y).
-    const bool pair_shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
-    const bool use_pair = p.rank == 0 && pairs > 0 && pair_shape_ok &&
-                          (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
+    const bool use_pair = use_pair_kernel(c, p, op, &pairs);
+    const long long ld_y = p.ld_y ? p.ld_y : p.N;
+    if (ld_y != p.N && !use_pair) throw CudaError("strided Y reached a kernel without a row pitch");
     g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
     g.sm_count = c.sm_count;
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
@@ -436,7 +467,7 @@ void run_problem(const Problem& p, cudaStream_t stream) {
         encode_2d(&g.tmap_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.scales, static_cast<uint64_t>(p.K) / 32,
                   static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K) / 8, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
         encode_2d(&g.tmap_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.y, static_cast<uint64_t>(p.N),
-                  static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.N) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+                  static_cast<uint64_t>(p.M), static_cast<uint64_t>(ld_y) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     }
     g.scales = p.scales; g.col_exp = col_exp; g.row_exp = row_exp; g.y = p.y;
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
@@ -938,6 +969,108 @@ int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, 
     });
 }
 
+int spaceslug_q4_weights_run_strided(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, uint64_t ld_y,
+                                     void* stream) {
+    if (!w || !x || !y) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (m == 0 || m > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "bad m");
+    if (ld_y < static_cast<uint64_t>(w->N) || ld_y > (uint64_t(1) << 40))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "ld_y must be >= the handle's column count");
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(y) & 3u))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "x must be 16-byte and y 4-byte aligned");
+    return guarded([&] {
+        if (current_device() != w->device) check(cudaSetDevice(w->device), "cudaSetDevice");
+        Problem p{x, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, y,
+                  static_cast<int>(m), w->N, w->K, static_cast<long long>(ld_y)};
+        if (ld_y == static_cast<uint64_t>(w->N) && !aligned16(y)) {
+            // the kernels want a 16-byte aligned Y: product in scratch, then one copy
+            // (a pitched, unaligned Y takes the same route inside run_problem)
+            Scratch ys(static_cast<size_t>(m) * w->N * 4, static_cast<cudaStream_t>(stream));
+            Problem q = p;
+            q.y = static_cast<float*>(ys.p);
+            q.ld_y = 0;
+            run_problem(q, static_cast<cudaStream_t>(stream));
+            check(cudaMemcpyAsync(y, ys.p, static_cast<size_t>(m) * w->N * 4, cudaMemcpyDeviceToDevice,
+                                  static_cast<cudaStream_t>(stream)),
+                  "cudaMemcpyAsync (unaligned Y)");
+            return SPACESLUG_OK;
+        }
+        run_problem(p, static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_ipc_export(const void* ptr, void* handle64, uint64_t* offset) {
+    if (!ptr || !handle64 || !offset) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    return guarded([&] {
+        cudaPointerAttributes a{};
+        check(cudaPointerGetAttributes(&a, ptr), "cudaPointerGetAttributes");
+        if (a.type != cudaMemoryTypeDevice) throw CudaError("not device memory");
+        using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+        static RangeFn range = [] {
+            void* fn = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+                q != cudaDriverEntryPointSuccess)
+                fn = nullptr;
+            return reinterpret_cast<RangeFn>(fn);
+        }();
+        if (!range) throw CudaError("cuMemGetAddressRange is unavailable");
+        const int prev = current_device();
+        check(cudaSetDevice(a.device), "cudaSetDevice");
+        CUdeviceptr base = 0;
+        size_t size = 0;
+        const CUresult r = range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+        if (r != CUDA_SUCCESS) {
+            cudaSetDevice(prev);
+            throw CudaError("cuMemGetAddressRange failed (" + std::to_string(static_cast<int>(r)) + ")");
+        }
+        cudaIpcMemHandle_t h;
+        const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+        cudaSetDevice(prev);
+        check(e, "cudaIpcGetMemHandle");
+        static_assert(sizeof(h) == 64, "IPC handle size");
+        std::memcpy(handle64, &h, sizeof(h));
+        *offset = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_ipc_open(const void* handle64, uint64_t offset, int device, void** ptr, void** base) {
+    if (!handle64 || !ptr || !base) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    *ptr = *base = nullptr;
+    return guarded([&] {
+        check(cudaSetDevice(device), "cudaSetDevice");
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle64, sizeof(h));
+        void* b = nullptr;
+        check(cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        *base = b;
+        *ptr = static_cast<char*>(b) + offset;
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_ipc_close(void* base) {
+    if (!base) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    return guarded([&] {
+        check(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_copy_2d(void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width_bytes,
+                      uint64_t rows, void* stream) {
+    if (!dst || !src) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (width_bytes > dpitch || width_bytes > spitch) return fail(SPACESLUG_INVALID_ARGUMENT, "width exceeds a pitch");
+    if (width_bytes == 0 || rows == 0) return SPACESLUG_OK;
+    return guarded([&] {
+        check(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width_bytes, rows, cudaMemcpyDefault,
+                                static_cast<cudaStream_t>(stream)),
+              "cudaMemcpy2DAsync");
+        return SPACESLUG_OK;
+    });
+}
+
 int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m) {
     if (!w || !x || !y) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
     if (m == 0 || m > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "bad m");
@@ -1197,6 +1330,25 @@ int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m,
         DeviceCtx& ctx = ctx_for(current_device());
         run_sgemm(ctx, a, b, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
                   static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_shards_relayout(const float* gathered, float* y, uint32_t parts, uint32_t rows, uint32_t width,
+                              uint32_t n_total, uint64_t ld_y, void* stream) {
+    if (!gathered || !y) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (parts == 0 || width == 0 || n_total == 0) return fail(SPACESLUG_INVALID_ARGUMENT, "zero dimension");
+    if (parts > (1u << 16) || rows > (1u << 30) || width > (1u << 30))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "dimension too large");
+    if (static_cast<uint64_t>(n_total) > static_cast<uint64_t>(parts) * width)
+        return fail(SPACESLUG_INVALID_ARGUMENT, "n_total exceeds parts * width");
+    if (ld_y < n_total || ld_y > (uint64_t(1) << 40)) return fail(SPACESLUG_INVALID_ARGUMENT, "bad ld_y");
+    if (rows == 0) return SPACESLUG_OK;
+    return guarded([&] {
+        check_launch(q4::launch_shards_relayout(gathered, y, static_cast<int>(parts), static_cast<int>(rows),
+                                                static_cast<int>(width), static_cast<int>(n_total),
+                                                static_cast<long long>(ld_y), static_cast<cudaStream_t>(stream)),
+                     "shards_relayout");
         return SPACESLUG_OK;
     });
 }

@@ -1,13 +1,19 @@
-"""N-sharding of the int4 GEMM over the GPUs of one node (BASELINE configs[4]).
+"""N-sharding of the int4 GEMM over the GPUs of one node.
 
 Output columns are independent: Y[:, n] needs only W[:, n], scales[n, :] and
 LoRA B[:, n].  In the reference layout a contiguous column range of W and of
 the scales is one contiguous byte range (packed byte n*(K/2) + k/2, scale
 n*(K/32) + k/32), so rank r uploads columns [begin, end) with no repacking
 (spaceslug_q4_weights_create with col_begin/col_end) and computes its Y shard
-locally.  The only exchange is an all-gather of the fp32 Y shards over
-NVLink (NCCL through torch.distributed), followed by the re-layout from the
-rank-major [P][M][N/P] gather buffer to row-major [M][N].
+locally.  The only exchange is the all-gather of the fp32 Y shards over
+NVLink, in two forms:
+
+* allgather_columns / ShardedGemm: NCCL all-gather (torch.distributed) into
+  a rank-major [P][M][N/P] buffer, then the re-layout kernel into row-major
+  [M][N]; ShardedGemm pipelines it over row bands of the GEMM.
+* ShardedGemmPush: the GEMM writes its columns straight into a row-major Y
+  that every peer has mapped (CUDA IPC), and copy engines push each finished
+  row band into the peers' Y while the SMs compute the next band.
 """
 from __future__ import annotations
 
@@ -45,3 +51,194 @@ def allgather_columns(y_shard, n_total: int, pg, stream=None):
     else:  # gloo (CPU): list form
         pg.all_gather(list(buf.unbind(0)), y_shard.contiguous())
     return buf.permute(1, 0, 2).reshape(m, world * w)[:, :n_total]
+
+
+def plan_bands(m: int, bands: int, align: int = 256) -> list[tuple[int, int]]:
+    """Row bands [r0, r1) of an M-row GEMM for the exchange pipeline.
+
+    The rows are cut into `align`-row tiles (whole tiles of the prefill
+    kernel); at most `bands` bands get whole tiles as evenly as possible, the
+    later bands the larger ones, and the last band also takes the ragged tail.
+    A last band shorter than `align` rows is merged into the one before it, so
+    no band of an M > 8 GEMM becomes a decode-sized (M <= 8) launch."""
+    if m < 1 or bands < 1 or align < 1:
+        raise ValueError("m, bands and align must be positive")
+    tiles = -(-m // align)
+    b = min(bands, tiles)
+    base, extra = divmod(tiles, b)
+    out, r0 = [], 0
+    for i in range(b):
+        r1 = min(m, r0 + (base + (1 if i >= b - extra else 0)) * align)
+        out.append((r0, r1))
+        r0 = r1
+    if len(out) > 1 and out[-1][1] - out[-1][0] < align:
+        out[-2:] = [(out[-2][0], out[-1][1])]
+    return out
+
+
+class ShardedGemm:
+    """One rank's part of an N-sharded int4 GEMM whose full Y every rank needs.
+
+    The rank's weight handle covers columns [c0, c1) of W (a contiguous byte
+    range of the reference layout, spaceslug_q4_weights_create with
+    col_begin / col_end).  run(x, y) computes the rank's Y shard row band by
+    row band on the caller's stream.  As soon as a band is done its shard rows
+    are all-gathered (NCCL through torch.distributed, on a second stream) and
+    written into the caller's row-major Y by the library's re-layout kernel
+    (spaceslug_shards_relayout, on a third stream), so the NVLink exchange of
+    band b overlaps the GEMM of band b + 1.  When run returns, the caller's
+    stream is ordered after the last re-layout.
+    """
+
+    def __init__(self, session, handle, m: int, n_total: int, dist, device, bands: int = 2, group=None) -> None:
+        import torch
+        self.torch, self.session, self.h, self.dist, self.group = torch, session, handle, dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.m, self.n_total, self.k = m, n_total, handle.k
+        self.c0, self.c1 = shard_columns(n_total, self.world, self.rank)
+        if (handle.col_begin, handle.col_end) != (self.c0, self.c1):
+            raise ValueError("the weight handle does not hold this rank's column shard")
+        self.width = shard_width(n_total, self.world)
+        self.device = torch.device(device)
+        self.bands = plan_bands(m, bands)
+        self.ys = torch.zeros((m, self.width), dtype=torch.float32, device=self.device)
+        self.direct = (self.c1 - self.c0) == self.width
+        self.tmp = None if self.direct else torch.empty((m, self.c1 - self.c0), dtype=torch.float32,
+                                                        device=self.device)
+        self.gathered = torch.empty(self.world * m * self.width, dtype=torch.float32, device=self.device)
+        self.comm = torch.cuda.Stream(device=self.device)
+        self.post = torch.cuda.Stream(device=self.device)
+
+    def run(self, x, y, stream=None) -> None:
+        """x: device fp32 [m][k]; y: device fp32 [m][>= n_total] (row stride y.stride(0))."""
+        torch = self.torch
+        if x.shape != (self.m, self.k) or not x.is_contiguous() or x.dtype != torch.float32:
+            raise ValueError("x must be a contiguous fp32 [m, k] tensor")
+        if y.dim() != 2 or y.shape[0] != self.m or y.shape[1] < self.n_total or y.stride(1) != 1:
+            raise ValueError("y must be fp32 [m, >= n_total] with unit column stride")
+        s0 = stream or torch.cuda.current_stream(self.device)
+        k, w, p = self.k, self.width, self.world
+        for r0, r1 in self.bands:
+            rows = r1 - r0
+            band = self.ys[r0:r1]
+            if self.direct:
+                self.h.run(x.data_ptr() + 4 * r0 * k, band.data_ptr(), rows, s0.cuda_stream)
+            else:
+                self.h.run(x.data_ptr() + 4 * r0 * k, self.tmp[r0:r1].data_ptr(), rows, s0.cuda_stream)
+                with torch.cuda.stream(s0):
+                    band[:, : self.c1 - self.c0].copy_(self.tmp[r0:r1])
+            done = torch.cuda.Event()
+            done.record(s0)
+            self.comm.wait_event(done)
+            g = self.gathered[p * r0 * w: p * r1 * w].view(p * rows, w)
+            with torch.cuda.stream(self.comm):
+                self.dist.all_gather_into_tensor(g, band, group=self.group)
+            got = torch.cuda.Event()
+            got.record(self.comm)
+            self.post.wait_event(got)
+            self.session.shards_relayout(g.data_ptr(), y[r0:r1].data_ptr(), p, rows, w, self.n_total, y.stride(0),
+                                         self.post.cuda_stream)
+        fin = torch.cuda.Event()
+        fin.record(self.post)
+        s0.wait_event(fin)
+
+
+class ShardedGemmPush:
+    """The N-sharded GEMM with the exchange on copy engines over NVLink.
+
+    Every rank's full Y [m][n_total] is one device allocation, mapped into
+    every other rank by CUDA IPC (spaceslug_ipc_export / spaceslug_ipc_open).
+    The GEMM of each row band writes this rank's columns [c0, c1) straight
+    into its own Y (spaceslug_q4_weights_run_strided, row pitch n_total), and
+    as soon as the band is done one pitched copy per peer
+    (spaceslug_copy_2d, a copy engine, no SMs) pushes those rows into that
+    peer's Y, while the SMs run the next band.  No gather buffer and no
+    re-layout.  Two one-element NCCL all-reduces per call fence the pushes:
+    one before the first push (every rank's earlier use of its Y is done) and
+    one after the last (every rank's Y is complete).  Construct and close()
+    collectively on every rank.
+    """
+
+    def __init__(self, session, handle, m: int, n_total: int, dist, device, bands: int = 4, group=None) -> None:
+        import torch
+        self.torch, self.session, self.h, self.dist, self.group = torch, session, handle, dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.m, self.n_total, self.k = m, n_total, handle.k
+        self.c0, self.c1 = shard_columns(n_total, self.world, self.rank)
+        if (handle.col_begin, handle.col_end) != (self.c0, self.c1):
+            raise ValueError("the weight handle does not hold this rank's column shard")
+        self.device = torch.device(device)
+        self.bands = plan_bands(m, bands)
+        self.y = torch.empty((m, n_total), dtype=torch.float32, device=self.device)
+        self.fence = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.comm = torch.cuda.Stream(device=self.device)
+        mine = session.ipc_export(self.y.data_ptr())
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=group)
+        self.peers = []  # (peer rank, mapped pointer to the peer's Y, base for ipc_close, push stream)
+        try:
+            for r, (hb, off) in enumerate(every):
+                if r != self.rank:
+                    ptr, base = session.ipc_open(hb, off, self.device.index)
+                    self.peers.append((r, ptr, base, torch.cuda.Stream(device=self.device)))
+        except Exception:
+            self._unmap()
+            raise
+
+    def _unmap(self) -> None:
+        for _, _, base, _ in self.peers:
+            self.session.ipc_close(base)
+        self.peers = []
+
+    def close(self) -> None:
+        """Unmaps the peers' Y on every rank before any rank may free its own."""
+        self.torch.cuda.synchronize(self.device)
+        self._unmap()
+        self.dist.barrier(group=self.group)
+
+    def _fence(self, s0) -> None:
+        torch = self.torch
+        e = torch.cuda.Event()
+        e.record(s0)
+        self.comm.wait_event(e)
+        for _, _, _, ps in self.peers:
+            e = torch.cuda.Event()
+            e.record(ps)
+            self.comm.wait_event(e)
+        with torch.cuda.stream(self.comm):
+            self.dist.all_reduce(self.fence, group=self.group)
+
+    def run(self, x, stream=None):
+        """x: device fp32 [m][k].  Returns Y (this object's [m][n_total] tensor),
+        complete on every rank once the caller's stream reaches this point."""
+        torch = self.torch
+        if x.shape != (self.m, self.k) or not x.is_contiguous() or x.dtype != torch.float32:
+            raise ValueError("x must be a contiguous fp32 [m, k] tensor")
+        s0 = stream or torch.cuda.current_stream(self.device)
+        n, k, c0 = self.n_total, self.k, self.c0
+        width = 4 * (self.c1 - self.c0)
+        if self.peers:
+            self._fence(s0)
+            start = torch.cuda.Event()
+            start.record(self.comm)
+            for _, _, _, ps in self.peers:
+                ps.wait_event(start)
+        yb = self.y.data_ptr()
+        for r0, r1 in self.bands:
+            off = 4 * (r0 * n + c0)
+            self.h.run_strided(x.data_ptr() + 4 * r0 * k, yb + off, r1 - r0, n, s0.cuda_stream)
+            if not self.peers:
+                continue
+            done = torch.cuda.Event()
+            done.record(s0)
+            for _, ptr, _, ps in self.peers:
+                ps.wait_event(done)
+                self.session.copy_2d(ptr + off, 4 * n, yb + off, 4 * n, width, r1 - r0, ps.cuda_stream)
+        if self.peers:
+            self._fence(s0)
+            fin = torch.cuda.Event()
+            fin.record(self.comm)
+            s0.wait_event(fin)
+        return self.y

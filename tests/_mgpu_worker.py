@@ -1,7 +1,8 @@
 """Worker for tests/test_multigpu_gpu.py (one process per GPU under
 torch.distributed.run): N-sharded int4 GEMM (+ LoRA) through the library on
-each rank, NCCL all-gather of the fp32 Y shards, rank 0 checks the gathered
-Y against the oracle and against an unsharded run on its own GPU."""
+each rank, exchange of the fp32 Y shards (NCCL all-gather, the banded
+ShardedGemm pipeline, and the copy-engine push of ShardedGemmPush), rank 0 checks the gathered Y against the oracle and
+against an unsharded run on its own GPU."""
 from __future__ import annotations
 
 import datetime
@@ -29,7 +30,7 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     s = backend.BackendSession()
     ok = True
-    for (m, k, n, r) in [(300, 1024, 2048, 8), (4, 4096, 4096, 0), (600, 2048, 1600, 0)]:
+    for (m, k, n, r) in [(300, 1024, 2048, 8), (4, 4096, 4096, 0), (600, 2048, 1600, 0), (520, 512, 200, 0)]:
         w_kn, packed, scales = synth.make_weights(k, n, 0.003, 0.01, seed=k + n)
         x = synth.make_x(m, k, seed=m)
         a = synth.normal(k * r, 3, 0.02).reshape(k, r) if r else None
@@ -44,10 +45,36 @@ def main() -> int:
             yv = torch.empty((m, c1 - c0), dtype=torch.float32, device=dev)
             h.run(xd.data_ptr(), yv.data_ptr(), m, torch.cuda.current_stream().cuda_stream)
             ys[:, : c1 - c0] = yv
+            # the banded pipeline (GEMM of band b+1 overlapping the all-gather
+            # and re-layout of band b) into a padded row-major Y
+            piped = sharding.ShardedGemm(s, h, m, n, dist, dev, bands=2)
+            yp = torch.full((m, n + 12), float("nan"), dtype=torch.float32, device=dev)
+            piped.run(xd, yp)
+            torch.cuda.synchronize(dev)
+            yp = yp.cpu().numpy()
+            # the copy-engine push exchange into IPC-mapped row-major Y
+            # (run twice, Y poisoned before each call: the start fence orders the
+            # poison before the peers' pushes, the end fence every push before the read)
+            push = sharding.ShardedGemmPush(s, h, m, n, dist, dev, bands=2)
+            for _ in range(2):
+                push.y.fill_(float("nan"))
+                ypush = push.run(xd)
+            torch.cuda.synchronize(dev)
+            yq = ypush.cpu().numpy()
+            push.close()
         y = sharding.allgather_columns(ys, n, dist).cpu().numpy()
+        pad_ok = bool(np.isnan(yp[:, n:]).all())
+        yp = yp[:, :n]
         if rank == 0:
             full = s.q4gemm(x, packed, scales, n, a, b, 16.0) if r else s.q4gemm(x, packed, scales, n)
-            same = np.max(np.abs(full - y)) <= 1e-5 * max(1.0, float(np.max(np.abs(full))))
+            tol = 1e-5 * max(1.0, float(np.max(np.abs(full))))
+            e_plain, e_band = float(np.max(np.abs(full - y))), float(np.max(np.abs(full - yp)))
+            e_push = float(np.max(np.abs(full - yq)))
+            same = e_plain <= tol and e_band <= tol and e_push <= tol and pad_ok
+            if not same:
+                bad = np.argwhere(np.abs(full - yp) > tol)
+                print(f"plain err {e_plain}, banded err {e_band}, push err {e_push}, tol {tol}, padding kept {pad_ok}, "
+                      f"banded mismatches {len(bad)} first {bad[:4].tolist()} last {bad[-4:].tolist()}", flush=True)
             sel = np.r_[0:2, m - 2:m]
             ref = Oracle().gemm(x[sel], w_kn, scales)
             if r:
@@ -58,7 +85,7 @@ def main() -> int:
             else:
                 rep = parity.gemm_error_report(y[sel], ref, x, 8 * float(np.abs(scales).max()), k)
                 good = rep["max_abs"] <= rep["abs_bound"] and rep["norm_rel"] <= parity.GEMM_NORM_REL_TOL
-            print(f"shape {(m, k, n, r)} world {world}: gathered==unsharded {same}, oracle {rep}", flush=True)
+            print(f"shape {(m, k, n, r)} world {world}: gathered==banded==pushed==unsharded {same}, oracle {rep}", flush=True)
             ok &= bool(same and good)
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)

@@ -111,6 +111,21 @@ def test_invalid_arguments_return_1_before_device_work(session):
     assert sg(_f(x), _f(x), _f(y), 64, 64, 32, None) == 1
     assert session.raw("spaceslug_sgemm_device")(None, None, None, 1, 1, 1, None) == 1
     assert session.raw("spaceslug_q4_weights_run")(None, 16, 16, 1, None) == 1
+    rs = session.raw("spaceslug_q4_weights_run_strided")
+    assert rs(None, 16, 16, 1, 64, None) == 1
+    assert session.raw("spaceslug_ipc_export")(None, None, None) == 1
+    assert session.raw("spaceslug_ipc_open")(None, 0, 0, None, None) == 1
+    assert session.raw("spaceslug_ipc_close")(None) == 1
+    c2 = session.raw("spaceslug_copy_2d")
+    assert c2(None, 64, 16, 64, 64, 1, None) == 1
+    assert c2(16, 32, 16, 64, 64, 1, None) == 1   # width > dpitch
+    assert c2(16, 64, 16, 64, 0, 1, None) == 0    # nothing to copy
+    rl = session.raw("spaceslug_shards_relayout")
+    assert rl(None, 16, 2, 4, 8, 16, 16, None) == 1
+    assert rl(16, 16, 2, 4, 8, 17, 17, None) == 1   # n_total > parts * width
+    assert rl(16, 16, 2, 4, 8, 16, 15, None) == 1   # ld_y < n_total
+    assert rl(16, 16, 0, 4, 8, 16, 16, None) == 1
+    assert rl(16, 16, 2, 0, 8, 16, 16, None) == 0   # nothing to move, no device work
     assert session.raw("spaceslug_q4_weights_destroy")(None) == 1
     assert session.raw("spaceslug_q4_set_operand_type")(7) == -1
 

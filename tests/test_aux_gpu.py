@@ -1,4 +1,5 @@
-"""GPU: bit-exact dequant, device packer, and the legacy LoRA delta ABI."""
+"""GPU: bit-exact dequant, device packer, the legacy LoRA delta ABI, and the
+re-layout of all-gathered column shards."""
 from __future__ import annotations
 
 import numpy as np
@@ -58,3 +59,20 @@ def test_lora_delta_against_shader_restatement(session, oracle, cuda, m, rank):
     y = session.lora_delta(x, a, b, m, rank)
     ref = oracle.lora_delta_f32(x, a, b, m, rank)
     assert np.allclose(y, ref, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("parts,rows,width,n_total,ld", [(2, 300, 1024, 2048, 2048), (8, 64, 3584, 28672, 28672),
+                                                        (2, 5, 104, 200, 200), (3, 7, 13, 37, 41), (4, 33, 8, 30, 64)])
+def test_shards_relayout(session, cuda, parts, rows, width, n_total, ld):
+    """Rank-major [parts][rows][width] -> rows of Y [rows][ld], columns [0, n_total),
+    bit-exact; the padding columns of the last shard and Y's columns >= n_total untouched."""
+    import torch
+    g = torch.from_numpy(synth.lcg_floats(parts * rows * width, 9, -4.0, 4.0)).to(cuda)
+    y = torch.full((rows, ld), 123.0, dtype=torch.float32, device=cuda)
+    session.shards_relayout(g.data_ptr(), y.data_ptr(), parts, rows, width, n_total, ld,
+                            torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = g.cpu().numpy().reshape(parts, rows, width).transpose(1, 0, 2).reshape(rows, parts * width)[:, :n_total]
+    out = y.cpu().numpy()
+    assert np.array_equal(out[:, :n_total].view(np.uint32), ref.view(np.uint32))
+    assert (out[:, n_total:] == 123.0).all()

@@ -179,3 +179,26 @@ def test_gemm_pair_kernel_on_large_ragged_problem(session, oracle, cuda, n):
     ref = oracle.gemm(x[sel], w_kn, scales)
     _check(y[sel], ref, x, scales, k)
     assert np.all(np.isfinite(y))
+
+
+@pytest.mark.parametrize("m,n,k,c0,c1,ld", [(1100, 4500, 1152, 0, 4096, 4500),   # pair kernel, pitched store
+                                            (1100, 4500, 1152, 400, 4500, 4504),  # pair kernel, shard at an offset
+                                            (300, 200, 512, 104, 200, 200),       # single-CTA kernel: scratch + copy
+                                            (4, 4096, 1024, 2048, 4096, 4096),    # decode: scratch + copy
+                                            (1100, 4501, 1152, 1, 4501, 4503)])   # unaligned Y: scratch + copy
+def test_run_strided_writes_only_its_columns(session, cuda, m, n, k, c0, c1, ld):
+    """spaceslug_q4_weights_run_strided: a column-shard handle writes its
+    product into Y[:, c0:c1] of a pitched row-major Y, bit-identical to the
+    dense run of the same handle, and leaves every other column alone."""
+    import torch
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=n + c0)
+    x = torch.from_numpy(synth.make_x(m, k, seed=7)).to(cuda)
+    with session.weights(packed, scales, k, n, c0, c1) as h:
+        dense = torch.empty((m, c1 - c0), dtype=torch.float32, device=cuda)
+        h.run(x.data_ptr(), dense.data_ptr(), m, torch.cuda.current_stream().cuda_stream)
+        y = torch.full((m, ld), 7.0, dtype=torch.float32, device=cuda)
+        h.run_strided(x.data_ptr(), y.data_ptr() + 4 * c0, m, ld, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        out = y.cpu().numpy()
+    assert np.array_equal(out[:, c0:c1].view(np.uint32), dense.cpu().numpy().view(np.uint32))
+    assert (out[:, :c0] == 7.0).all() and (out[:, c1:] == 7.0).all()

@@ -68,3 +68,21 @@ def test_shard_columns_cover_every_column_once():
             assert (c1 - c0) % 8 == 0 or c1 == n
             cols.extend(range(c0, c1))
         assert cols == list(range(n))
+
+
+def test_plan_bands_cover_rows_in_tile_multiples():
+    from spaceslug_b200 import sharding
+    assert sharding.plan_bands(4096, 2) == [(0, 2048), (2048, 4096)]
+    assert sharding.plan_bands(4096, 4) == [(0, 1024), (1024, 2048), (2048, 3072), (3072, 4096)]
+    assert sharding.plan_bands(300, 4) == [(0, 300)]            # a 44-row tail joins the band before it
+    assert sharding.plan_bands(520, 2) == [(0, 256), (256, 520)]
+    assert sharding.plan_bands(600, 4) == [(0, 256), (256, 600)]
+    assert sharding.plan_bands(5, 3) == [(0, 5)]
+    for m in (1, 255, 256, 257, 4095, 4096, 5000):
+        for b in (1, 2, 3, 4, 8):
+            bands = sharding.plan_bands(m, b)
+            assert bands[0][0] == 0 and bands[-1][1] == m and len(bands) <= b
+            assert all(r0 < r1 for r0, r1 in bands)
+            assert all(a[1] == c[0] for a, c in zip(bands, bands[1:]))
+            assert all(r0 % 256 == 0 for r0, _ in bands)
+            assert len(bands) == 1 or all(r1 - r0 >= 256 for r0, r1 in bands)
