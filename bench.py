@@ -561,14 +561,15 @@ def sgemm_gpu(args, dist: Dist, torch, session) -> dict:
 def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     """columns of W sharded over the ranks; Y all-gathered over NVLink.
 
-    Timed per step (L2 flushed before each), for 1, 2 and 4 row bands, both
+    Timed per step (L2 flushed before each), over row-band counts, the
     exchanges of the sharding module: ShardedGemm (GEMM of row band b+1 on the
     compute stream while band b is all-gathered by NCCL and re-laid out into
     row-major Y) and ShardedGemmPush (GEMM writes into a row-major Y every
-    peer has mapped; copy engines push each finished band to the peers).  The
-    value is the fastest of the six; the GEMM alone, the NCCL all-gather of the
-    whole Y alone and the re-layout alone are timed the same way for the
-    breakdown."""
+    peer has mapped; each finished band is pushed to the peers by copy
+    engines, or by a push kernel on SMs the GEMM leaves free).  The value is
+    the fastest variant (named in the line); the GEMM alone, the NCCL
+    all-gather of the whole Y alone and the re-layout alone are timed the
+    same way for the breakdown."""
     from spaceslug_b200 import sharding
     dev = torch.device("cuda", dist.local)
     cfg = synth.CONFIGS["mlp70b"]
@@ -642,17 +643,20 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     best = (best[0], best[1], best[2], "nccl")
     del y
     torch.cuda.empty_cache()
-    for bands in (1, 2, 4):
-        push = sharding.ShardedGemmPush(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands)
+    for engine, bands, sms in (("copy", 1, 0), ("copy", 2, 0), ("copy", 4, 0), ("sm", 2, 16), ("sm", 4, 16),
+                               ("sm", 4, 24), ("sm", 8, 16)):
+        push = sharding.ShardedGemmPush(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands, engine=engine,
+                                        push_sms=sms or 16)
         n0 = session.launch_count()
         push.run(x, stream)
         launches = session.launch_count() - n0
         stream.synchronize()
         dist.barrier()
         t_ms = timed(lambda: push.run(x, stream), steps)
-        detail[f"push_bands{bands}_ms"] = t_ms
+        name = f"push_{engine}_bands{bands}" + (f"_sms{sms}" if engine == "sm" else "")
+        detail[name + "_ms"] = t_ms
         if t_ms < best[1]:
-            best = (bands, t_ms, launches, "push")
+            best = (bands, t_ms, launches, name)
         push.close()
         del push
         torch.cuda.empty_cache()

@@ -226,6 +226,17 @@ int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m,
 int spaceslug_q4_weights_run_strided(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, uint64_t ld_y,
                                      void* stream);
 
+/* Caps the SMs a GEMM launch of this handle occupies (0: all, else >= 2), so
+ * that kernels on other streams (an exchange running beside the GEMM) find
+ * free SMs.  Decode-sized launches (m <= 8) ignore it. */
+int spaceslug_q4_weights_set_sm_budget(spaceslug_q4_weights* w, uint32_t sms);
+/* Stores rows [0, rows) x columns [0, width) of the pitched fp32 block at
+ * `src` (row pitch ld floats) to the same offsets in npeers (<= 7) peer-mapped
+ * buffers (peer_dst: host array of device pointers), with `ctas` CTAs of plain
+ * global stores over NVLink; asynchronous on `stream`. */
+int spaceslug_push_rows(const float* src, float* const* peer_dst, uint32_t npeers, uint32_t rows, uint32_t width,
+                        uint64_t ld, uint32_t ctas, void* stream);
+
 /* CUDA IPC between the ranks of one node (no reference counterpart).
  * export: 64-byte handle of the device allocation holding `ptr` and the byte
  * offset of ptr inside it.  open: maps a peer's allocation on `device`

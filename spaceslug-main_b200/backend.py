@@ -61,6 +61,8 @@ _SIGNATURES = {
     "spaceslug_sgemm_device": ([_vp, _vp, _vp, _u32, _u32, _u32, _vp], ctypes.c_int),
     "spaceslug_shards_relayout": ([_vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, _vp], ctypes.c_int),
     "spaceslug_q4_weights_run_strided": ([_vp, _vp, _vp, _u32, ctypes.c_uint64, _vp], ctypes.c_int),
+    "spaceslug_q4_weights_set_sm_budget": ([_vp, _u32], ctypes.c_int),
+    "spaceslug_push_rows": ([_vp, ctypes.POINTER(_vp), _u32, _u32, _u32, ctypes.c_uint64, _u32, _vp], ctypes.c_int),
     "spaceslug_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "spaceslug_ipc_open": ([_vp, ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)],
                            ctypes.c_int),
@@ -291,6 +293,12 @@ class BackendSession:
     def ipc_close(self, base: int) -> None:
         self._call("spaceslug_ipc_close", base)
 
+    def push_rows(self, src: int, peer_dst: list[int], rows: int, width: int, ld: int, ctas: int,
+                  stream: int = 0) -> None:
+        """Device pointers: rows x width floats (pitch ld) from src to the same offsets in each peer buffer."""
+        arr = (_vp * max(1, len(peer_dst)))(*peer_dst)
+        self._call("spaceslug_push_rows", src, arr, len(peer_dst), rows, width, ld, ctas, stream or None)
+
     def copy_2d(self, dst: int, dpitch: int, src: int, spitch: int, width_bytes: int, rows: int,
                 stream: int = 0) -> None:
         self._call("spaceslug_copy_2d", dst, dpitch, src, spitch, width_bytes, rows, stream or None)
@@ -372,6 +380,10 @@ class Q4Weights:
 
     def run(self, x: int, y: int, m: int, stream: int = 0) -> None:
         self.session._call("spaceslug_q4_weights_run", self.handle, x, y, m, stream or None)
+
+    def set_sm_budget(self, sms: int) -> None:
+        """At most `sms` SMs for this handle's GEMM launches (0: all)."""
+        self.session._call("spaceslug_q4_weights_set_sm_budget", self.handle, sms)
 
     def run_strided(self, x: int, y: int, m: int, ld_y: int, stream: int = 0) -> None:
         """Y rows with pitch ld_y floats (this handle's columns only)."""

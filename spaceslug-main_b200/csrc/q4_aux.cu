@@ -462,6 +462,64 @@ int launch_shards_relayout(const float* gathered, float* y, int parts, int rows,
     return static_cast<int>(cudaGetLastError());
 }
 
+namespace {
+
+// Rows [0, rows) x columns [0, width) of a pitched fp32 block on this GPU,
+// stored to the same place in up to kMaxPeers peers' buffers (plain global
+// stores through NVLink peer mappings).  Each element is read once (the band
+// was just written, so mostly from L2) and stored once per peer.  A thread
+// loads kPushUnroll elements (grid-stride apart) before it stores any, so a
+// CTA keeps that many loads in flight instead of waiting out one load
+// latency per element.  V = 4: float4 (16-byte aligned addresses, width and
+// ld multiples of 4).
+constexpr int kPushUnroll = 4;
+
+template <int V>
+__global__ void __launch_bounds__(512) push_rows_kernel(const float* __restrict__ src, PeerPtrs dst, int npeers,
+                                                        int rows, int wv, long long ldv) {
+    using T = typename std::conditional<V == 4, float4, float>::type;
+    const T* s = reinterpret_cast<const T*>(src);
+    const long long total = static_cast<long long>(rows) * wv;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long base = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; base < total;
+         base += kPushUnroll * stride) {
+        T v[kPushUnroll];
+        long long at[kPushUnroll];
+#pragma unroll
+        for (int u = 0; u < kPushUnroll; ++u) {
+            const long long i = base + u * stride;
+            at[u] = -1;
+            if (i < total) {
+                const long long r = i / wv;
+                at[u] = r * ldv + (i - r * wv);
+                v[u] = s[at[u]];
+            }
+        }
+        for (int q = 0; q < npeers; ++q) {
+            T* d = reinterpret_cast<T*>(dst.p[q]);
+#pragma unroll
+            for (int u = 0; u < kPushUnroll; ++u)
+                if (at[u] >= 0) d[at[u]] = v[u];
+        }
+    }
+}
+
+}  // namespace
+
+int launch_push_rows(const float* src, const PeerPtrs& peers, int npeers, int rows, int width, long long ld, int ctas,
+                     cudaStream_t stream) {
+    if (npeers < 0 || npeers > kMaxPeers || rows < 0 || width < 1 || ld < width || ctas < 1)
+        return static_cast<int>(cudaErrorInvalidValue);
+    if (npeers == 0 || rows == 0) return 0;
+    bool v4 = width % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+    for (int q = 0; q < npeers; ++q) v4 = v4 && (reinterpret_cast<uintptr_t>(peers.p[q]) & 15u) == 0;
+    if (v4)
+        push_rows_kernel<4><<<ctas, 512, 0, stream>>>(src, peers, npeers, rows, width / 4, ld / 4);
+    else
+        push_rows_kernel<1><<<ctas, 512, 0, stream>>>(src, peers, npeers, rows, width, ld);
+    return static_cast<int>(cudaGetLastError());
+}
+
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream) {
     lora_delta64_kernel<<<M, 64, 0, stream>>>(x, a, b, y, rank);

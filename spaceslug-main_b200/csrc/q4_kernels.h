@@ -135,6 +135,14 @@ int lora_xa_chunks(int K);
 // All-gathered column shards [parts][rows][width] (rank-major) -> rows
 // [rows][ld_y] of row-major Y, columns [0, n_total) (the last shard may be
 // partly padding).  HBM-bound copy; float4 when every address is aligned.
+// Push of a pitched fp32 row block to the same offset in peers' buffers
+// (peer-mapped device pointers) by `ctas` CTAs of plain global stores.
+constexpr int kMaxPeers = 7;
+struct PeerPtrs {
+    float* p[kMaxPeers];
+};
+int launch_push_rows(const float* src, const PeerPtrs& peers, int npeers, int rows, int width, long long ld, int ctas,
+                     cudaStream_t stream);
 int launch_shards_relayout(const float* gathered, float* y, int parts, int rows, int width, int n_total,
                            long long ld_y, cudaStream_t stream);
 // CQ4 activation transform into the code basis, fp16 [M][K] -> fp16 [M][K]:

@@ -227,6 +227,7 @@ struct Problem {
     float* y;
     int M, N, K;
     long long ld_y = 0;  // row pitch of Y in floats (0: N)
+    int sm_budget = 0;   // SMs the GEMM may occupy (0: all)
 };
 
 // GEMV launch geometry.  K is split over a cluster of S CTAs (S | G, slice
@@ -324,7 +325,8 @@ int pair_capacity(DeviceCtx& c, q4::Operand16 op) {
 // kernel.
 bool use_pair_kernel(DeviceCtx& c, const Problem& p, q4::Operand16 op, int* pairs_out) {
     const long long ld = p.ld_y ? p.ld_y : p.N;
-    const int pairs = pair_capacity(c, op);
+    int pairs = pair_capacity(c, op);
+    if (p.sm_budget > 0 && pairs > p.sm_budget / 2) pairs = p.sm_budget / 2;
     if (pairs_out) *pairs_out = pairs;
     const int variant = g_gemm_variant.load();
     const bool shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && ld % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
@@ -454,7 +456,7 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     const long long ld_y = p.ld_y ? p.ld_y : p.N;
     if (ld_y != p.N && !use_pair) throw CudaError("strided Y reached a kernel without a row pitch");
     g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
-    g.sm_count = c.sm_count;
+    g.sm_count = p.sm_budget > 0 && p.sm_budget < c.sm_count ? p.sm_budget : c.sm_count;
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
               static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) * 2, 64,
               static_cast<uint32_t>(128 * g.halves), CU_TENSOR_MAP_SWIZZLE_128B);
@@ -570,6 +572,7 @@ struct spaceslug_q4_weights {
     float* lora_b = nullptr;
     int rank = 0;
     float alpha = 0.0f;
+    int sm_budget = 0;  // SMs a GEMM launch of this handle may occupy (0: all)
     // training state (allocated on first use, reset by set_lora)
     float* lora_da = nullptr;
     float* lora_db = nullptr;
@@ -964,6 +967,7 @@ int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, 
         if (current_device() != w->device) check(cudaSetDevice(w->device), "cudaSetDevice");
         Problem p{x, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, y,
                   static_cast<int>(m), w->N, w->K};
+        p.sm_budget = w->sm_budget;
         run_problem(p, static_cast<cudaStream_t>(stream));
         return SPACESLUG_OK;
     });
@@ -980,7 +984,7 @@ int spaceslug_q4_weights_run_strided(spaceslug_q4_weights* w, const float* x, fl
     return guarded([&] {
         if (current_device() != w->device) check(cudaSetDevice(w->device), "cudaSetDevice");
         Problem p{x, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, y,
-                  static_cast<int>(m), w->N, w->K, static_cast<long long>(ld_y)};
+                  static_cast<int>(m), w->N, w->K, static_cast<long long>(ld_y), w->sm_budget};
         if (ld_y == static_cast<uint64_t>(w->N) && !aligned16(y)) {
             // the kernels want a 16-byte aligned Y: product in scratch, then one copy
             // (a pitched, unaligned Y takes the same route inside run_problem)
@@ -995,6 +999,35 @@ int spaceslug_q4_weights_run_strided(spaceslug_q4_weights* w, const float* x, fl
             return SPACESLUG_OK;
         }
         run_problem(p, static_cast<cudaStream_t>(stream));
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_set_sm_budget(spaceslug_q4_weights* w, uint32_t sms) {
+    if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
+    if (sms == 1 || sms > 4096) return fail(SPACESLUG_INVALID_ARGUMENT, "sms must be 0 (all) or 2..4096");
+    w->sm_budget = static_cast<int>(sms);
+    return SPACESLUG_OK;
+}
+
+int spaceslug_push_rows(const float* src, float* const* peer_dst, uint32_t npeers, uint32_t rows, uint32_t width,
+                        uint64_t ld, uint32_t ctas, void* stream) {
+    if (!src || (npeers && !peer_dst)) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (npeers > static_cast<uint32_t>(q4::kMaxPeers)) return fail(SPACESLUG_INVALID_ARGUMENT, "at most 7 peers");
+    if (width == 0 || ld < width || ld > (uint64_t(1) << 40) || rows > (1u << 30) || width > (1u << 30))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "bad width / ld / rows");
+    if (ctas == 0 || ctas > 65535) return fail(SPACESLUG_INVALID_ARGUMENT, "ctas must be 1..65535");
+    q4::PeerPtrs pp{};
+    for (uint32_t q = 0; q < npeers; ++q) {
+        if (!peer_dst[q]) return fail(SPACESLUG_INVALID_ARGUMENT, "null peer pointer");
+        pp.p[q] = peer_dst[q];
+    }
+    if (npeers == 0 || rows == 0) return SPACESLUG_OK;
+    return guarded([&] {
+        check_launch(q4::launch_push_rows(src, pp, static_cast<int>(npeers), static_cast<int>(rows),
+                                          static_cast<int>(width), static_cast<long long>(ld), static_cast<int>(ctas),
+                                          static_cast<cudaStream_t>(stream)),
+                     "push_rows");
         return SPACESLUG_OK;
     });
 }

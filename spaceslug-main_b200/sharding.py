@@ -145,24 +145,37 @@ class ShardedGemm:
 
 
 class ShardedGemmPush:
-    """The N-sharded GEMM with the exchange on copy engines over NVLink.
+    """The N-sharded GEMM with the exchange pushed into peer-mapped Y over NVLink.
 
     Every rank's full Y [m][n_total] is one device allocation, mapped into
     every other rank by CUDA IPC (spaceslug_ipc_export / spaceslug_ipc_open).
     The GEMM of each row band writes this rank's columns [c0, c1) straight
     into its own Y (spaceslug_q4_weights_run_strided, row pitch n_total), and
-    as soon as the band is done one pitched copy per peer
-    (spaceslug_copy_2d, a copy engine, no SMs) pushes those rows into that
-    peer's Y, while the SMs run the next band.  No gather buffer and no
-    re-layout.  Two one-element NCCL all-reduces per call fence the pushes:
-    one before the first push (every rank's earlier use of its Y is done) and
-    one after the last (every rank's Y is complete).  Construct and close()
+    as soon as the band is done its rows go to the same place in every
+    peer's Y while the GEMM computes the next band.  No gather buffer and no
+    re-layout.  Two engines:
+
+    * engine="copy": one pitched copy per peer (spaceslug_copy_2d) on the
+      copy engines, no SMs.  A copy engine moves a pitched copy row by row
+      (~80 ns per row measured on B200), so this suits few peers.
+    * engine="sm": one spaceslug_push_rows kernel per band (plain peer
+      stores, each element read once and stored to every peer) on
+      `push_sms` SMs that the GEMM leaves free
+      (spaceslug_q4_weights_set_sm_budget) while a push runs beside it.
+
+    Two one-element NCCL all-reduces per call fence the pushes: one before
+    the first push (every rank's earlier use of its Y is done) and one after
+    the last (every rank's Y is complete).  Construct and close()
     collectively on every rank.
     """
 
-    def __init__(self, session, handle, m: int, n_total: int, dist, device, bands: int = 4, group=None) -> None:
+    def __init__(self, session, handle, m: int, n_total: int, dist, device, bands: int = 4, group=None,
+                 engine: str = "copy", push_sms: int = 16) -> None:
         import torch
+        if engine not in ("copy", "sm"):
+            raise ValueError("engine is 'copy' or 'sm'")
         self.torch, self.session, self.h, self.dist, self.group = torch, session, handle, dist, group
+        self.engine = engine
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.m, self.n_total, self.k = m, n_total, handle.k
@@ -170,6 +183,8 @@ class ShardedGemmPush:
         if (handle.col_begin, handle.col_end) != (self.c0, self.c1):
             raise ValueError("the weight handle does not hold this rank's column shard")
         self.device = torch.device(device)
+        self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.push_sms = max(1, min(int(push_sms), self.sm_count - 2))
         self.bands = plan_bands(m, bands)
         self.y = torch.empty((m, n_total), dtype=torch.float32, device=self.device)
         self.fence = torch.zeros(1, dtype=torch.float32, device=self.device)
@@ -177,18 +192,20 @@ class ShardedGemmPush:
         mine = session.ipc_export(self.y.data_ptr())
         every = [None] * self.world
         dist.all_gather_object(every, mine, group=group)
-        self.peers = []  # (peer rank, mapped pointer to the peer's Y, base for ipc_close, push stream)
+        self.peers = []  # (peer rank, mapped pointer to the peer's Y, base for ipc_close)
         try:
             for r, (hb, off) in enumerate(every):
                 if r != self.rank:
                     ptr, base = session.ipc_open(hb, off, self.device.index)
-                    self.peers.append((r, ptr, base, torch.cuda.Stream(device=self.device)))
+                    self.peers.append((r, ptr, base))
         except Exception:
             self._unmap()
             raise
+        n_streams = len(self.peers) if engine == "copy" else min(1, len(self.peers))
+        self.push_streams = [torch.cuda.Stream(device=self.device, priority=-1) for _ in range(n_streams)]
 
     def _unmap(self) -> None:
-        for _, _, base, _ in self.peers:
+        for _, _, base in self.peers:
             self.session.ipc_close(base)
         self.peers = []
 
@@ -203,7 +220,7 @@ class ShardedGemmPush:
         e = torch.cuda.Event()
         e.record(s0)
         self.comm.wait_event(e)
-        for _, _, _, ps in self.peers:
+        for ps in self.push_streams:
             e = torch.cuda.Event()
             e.record(ps)
             self.comm.wait_event(e)
@@ -218,24 +235,37 @@ class ShardedGemmPush:
             raise ValueError("x must be a contiguous fp32 [m, k] tensor")
         s0 = stream or torch.cuda.current_stream(self.device)
         n, k, c0 = self.n_total, self.k, self.c0
-        width = 4 * (self.c1 - self.c0)
+        cols = self.c1 - self.c0
         if self.peers:
             self._fence(s0)
             start = torch.cuda.Event()
             start.record(self.comm)
-            for _, _, _, ps in self.peers:
+            for ps in self.push_streams:
                 ps.wait_event(start)
         yb = self.y.data_ptr()
-        for r0, r1 in self.bands:
-            off = 4 * (r0 * n + c0)
-            self.h.run_strided(x.data_ptr() + 4 * r0 * k, yb + off, r1 - r0, n, s0.cuda_stream)
-            if not self.peers:
-                continue
-            done = torch.cuda.Event()
-            done.record(s0)
-            for _, ptr, _, ps in self.peers:
-                ps.wait_event(done)
-                self.session.copy_2d(ptr + off, 4 * n, yb + off, 4 * n, width, r1 - r0, ps.cuda_stream)
+        sm = self.engine == "sm" and bool(self.peers)
+        try:
+            for b, (r0, r1) in enumerate(self.bands):
+                off = 4 * (r0 * n + c0)
+                if sm:  # bands after the first run beside the previous band's push
+                    self.h.set_sm_budget(0 if b == 0 else self.sm_count - self.push_sms)
+                self.h.run_strided(x.data_ptr() + 4 * r0 * k, yb + off, r1 - r0, n, s0.cuda_stream)
+                if not self.peers:
+                    continue
+                done = torch.cuda.Event()
+                done.record(s0)
+                for ps in self.push_streams:
+                    ps.wait_event(done)
+                if sm:
+                    ps = self.push_streams[0]
+                    self.session.push_rows(yb + off, [ptr + off for _, ptr, _ in self.peers], r1 - r0, cols, n,
+                                           2 * self.push_sms, ps.cuda_stream)
+                else:
+                    for (_, ptr, _), ps in zip(self.peers, self.push_streams):
+                        self.session.copy_2d(ptr + off, 4 * n, yb + off, 4 * n, 4 * cols, r1 - r0, ps.cuda_stream)
+        finally:
+            if sm:
+                self.h.set_sm_budget(0)
         if self.peers:
             self._fence(s0)
             fin = torch.cuda.Event()

@@ -55,13 +55,15 @@ def main() -> int:
             # the copy-engine push exchange into IPC-mapped row-major Y
             # (run twice, Y poisoned before each call: the start fence orders the
             # poison before the peers' pushes, the end fence every push before the read)
-            push = sharding.ShardedGemmPush(s, h, m, n, dist, dev, bands=2)
-            for _ in range(2):
-                push.y.fill_(float("nan"))
-                ypush = push.run(xd)
-            torch.cuda.synchronize(dev)
-            yq = ypush.cpu().numpy()
-            push.close()
+            yq = {}
+            for engine in ("copy", "sm"):
+                push = sharding.ShardedGemmPush(s, h, m, n, dist, dev, bands=2, engine=engine, push_sms=8)
+                for _ in range(2):
+                    push.y.fill_(float("nan"))
+                    ypush = push.run(xd)
+                torch.cuda.synchronize(dev)
+                yq[engine] = ypush.cpu().numpy()
+                push.close()
         y = sharding.allgather_columns(ys, n, dist).cpu().numpy()
         pad_ok = bool(np.isnan(yp[:, n:]).all())
         yp = yp[:, :n]
@@ -69,7 +71,7 @@ def main() -> int:
             full = s.q4gemm(x, packed, scales, n, a, b, 16.0) if r else s.q4gemm(x, packed, scales, n)
             tol = 1e-5 * max(1.0, float(np.max(np.abs(full))))
             e_plain, e_band = float(np.max(np.abs(full - y))), float(np.max(np.abs(full - yp)))
-            e_push = float(np.max(np.abs(full - yq)))
+            e_push = max(float(np.max(np.abs(full - v))) for v in yq.values())
             same = e_plain <= tol and e_band <= tol and e_push <= tol and pad_ok
             if not same:
                 bad = np.argwhere(np.abs(full - yp) > tol)
