@@ -217,6 +217,17 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// 2-D tiled bulk tensor reduce-add shared (this CTA) -> global (fp32 add at
+// L2, per element atomic), in the thread's bulk group, with an L2 cache hint.
+__device__ __forceinline__ void tma_reduce_add_2d_hint(const void* tmap, uint32_t src, int32_t c0, int32_t c1,
+                                                       uint64_t policy) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+            reinterpret_cast<uint64_t>(tmap)),
+        "r"(src), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
 // Wait until at most N of this thread's bulk groups still read shared memory.
 template <int N>
 __device__ __forceinline__ void bulk_wait_group_read() {

@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(256) pack_kernel(const int8_t* __restrict__ b_
 // the chunks in fixed order (deterministic).
 constexpr int kXaRows = 64;
 constexpr int kXaCols = 16;
-constexpr int kXaChunk = 256;
+constexpr int kXaChunk = 128;
 constexpr int kXaXPitch = kXaChunk + 4;  // floats per staged X row
 constexpr int kXaAPitch = kXaCols + 4;   // floats per staged A row
 constexpr int kXaSmem = (kXaRows * kXaXPitch + kXaChunk * kXaAPitch) * 4;
@@ -220,22 +220,30 @@ __global__ void __launch_bounds__(256) lora_xa_kernel(const float* __restrict__ 
     const int g = tid >> 4, q = tid & 15;
     for (int kb = blockIdx.z * kchunk; kb < min(K, (blockIdx.z + 1) * kchunk); kb += kXaChunk) {
         const int kn = min(kXaChunk, K - kb);  // a multiple of 32 (K % 32 == 0)
-        // stage X rows m0.. (zero past M) and A rows kb.. (zero past rank)
-        const bool xvec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;  // else scalar loads
+        // stage X rows m0.. (zero past M) and A rows kb.. (zero past rank).
+        // Aligned X goes by cp.async (16 bytes each, all of a thread's copies in
+        // flight together), else by scalar loads.
+        const bool xvec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && K % 4 == 0;
         for (int i = tid; i < kXaRows * (kXaChunk / 4); i += 256) {
             const int r = i / (kXaChunk / 4), c4 = (i % (kXaChunk / 4)) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            float* dst = xs + r * kXaXPitch + c4;
             if (m0 + r < M && c4 < kn) {
                 const float* src = x + static_cast<size_t>(m0 + r) * K + kb + c4;
-                v = xvec ? __ldg(reinterpret_cast<const float4*>(src))
-                         : make_float4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+                if (xvec) {
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+                } else {
+                    *reinterpret_cast<float4*>(dst) = make_float4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+                }
+            } else {
+                *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            *reinterpret_cast<float4*>(xs + r * kXaXPitch + c4) = v;
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
         for (int i = tid; i < kXaChunk * kXaCols; i += 256) {
             const int k = i / kXaCols, j = i % kXaCols;
             as[k * kXaAPitch + j] = (k < kn && j < cols) ? __ldg(a + static_cast<size_t>(kb + k) * rank + j0 + j) : 0.0f;
         }
+        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
 #pragma unroll 4
         for (int k = q; k < kXaChunk; k += 16) {
@@ -315,6 +323,28 @@ __global__ void __launch_bounds__(256) lora_xa_reduce_kernel(const float* __rest
     float s = 0.0f;
     for (int z = 0; z < chunks; ++z) s += partial[static_cast<size_t>(z) * MR + i];
     t[i] = s;
+}
+
+// T = sum over chunks of partial[z][M * rank] for 32 outputs per CTA: warp g
+// sums chunks g, g + 8, g + 16, ... in order, then one warp adds the eight
+// partial sums in order (deterministic, 8x the loads in flight of one
+// thread per output).
+__global__ void __launch_bounds__(256) lora_xa_sum_kernel(const float* __restrict__ partial, float* __restrict__ t,
+                                                          int MR, int chunks) {
+    __shared__ float ps[8][32];
+    const int g = threadIdx.x >> 5, o = threadIdx.x & 31;
+    const int i = blockIdx.x * 32 + o;
+    float s = 0.0f;
+    if (i < MR)
+        for (int z = g; z < chunks; z += 8) s += partial[static_cast<size_t>(z) * MR + i];
+    ps[g][o] = s;
+    __syncthreads();
+    if (g == 0 && i < MR) {
+        float v = ps[0][o];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) v += ps[q][o];
+        t[i] = v;
+    }
 }
 
 // Legacy delta (vulkan-runtime/shaders/lora_delta.comp:10-21): one CTA of 64
@@ -397,8 +427,7 @@ int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int r
         const int W = (rank + 15) / 16 * 64;
         lora_xa_reduce_kernel<<<(M * W + 255) / 256, 256, 0, stream>>>(partial, t, M, rank, chunks, row_exp, t_op);
     } else {
-        lora_xa_reduce_kernel<<<(M * rank + 255) / 256, 256, 0, stream>>>(partial, t, M, rank, chunks, nullptr,
-                                                                          nullptr);
+        lora_xa_sum_kernel<<<(M * rank + 31) / 32, 256, 0, stream>>>(partial, t, M * rank, chunks);
     }
     return static_cast<int>(cudaGetLastError());
 }

@@ -5,8 +5,11 @@
 // Blackwell tensor-core pipeline.  One CTA per SM walks output tiles of
 // (128*H) x 128; per tile and 64-wide k-step:
 //
-//   warp 0        TMA producer: X tile (16-bit, 64 x 128H, 128B swizzle) and
-//                 the raw packed W tile (128 columns x 32 bytes);
+//   warp 0        TMA producer of X tiles (16-bit, 64 x 128H, 128B swizzle);
+//   warp 14       TMA producer of the raw packed W tiles (128 columns x 32
+//                 bytes) into their own deeper ring, released by the dequant
+//                 warps, so the weight stream runs ahead of the MMA instead
+//                 of waiting for it to free a whole stage;
 //   warp 1        allocates TMEM (2 accumulator buffers x H x 128 columns);
 //                 one elected thread issues tcgen05.mma kind::f16 (M=128,
 //                 N=128, K=16; H row halves share one B tile), commits each
@@ -53,23 +56,28 @@ namespace {
 
 constexpr int kBN = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 448;  // 14 warps
+constexpr int kThreads = 480;  // 15 warps
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarp0 = 10;
 constexpr int kEpiWarps = 4;
+constexpr int kRawWarp = 14;
+constexpr int kScaleAhead = 8;  // k-steps of scales in flight per dequant thread
 
 template <int H>
 struct Cfg {
     static constexpr int kBM = 128 * H;
-    static constexpr int kStages = H == 2 ? 4 : 6;
+    static constexpr int kStages = H == 2 ? 4 : 6;  // X + dequantised-W ring
+    static constexpr int kRawStages = 8;            // packed-W ring
     static constexpr int kABytes = kBM * kBK * 2;  // 16 KB per 128-row half
     static constexpr int kBBytes = kBN * kBK * 2;  // 16 KB
     static constexpr int kRBytes = kBN * kBK / 2;  // 4 KB (packed nibbles)
     static constexpr int kAOff = 0;
     static constexpr int kBOff = kAOff + kStages * kABytes;
     static constexpr int kROff = kBOff + kStages * kBBytes;
-    static constexpr int kBarOff = kROff + kStages * kRBytes;
-    static constexpr int kNumBars = 4 * kStages + 2 + 2 + 1;  // ring, acc_full[2], acc_empty[2], done
+    static constexpr int kBarOff = kROff + kRawStages * kRBytes;
+    // full_a, full_b, empty [kStages]; full_r, empty_r [kRawStages];
+    // acc_full[2], acc_empty[2], done
+    static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 2 + 2 + 1;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kLutOff = kMiscOff + 16;     // CQ4: 256 f16 pairs (codebook[b & 15], codebook[b >> 4])
     static constexpr int kBytes = kLutOff + 1024;
@@ -88,6 +96,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const uint32_t* __restrict__ lut, __half* __restrict__ y16, int* __restrict__ status) {
     using C = Cfg<H>;
     constexpr int ST = C::kStages;
+    constexpr int RT = C::kRawStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -98,12 +107,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t r_s = base + C::kROff;
     const uint32_t bar = base + C::kBarOff;
     auto full_a = [&](int s) { return bar + 8u * s; };
-    auto full_r = [&](int s) { return bar + 8u * (ST + s); };
-    auto full_b = [&](int s) { return bar + 8u * (2 * ST + s); };
-    auto empty = [&](int s) { return bar + 8u * (3 * ST + s); };
-    auto acc_full = [&](int b) { return bar + 8u * (4 * ST + b); };
-    auto acc_empty = [&](int b) { return bar + 8u * (4 * ST + 2 + b); };
-    const uint32_t done_bar = bar + 8u * (4 * ST + 4);
+    auto full_b = [&](int s) { return bar + 8u * (ST + s); };
+    auto empty = [&](int s) { return bar + 8u * (2 * ST + s); };
+    auto full_r = [&](int r) { return bar + 8u * (3 * ST + r); };
+    auto empty_r = [&](int r) { return bar + 8u * (3 * ST + RT + r); };
+    auto acc_full = [&](int b) { return bar + 8u * (3 * ST + 2 * RT + b); };
+    auto acc_empty = [&](int b) { return bar + 8u * (3 * ST + 2 * RT + 2 + b); };
+    const uint32_t done_bar = bar + 8u * (3 * ST + 2 * RT + 4);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
 
@@ -118,9 +128,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < ST; ++s) {
             mbar_init(full_a(s), 1);
-            mbar_init(full_r(s), 1);
             mbar_init(full_b(s), kDequantWarps);
             mbar_init(empty(s), 1);
+        }
+        for (int r = 0; r < RT; ++r) {
+            mbar_init(full_r(r), 1);
+            mbar_init(empty_r(r), kDequantWarps);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
@@ -145,25 +158,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
-        // ------------------------------------------------------ producer --
+        // -------------------------------------------------- X producer --
         if (lane == 0) {
             int it = 0;
             bool ok = true;
-            // The packed weights do not depend on the previous launch (the X
-            // cast, the X*A projection): the first tile's first ST raw stages
-            // go out before griddepcontrol.wait.
-            int pre = 0;
-            if (static_cast<int>(blockIdx.x) < tiles) {
-                const int n00 = (static_cast<int>(blockIdx.x) / MT) * kBN;
-                pre = KT < ST ? KT : ST;
-                for (int kt = 0; kt < pre; ++kt) {
-                    mbar_arrive_expect_tx(full_r(kt), C::kRBytes);
-                    tma_load_2d(r_s + kt * C::kRBytes, &tmap_w, full_r(kt), kt * (kBK / 8), n00);
-                }
-            }
-            pdl_wait();
+            pdl_wait();  // X16 (and T) are written by the previous launches
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int m0 = (t % MT) * C::kBM, n0 = (t / MT) * kBN;
+                const int m0 = (t % MT) * C::kBM;
                 for (int kt = 0; kt < KS; ++kt, ++it) {
                     const int s = it % ST;
                     const uint32_t ph = (it / ST) & 1u;
@@ -174,21 +175,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(full_a(s), C::kABytes);
                     if (kt < KT) {
                         tma_load_2d(a_s + s * C::kABytes, &tmap_x, full_a(s), kt * kBK, m0);
-                        if (it >= pre) {
-                            mbar_arrive_expect_tx(full_r(s), C::kRBytes);
-                            tma_load_2d(r_s + s * C::kRBytes, &tmap_w, full_r(s), kt * (kBK / 8), n0);
-                        }
-                    } else {  // LoRA stage: the T operand; no packed weights
+                    } else {  // LoRA stage: the T operand
                         tma_load_2d(a_s + s * C::kABytes, &tmap_t, full_a(s), (kt - KT) * kBK, m0);
-                        mbar_arrive(full_r(s));
                     }
                 }
             }
             if (*abort_flag) {  // let the copies in flight land before exit
-                for (int j = (it > ST ? it - ST : 0); j < it; ++j) {
-                    mbar_drain(full_a(j % ST), (j / ST) & 1u);
-                    mbar_drain(full_r(j % ST), (j / ST) & 1u);
+                for (int j = (it > ST ? it - ST : 0); j < it; ++j) mbar_drain(full_a(j % ST), (j / ST) & 1u);
+            }
+        }
+    } else if (warp == kRawWarp) {
+        // -------------------------------------------- packed-W producer --
+        // The packed weights do not depend on the previous launch (the X cast,
+        // the X*A projection): no griddepcontrol.wait here.
+        if (lane == 0) {
+            int ir = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int n0 = (t / MT) * kBN;
+                for (int kt = 0; kt < KT; ++kt, ++ir) {
+                    const int r = ir % RT;
+                    const uint32_t ph = (ir / RT) & 1u;
+                    if (!mbar_wait(empty_r(r), ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_r(r), C::kRBytes);
+                    tma_load_2d(r_s + r * C::kRBytes, &tmap_w, full_r(r), kt * (kBK / 8), n0);
                 }
+            }
+            if (*abort_flag) {
+                for (int j = (ir > RT ? ir - RT : 0); j < ir; ++j) mbar_drain(full_r(j % RT), (j / RT) & 1u);
             }
         }
     } else if (warp == 1) {
@@ -235,46 +252,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------- dequant --
         const int dt = tid - 64;
         const int nl = dt >> 1, hh = dt & 1;  // unit: column nl, group half hh of the k-step
-        int it = 0;
+        int it = 0, ir = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const int n = (t / MT) * kBN + nl;
             const bool col_ok = n < N;
             const float cs = (col_exp != nullptr && col_ok) ? exp2i(col_exp[n]) : 1.0f;
             const float* srow = scales + static_cast<size_t>(col_ok ? n : 0) * G;
-            // Scales of the next four k-steps in flight (L2 latency exceeds one
-            // k-step), rotated through registers.
+            // Scales of the next kScaleAhead k-steps in flight (L2 latency spans
+            // several k-steps), rotated through registers.
             auto scale_at = [&](int kt) {
                 const int g = kt * 2 + hh;
                 return (col_ok && g < G) ? __ldg(srow + g) : 0.0f;
             };
-            float s0 = scale_at(0), s1 = scale_at(1), s2 = scale_at(2), s3 = scale_at(3);
+            float sq[kScaleAhead];
+#pragma unroll
+            for (int j = 0; j < kScaleAhead; ++j) sq[j] = scale_at(j);
             for (int kt = 0; kt < KS; ++kt, ++it) {
                 const int s = it % ST;
                 const uint32_t ph = (it / ST) & 1u;
-                const float sc = s0;
-                s0 = s1;
-                s1 = s2;
-                s2 = s3;
-                s3 = scale_at(kt + 4);
-                if (!mbar_wait(full_r(s), ph, abort_flag, status, kStatusTimeoutDequant)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
+                const float sc = sq[0];
+#pragma unroll
+                for (int j = 0; j + 1 < kScaleAhead; ++j) sq[j] = sq[j + 1];
+                sq[kScaleAhead - 1] = scale_at(kt + kScaleAhead);
+                uint4 out[4];
                 if (kt < KT) {
+                    const int r = ir % RT;
+                    const uint32_t rph = (ir / RT) & 1u;
+                    ++ir;
+                    if (!mbar_wait_warp(full_r(r), rph, abort_flag, status, kStatusTimeoutDequant)) {
+                        ok = false;
+                        break;
+                    }
                     const uint4 q =
-                        *reinterpret_cast<const uint4*>(smem + C::kROff + s * C::kRBytes + nl * 32 + hh * 16);
+                        *reinterpret_cast<const uint4*>(smem + C::kROff + r * C::kRBytes + nl * 32 + hh * 16);
                     const float sv = sc * cs;
                     const float2 s2v = make_float2(sv, sv);
                     const __half2 s2h = __float2half2_rn(sv);
                     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
                     if (lut == nullptr) {
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const int chunk = (hh * 4 + j) ^ (nl & 7);
-                            *reinterpret_cast<uint4*>(brow + chunk * 16) = dequant_f16x2_or<T16>(words[j], s2v, s2h);
-                        }
+                        for (int j = 0; j < 4; ++j) out[j] = dequant_f16x2_or<T16>(words[j], s2v, s2h);
                     } else {
                         // CQ4: pair (k, k+1) = RN16(codebook[idx] * norm), idx from byte b of the word
 #pragma unroll
@@ -286,10 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const __half2 w = __hmul2(*reinterpret_cast<const __half2*>(&e), s2h);
                                 o[b] = *reinterpret_cast<const uint32_t*>(&w);
                             }
-                            const int chunk = (hh * 4 + j) ^ (nl & 7);
-                            *reinterpret_cast<uint4*>(brow + chunk * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                            out[j] = make_uint4(o[0], o[1], o[2], o[3]);
                         }
                     }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty_r(r));  // the packed stage is consumed
                 } else {
                     // LoRA stage q: (alpha/r) * B_lora[16q .. 16q+15, n] * 2^f_n as bf16;
                     // positions [0,16) hi, [16,32) hi (hh = 0), [32,48) lo, [48,64) 0 (hh = 1)
@@ -313,16 +332,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const uint4 c0 = make_uint4(pk[0], pk[1], pk[2], pk[3]), c1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-                    const uint4 v[4] = {c0, c1, hh == 0 ? c0 : z, hh == 0 ? c1 : z};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(brow + (((hh * 4 + j) ^ (nl & 7)) * 16)) = v[j];
+                    out[0] = c0;
+                    out[1] = c1;
+                    out[2] = hh == 0 ? c0 : z;
+                    out[3] = hh == 0 ? c1 : z;
                 }
+                // the B slot is free once the MMAs of its previous round completed
+                if (!mbar_wait_warp(empty(s), ph ^ 1u, abort_flag, status, kStatusTimeoutDequant)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* brow = smem + C::kBOff + s * C::kBBytes + nl * 128;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(brow + (((hh * 4 + j) ^ (nl & 7)) * 16)) = out[j];
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(full_b(s));
             }
         }
-    } else {
+    } else if (warp < kEpiWarp0 + kEpiWarps) {
         // ------------------------------------------------------ epilogue --
         pdl_wait();  // row exponents and Y belong to the previous launch until it completes
         const int quarter = warp & 3;

@@ -1,6 +1,4 @@
-// Prefill GEMM on CTA pairs (cta_group::2):  Y = X . dequant(W).  (With a
-// LoRA term the runtime uses the single-CTA kernel, whose LoRA stages share
-// its accumulator.)
+// Prefill GEMM on CTA pairs (cta_group::2):  Y = X . dequant(W) (+ LoRA).
 //
 // Same computation as q4_gemm.cu (the reference's q4gemm.comp:61-175 with
 // w = float(v) * scale, q4gemm.comp:116-122), for large problems.  A cluster
@@ -26,6 +24,14 @@
 //     (two per lane quarter, four blocks each) scales a 32 x 32 block, stages
 //     it in shared memory (row = one row of Y, 128 bytes) and writes it with
 //     a TMA bulk store.
+//   * split K: with ksplit = 2 a work unit is (tile, half of K), so a problem
+//     with too few tiles for one wave still fills the pairs.  Each unit
+//     reduce-adds its block into a zeroed Y (TMA bulk reduce .add.f32); two
+//     addends onto zero give the same sum in either order, so the result is
+//     deterministic.
+//   * LoRA: the epilogue adds (alpha/r) * sum_r T[m][r] B[r][n] in fp32 (T =
+//     X*A from the projection kernel) to each staged block before it leaves;
+//     with ksplit = 2 each K half adds half of the ranks.
 //
 // Shared memory per SM and stage carries 32 KB of X written by TMA and read
 // by the MMA plus 10 KB of packed W and scales in and out: about 84 B/clk at
@@ -94,8 +100,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     q4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_y,
                         const int* __restrict__ col_exp,
-                        const int* __restrict__ row_exp, int M, int N, int K,
-                        int* __restrict__ status) {
+                        const int* __restrict__ row_exp, int M, int N, int K, int ksplit,
+                        const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
+                        float lora_scale, int* __restrict__ status) {
     using C = PCfg;
     constexpr int ST = kStages;
     constexpr int RT = kRawStages;
@@ -126,7 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int MT = (M + kPairRows - 1) / kPairRows;
     const int NT = (N + kPairCols - 1) / kPairCols;
     const int tiles = MT * NT;
-    const int KT = (K + kBK - 1) / kBK;
+    const int units = tiles * ksplit;           // unit u: tile u / ksplit, K part u % ksplit
+    const int KT = (K + kBK - 1) / kBK / ksplit;  // k-stages per unit (the host keeps this exact)
     auto leader_addr = [&](uint32_t a) { return mapa_shared(a, 0); };
 
     if (tid == 0) {
@@ -165,7 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             pdl_wait();  // X16 is written by the previous launch (the cast)
             const uint64_t keep = l2_policy_evict_last();  // every X tile is read by all column tiles
-            for (int t = pair; t < tiles && ok; t += npairs) {
+            for (int u = pair; u < units && ok; u += npairs) {
+                const int t = u / ksplit, k0 = (u % ksplit) * KT * kBK;
                 const int m0 = (t % MT) * kPairRows + static_cast<int>(crank) * kHalf;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % ST;
@@ -176,8 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (leader) mbar_arrive_expect_tx(full_x(s), 2u * C::kXBytes);
                     const uint32_t fx = leader_addr(full_x(s));
-                    tma_load_2d_pair_hint(x_s + s * C::kXBytes, &tmap_x, fx, kt * kBK, m0, keep);
-                    tma_load_2d_pair_hint(x_s + s * C::kXBytes + C::kSubBytes, &tmap_x, fx, kt * kBK + kSub, m0, keep);
+                    tma_load_2d_pair_hint(x_s + s * C::kXBytes, &tmap_x, fx, k0 + kt * kBK, m0, keep);
+                    tma_load_2d_pair_hint(x_s + s * C::kXBytes + C::kSubBytes, &tmap_x, fx, k0 + kt * kBK + kSub, m0,
+                                          keep);
                 }
             }
             if (*abort_flag && leader)  // let the copies in flight land before exit
@@ -190,7 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             bool ok = true;
             const uint64_t keep = l2_policy_evict_last();  // every weight tile is read by all row tiles
-            for (int t = pair; t < tiles && ok; t += npairs) {
+            for (int u = pair; u < units && ok; u += npairs) {
+                const int t = u / ksplit, kb = (u % ksplit) * KT;  // first k-stage of the unit
                 const int nb = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int r = it % RT;
@@ -200,8 +211,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(full_r(r), C::kRBytes);
-                    tma_load_2d_hint(r_s + r * C::kRBytes, &tmap_w, full_r(r), kt * (kBK / 8), nb, keep);
-                    tma_load_2d_hint(r_s + r * C::kRBytes + C::kWBytes, &tmap_s, full_r(r), kt * (kBK / 32), nb, keep);
+                    tma_load_2d_hint(r_s + r * C::kRBytes, &tmap_w, full_r(r), (kb + kt) * (kBK / 8), nb, keep);
+                    tma_load_2d_hint(r_s + r * C::kRBytes + C::kWBytes, &tmap_s, full_r(r), (kb + kt) * (kBK / 32), nb,
+                                     keep);
                 }
             }
             if (*abort_flag)
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                   static_cast<uint32_t>(kPairCols), static_cast<uint32_t>(kPairRows));
             int it = 0, i = 0;
             bool ok = true;
-            for (int t = pair; t < tiles && ok; t += npairs, ++i) {
+            for (int u = pair; u < units && ok; u += npairs, ++i) {
                 if (!mbar_wait(acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u, abort_flag, status, kStatusTimeoutMma))
                     break;
                 tc_fence_after_sync();
@@ -257,7 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
         int it = 0;
         bool ok = true;
-        for (int t = pair; t < tiles && ok; t += npairs) {
+        for (int u = pair; u < units && ok; u += npairs) {
+            const int t = u / ksplit;
             const int n = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf + nl;
             const float cs = (col_exp != nullptr && n < N) ? exp2i(__ldg(col_exp + n)) : 1.0f;
             for (int kt = 0; kt < KT; ++kt, ++it) {
@@ -320,14 +333,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* bufp = reinterpret_cast<float*>(smem + C::kYOff + (warp - kEpiWarp0) * C::kYBufBytes);
         const uint64_t once = l2_policy_evict_first();  // Y is written once: keep X and W resident instead
         int i = 0;
-        for (int t = pair; t < tiles; t += npairs, ++i) {
+        for (int u = pair; u < units; u += npairs, ++i) {
             if (!mbar_wait_warp(acc_full, static_cast<uint32_t>(i) & 1u, abort_flag, status, kStatusTimeoutEpilogue))
                 break;
             tc_fence_after_sync();
+            const int t = u / ksplit, kz = u % ksplit;
             const int m0 = (t % MT) * kPairRows;
             const int n = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf + quarter * 32 + lane;
             const float cinv = (col_exp != nullptr && n < N) ? exp2i(-col_exp[n]) : 1.0f;
             const int nx = (t / MT) * kPairCols + static_cast<int>(crank) * kHalf + quarter * 32;  // block's first column
+            // LoRA ranks [r_lo, r_hi) of this K part (multiples of 4 when rank is,
+            // so the float4 loads of T rows stay aligned and inside the part)
+            int rpk = (rank + ksplit - 1) / ksplit;
+            if (rank % 4 == 0) rpk = (rpk + 3) / 4 * 4;
+            const int r_lo = lora_b != nullptr ? min(rank, kz * rpk) : 0;
+            const int r_hi = lora_b != nullptr ? min(rank, r_lo + rpk) : 0;
+            const bool t_vec = (rank % 4) == 0 && (reinterpret_cast<uintptr_t>(lora_t) & 15u) == 0;
             uint32_t rv[2][32];
             tmem_ld32(tmem_base + t_lane + static_cast<uint32_t>(c0 * 32), rv[0]);
             tmem_ld_wait_regs(rv[0]);
@@ -352,10 +373,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float rs = __shfl_sync(0xffffffffu, rs_l, e);
                     bufp[e * 32 + lane] = __uint_as_float(rv[cc & 1][e]) * rs * cinv;
                 }
+                for (int r0 = r_lo; r0 < r_hi; r0 += 8) {
+                    // bufp[e][lane] += sum_{r in [r0, r0 + rc)} T[mc + e][r] * (alpha/r) B[r][n]:
+                    // lane e loads row mc + e of T (all loads of the block in flight
+                    // together), the rows reach the other lanes by shuffles.
+                    const int rc = min(8, r_hi - r0);
+                    float bv[8], tv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        bv[j] = (j < rc && n < N) ? __ldg(lora_b + static_cast<size_t>(r0 + j) * N + n) * lora_scale : 0.0f;
+                    const float* trow = lora_t + static_cast<size_t>(me < M ? me : 0) * rank + r0;
+                    if (t_vec) {  // rc is a multiple of 4 here
+#pragma unroll
+                        for (int j = 0; j < 8; j += 4) {
+                            const float4 v4 = (j + 4 <= rc && me < M) ? __ldg(reinterpret_cast<const float4*>(trow + j))
+                                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                            tv[j] = v4.x; tv[j + 1] = v4.y; tv[j + 2] = v4.z; tv[j + 3] = v4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) tv[j] = (j < rc && me < M) ? __ldg(trow + j) : 0.0f;
+                    }
+#pragma unroll 2
+                    for (int e = 0; e < 32; ++e) {
+                        float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+                        for (int j = 0; j < 8; j += 2)
+                            acc = __ffma2_rn(make_float2(__shfl_sync(0xffffffffu, tv[j], e),
+                                                         __shfl_sync(0xffffffffu, tv[j + 1], e)),
+                                             make_float2(bv[j], bv[j + 1]), acc);
+                        bufp[e * 32 + lane] += acc.x + acc.y;
+                    }
+                }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && mc < M) {
-                    tma_store_2d_hint(&tmap_y, buf, nx, mc, once);
+                    if (ksplit > 1) {
+                        tma_reduce_add_2d_hint(&tmap_y, buf, nx, mc, once);
+                    } else {
+                        tma_store_2d_hint(&tmap_y, buf, nx, mc, once);
+                    }
                     bulk_commit_group();
                 }
                 if (cc + 1 < kEpiChunks) tmem_ld_wait_regs(rv[(cc + 1) & 1]);
@@ -392,7 +449,7 @@ int launch_pair_t(const GemmArgs& a, int pairs, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.tmap_s, a.tmap_y, a.col_exp, a.row_exp, a.M, a.N,
-                           a.K, a.status);
+                           a.K, a.ksplit, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
     return static_cast<int>(e);
 }
 
@@ -426,8 +483,11 @@ int gemm_pair_tiles(int M, int N) {
 int gemm_pair_max_active(Operand16 op) { return op == Operand16::kF16 ? max_pairs_t<__half>() : max_pairs_t<__nv_bfloat16>(); }
 
 int launch_gemm_pair(const GemmArgs& a, int max_pairs, cudaStream_t stream) {
-    const int tiles = gemm_pair_tiles(a.M, a.N);
-    const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    if (a.ksplit < 1 || a.ksplit > 2 || a.K % (kBK * a.ksplit) != 0) return static_cast<int>(cudaErrorInvalidValue);
+    if (a.lora_b != nullptr && (a.lora_t == nullptr || a.rank < 1 || a.rank > 64))
+        return static_cast<int>(cudaErrorInvalidValue);
+    const int units = gemm_pair_tiles(a.M, a.N) * a.ksplit;
+    const int pairs = units < max_pairs ? units : max_pairs;
     if (pairs < 1) return static_cast<int>(cudaErrorInvalidValue);
     return a.op == Operand16::kF16 ? launch_pair_t<__half>(a, pairs, stream)
                                    : launch_pair_t<__nv_bfloat16>(a, pairs, stream);

@@ -105,6 +105,7 @@ struct GemmArgs {
     const uint32_t* lut = nullptr;  // single-CTA kernel, f16 only: CQ4 codebook pairs (256 words); the
                                     // scales are then the norms and W = RN16(codebook[idx] * norm)
     void* y16 = nullptr;            // single-CTA kernel: fp16 [M][N] output instead of y
+    int ksplit = 1;           // pair kernel: 1, or 2 = each tile as two K halves reduce-added into a zeroed Y
     int* status;              // kernel status word (0 = ok)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);

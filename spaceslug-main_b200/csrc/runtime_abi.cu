@@ -317,12 +317,22 @@ int pair_capacity(DeviceCtx& c, q4::Operand16 op) {
     return mp;
 }
 
-// The GEMM takes the CTA-pair kernel (256 x 256 tiles, half the
-// operand bytes per FLOP) when it still fills every co-resident pair and the
-// shape suits its TMA maps: scales loaded with row stride K/8 bytes (K % 128
-// == 0), Y stored with row stride 4 ld bytes (N % 4 == 0, ld % 4 == 0,
-// 16-byte aligned Y).  LoRA runs as extra bf16 k-stages of the single-CTA
-// kernel.
+// K split of the pair kernel: 2 when the tiles fill at most half of the
+// co-resident pairs (two K halves per tile then fit one wave) and each half
+// is whole 128-k stages of a long enough K.
+int pair_ksplit(const Problem& p, int pairs) {
+    const int tiles = q4::gemm_pair_tiles(p.M, p.N);
+    return (p.K % 256 == 0 && p.K >= 1024 && 2 * tiles <= pairs) ? 2 : 1;
+}
+
+// The GEMM takes the CTA-pair kernel (256 x 256 tiles, half the operand bytes
+// per FLOP, the dequantised weights in tensor memory, a deeper pipeline per
+// SM) whenever the shape suits its TMA maps: scales loaded with row stride
+// K/8 bytes (K % 128 == 0), Y stored with row stride 4 ld bytes (N % 4 == 0,
+// ld % 4 == 0, 16-byte aligned Y).  Measured on B200 it beats the
+// single-CTA kernel also when its units do not fill the pairs (M = 256 to
+// 1024 at K = N = 4096: 33 / 35 / 82 us against 50 / 52 / 115 us, the last
+// with LoRA).  Its epilogue adds the LoRA term in fp32.
 bool use_pair_kernel(DeviceCtx& c, const Problem& p, q4::Operand16 op, int* pairs_out) {
     const long long ld = p.ld_y ? p.ld_y : p.N;
     int pairs = pair_capacity(c, op);
@@ -330,8 +340,7 @@ bool use_pair_kernel(DeviceCtx& c, const Problem& p, q4::Operand16 op, int* pair
     if (pairs_out) *pairs_out = pairs;
     const int variant = g_gemm_variant.load();
     const bool shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && ld % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
-    return p.rank == 0 && pairs > 0 && shape_ok &&
-           (variant == 2 || (variant == 0 && q4::gemm_pair_tiles(p.M, p.N) >= pairs));
+    return p.rank <= 64 && pairs > 0 && shape_ok && (variant == 0 || variant == 2);
 }
 
 void run_problem(const Problem& p, cudaStream_t stream) {
@@ -436,6 +445,19 @@ void run_problem(const Problem& p, cudaStream_t stream) {
 
     const q4::Operand16 op = operand_type();
     const bool f16 = op == q4::Operand16::kF16;
+    // Variant: the CTA-pair kernel where use_pair_kernel allows it; else the
+    // single-CTA kernel with 256-row tiles when they fill every SM; else
+    // 128-row tiles.
+    int pairs = 0;
+    const int variant = g_gemm_variant.load();
+    const bool use_pair = use_pair_kernel(c, p, op, &pairs);
+    const int ksplit = use_pair ? pair_ksplit(p, pairs) : 1;
+    const long long ld_y = p.ld_y ? p.ld_y : p.N;
+    if (ld_y != p.N && !use_pair) throw CudaError("strided Y reached a kernel without a row pitch");
+    if (ksplit > 1)  // the K halves reduce-add into Y: zero it first (before the cast, so PDL still overlaps)
+        check(cudaMemset2DAsync(p.y, static_cast<size_t>(ld_y) * 4, 0, static_cast<size_t>(p.N) * 4,
+                                static_cast<size_t>(p.M), stream),
+              "cudaMemset2DAsync (split-K Y)");
     Scratch x16(static_cast<size_t>(p.M) * p.K * 2, stream);
     Scratch rexp(f16 ? static_cast<size_t>(p.M) * sizeof(int) : 0, stream);
     Scratch cexp(f16 && p.col_exp == nullptr ? static_cast<size_t>(p.N) * sizeof(int) : 0, stream);
@@ -446,15 +468,7 @@ void run_problem(const Problem& p, cudaStream_t stream) {
         check_launch(q4::launch_col_exp(p.scales, static_cast<int*>(cexp.p), p.N, p.K, stream), "col_exp");
 
     q4::GemmArgs g{};
-    // Variant: the CTA-pair kernel (256 x 256 tiles, half the operand bytes
-    // per FLOP) when it still fills every co-resident pair; else the
-    // single-CTA kernel with 256-row tiles when they fill every SM; else
-    // 128-row tiles.
-    int pairs = 0;
-    const int variant = g_gemm_variant.load();
-    const bool use_pair = use_pair_kernel(c, p, op, &pairs);
-    const long long ld_y = p.ld_y ? p.ld_y : p.N;
-    if (ld_y != p.N && !use_pair) throw CudaError("strided Y reached a kernel without a row pitch");
+    g.ksplit = ksplit;
     g.halves = use_pair ? 1 : (variant == 3 || (variant == 0 && q4::gemm_tiles(p.M, p.N, 2) >= c.sm_count) ? 2 : 1);
     g.sm_count = p.sm_budget > 0 && p.sm_budget < c.sm_count ? p.sm_budget : c.sm_count;
     encode_2d(&g.tmap_x16, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x16.p,
@@ -475,9 +489,17 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
     g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
     g.status = c.status;
-    const int lstages = (p.rank + 15) / 16;
+    const int lstages = use_pair ? 0 : (p.rank + 15) / 16;
     Scratch t_op(lstages > 0 ? static_cast<size_t>(p.M) * lstages * 64 * 2 : 0, stream);
-    if (p.rank > 0) {
+    if (p.rank > 0 && use_pair) {
+        // T = X * A in fp32: the pair kernel's epilogue adds (alpha/r) T B
+        check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
+                                        static_cast<float*>(t_part.p)),
+                     "lora_xa");
+        g.tmap_t = g.tmap_x16;  // never read
+        g.lora_t = lora_t;
+        g.lora_stages = 0;
+    } else if (p.rank > 0) {
         // T = X * A and its bf16 [hi | lo | hi | 0] operand scaled by the row exponents
         check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
                                         static_cast<float*>(t_part.p), row_exp, static_cast<uint16_t*>(t_op.p)),

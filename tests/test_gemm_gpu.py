@@ -185,6 +185,7 @@ def test_gemm_pair_kernel_on_large_ragged_problem(session, oracle, cuda, n):
                                             (1100, 4500, 1152, 400, 4500, 4504),  # pair kernel, shard at an offset
                                             (300, 200, 512, 104, 200, 200),       # single-CTA kernel: scratch + copy
                                             (4, 4096, 1024, 2048, 4096, 4096),    # decode: scratch + copy
+                                            (512, 4096, 4096, 0, 4096, 4100),     # pair kernel, split K (zeroed pitched Y)
                                             (1100, 4501, 1152, 1, 4501, 4503)])   # unaligned Y: scratch + copy
 def test_run_strided_writes_only_its_columns(session, cuda, m, n, k, c0, c1, ld):
     """spaceslug_q4_weights_run_strided: a column-shard handle writes its
@@ -202,3 +203,32 @@ def test_run_strided_writes_only_its_columns(session, cuda, m, n, k, c0, c1, ld)
         out = y.cpu().numpy()
     assert np.array_equal(out[:, c0:c1].view(np.uint32), dense.cpu().numpy().view(np.uint32))
     assert (out[:, :c0] == 7.0).all() and (out[:, c1:] == 7.0).all()
+
+
+@pytest.mark.parametrize("m,n,k,rank,forced", [(512, 4096, 4096, 0, False),   # configs[3] shape: split K, auto
+                                               (512, 4096, 4096, 16, False),  # ... with its LoRA
+                                               (300, 1000, 1024, 0, True),    # ragged tiles, split K
+                                               (300, 1000, 1024, 6, True),    # LoRA rank not a multiple of 4
+                                               (129, 260, 2048, 12, True)])   # uneven rank halves (8 + 4)
+def test_gemm_pair_split_k_and_lora_epilogue(session, oracle, cuda, m, n, k, rank, forced):
+    """The pair kernel with K split in two (each half reduce-added into a
+    zeroed Y) and the LoRA term added in its fp32 epilogue: oracle parity and
+    bit-identical repeats (two addends onto zero sum the same in any order)."""
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=m + n + k + rank)
+    x = synth.make_x(m, k, seed=m + 5)
+    a = synth.normal(k * rank, 3, 0.02).reshape(k, rank) if rank else None
+    b = synth.normal(rank * n, 4, 0.02).reshape(rank, n) if rank else None
+    prev = session.set_gemm_variant("pair" if forced else "auto")
+    try:
+        run = (lambda: session.q4gemm(x, packed, scales, n, a, b, 2.0 * rank)) if rank else \
+              (lambda: session.q4gemm(x, packed, scales, n))
+        y1, y2 = run(), run()
+    finally:
+        session.set_gemm_variant(prev)
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+    sel = np.r_[0:4, m // 2: m // 2 + 4, m - 4:m]
+    ref = oracle.gemm(x[sel], w_kn, scales)
+    if rank:
+        oracle.lora_add(ref, x[sel], a, b, 2.0 * rank)
+    _check(y1[sel], ref, x, scales, k)
+    assert session.device_status(0) == 0
