@@ -125,21 +125,26 @@ import sys, time, pynvml
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
 print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+i, power = 0, 0
 while True:
     t = time.time_ns()
     try:
+        if i % 8 == 0:
+            power = pynvml.nvmlDeviceGetPowerUsage(h)
         print(t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
-              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), pynvml.nvmlDeviceGetPowerUsage(h), flush=True)
+              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), power, flush=True)
     except pynvml.NVMLError:
         break
-    time.sleep(0.0005)
+    i += 1
+    time.sleep(0.0002)
 """
 
 
 class ClockSampler:
     """SM clock, clock-event (throttle) reasons and power, read through NVML
-    every ~0.5 ms by a separate process (read-only queries); only samples
-    taken between start() and stop() are kept."""
+    by a separate process (read-only queries); the samples taken between
+    start() and stop() are kept (or, when a short region falls between two
+    polls, the two polls that bracket it, and the line says so)."""
 
     REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
                ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
@@ -188,18 +193,27 @@ class ClockSampler:
         self.fh.close()
         out = Path(self.path).read_text()
         os.unlink(self.path)
-        samples = []
+        every = []
         for line in out.splitlines():
             f = line.split()
-            if len(f) == 4 and f[0].isdigit() and self.t0 <= int(f[0]) <= t1:
-                samples.append((int(f[1]), int(f[2]), int(f[3])))
+            if len(f) == 4 and f[0].isdigit():
+                every.append((int(f[0]), int(f[1]), int(f[2]), int(f[3])))
+        samples = [e[1:] for e in every if self.t0 <= e[0] <= t1]
+        window = "inside the timed region"
         if not samples:
-            return {"unavailable": "no samples in the timed region"}
+            # a short region can fall between two polls: take the polls that
+            # bracket it (the last one before it and the first one after it)
+            before = [e for e in every if e[0] < self.t0 and self.t0 - e[0] < 50_000_000]
+            after = [e for e in every if e[0] > t1 and e[0] - t1 < 50_000_000]
+            samples = [e[1:] for e in before[-1:] + after[:1]]
+            window = f"the polls bracketing the {(t1 - self.t0) / 1e6:.1f} ms timed region (none fell inside)"
+        if not samples:
+            return {"unavailable": "no NVML samples in or around the timed region"}
         reasons = sorted({name for _, r, _ in samples for name, bit in self.REASONS if r & bit})
         return {"sm_mhz": statistics.median(c for c, _, _ in samples), "sm_max_mhz": self.max_mhz,
                 "reasons": reasons, "samples": len(samples),
                 "power_w_max": round(max(p for _, _, p in samples) / 1000.0, 1),
-                "source": "NVML, every ~0.5 ms during the timed region"}
+                "source": f"NVML polled every ~0.2 ms (power every 8th poll); samples {window}"}
 
 
 # --------------------------------------------------------- CPU baselines --
