@@ -61,8 +61,11 @@ struct DeviceCtx {
     std::string init_error;
     int sm_count = 0;
     int* status = nullptr;  // device int, kernels record wait timeouts here
+    int* status_host = nullptr;     // pinned host word the host entry points read `status` into
     cudaStream_t stream = nullptr;  // for the synchronous host-pointer entry points
-    std::mutex host_mu;             // serialises use of `stream` by host entry points
+    std::mutex host_mu;             // serialises use of `stream` and `hbuf` by host entry points
+    void* hbuf = nullptr;           // device staging of X and Y for spaceslug_q4_weights_run_host (grows)
+    size_t hbuf_bytes = 0;
     int max_pairs[2] = {-1, -1};    // co-resident CTA pairs of the pair GEMM, per operand type
     std::mutex pair_mu;
     cublasHandle_t blas = nullptr;  // spaceslug_sgemm (created on first use)
@@ -104,6 +107,9 @@ DeviceCtx& ctx_for(int device) {
                                              std::to_string(major) + std::to_string(minor));
             check(cudaMalloc(&c.status, sizeof(int)), "cudaMalloc status");
             check(cudaMemset(c.status, 0, sizeof(int)), "cudaMemset status");
+            check(cudaHostAlloc(reinterpret_cast<void**>(&c.status_host), sizeof(int), cudaHostAllocDefault),
+                  "cudaHostAlloc status");
+            *c.status_host = 0;
             check(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate");
             cudaMemPool_t pool;
             check(cudaDeviceGetDefaultMemPool(&pool, device), "default mem pool");
@@ -520,12 +526,34 @@ void run_problem(const Problem& p, cudaStream_t stream) {
 }
 
 // Reads and clears the status word (synchronises `stream` first).
+// The status word rides on the same stream as the call's own copies, so one
+// synchronisation covers both (no second round trip per call).
 int take_status(DeviceCtx& c, cudaStream_t stream) {
+    check(cudaMemcpyAsync(c.status_host, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream), "read status");
     check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
-    int st = 0;
-    check(cudaMemcpy(&st, c.status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
-    if (st) check(cudaMemset(c.status, 0, sizeof(int)), "clear status");
+    const int st = *c.status_host;
+    if (st) {
+        check(cudaMemsetAsync(c.status, 0, sizeof(int), stream), "clear status");
+        check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    }
     return st;
+}
+
+// Device staging for a host-pointer call, kept per device and grown on
+// demand (caller holds c.host_mu).
+void* host_staging(DeviceCtx& c, size_t bytes) {
+    if (bytes > c.hbuf_bytes) {
+        if (c.hbuf) {
+            check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+            cudaFree(c.hbuf);
+            c.hbuf = nullptr;
+            c.hbuf_bytes = 0;
+        }
+        const size_t want = std::max(bytes, static_cast<size_t>(1) << 20);
+        check(cudaMalloc(&c.hbuf, want), "cudaMalloc host-call staging");
+        c.hbuf_bytes = want;
+    }
+    return c.hbuf;
 }
 
 template <typename F>
@@ -1134,12 +1162,16 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
         DeviceCtx& c = ctx_for(w->device);
         std::lock_guard<std::mutex> lk(c.host_mu);
         const size_t xb = static_cast<size_t>(m) * w->K * 4, yb = static_cast<size_t>(m) * w->N * 4;
-        Scratch dx(xb, c.stream), dy(yb, c.stream);
-        h2d(dx.p, x, xb, c.stream);
-        Problem p{static_cast<float*>(dx.p), w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank,
-                  w->alpha, static_cast<float*>(dy.p), static_cast<int>(m), w->N, w->K};
+        const size_t yoff = (xb + 255) / 256 * 256;
+        char* stage = static_cast<char*>(host_staging(c, yoff + yb));
+        float* dx = reinterpret_cast<float*>(stage);
+        float* dy = reinterpret_cast<float*>(stage + yoff);
+        h2d(dx, x, xb, c.stream);
+        Problem p{dx, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, dy,
+                  static_cast<int>(m), w->N, w->K};
+        p.sm_budget = w->sm_budget;
         run_problem(p, c.stream);
-        d2h(y, dy.p, yb, c.stream);
+        d2h(y, dy, yb, c.stream);
         if (take_status(c, c.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
         return SPACESLUG_OK;
     });
