@@ -190,13 +190,14 @@ __global__ void __launch_bounds__(256) pack_kernel(const int8_t* __restrict__ b_
 }
 
 // T = X * A in fp32 (the LoRA projection, lora.py:21-23 forward).  A block
-// covers 64 rows x 16 ranks x a 256-k chunk: it stages the X tile and the A
+// covers 64 rows x 16 ranks x a 128-k chunk: it stages the X tile and the A
 // slice in shared memory (all loads issued at once; rows padded so the reads
 // below are free of bank conflicts), then thread (row group g = t / 16, k lane
 // q = t % 16) accumulates rows 4g..4g+3 x 16 ranks over k = q, q + 16, ...
 // (4 scalar X reads and 4 float4 A reads per 64 FMAs) and the 16 k lanes are
 // summed with a butterfly reduce-scatter.  With one chunk the block writes T;
-// with several it writes partial[z][M][rank] and lora_xa_reduce_kernel sums
+// with several it writes partial[z][M][rank] and lora_xa_sum_kernel (or, when
+// the single-CTA GEMM needs its bf16 operand, lora_xa_reduce_kernel) sums
 // the chunks in fixed order (deterministic).
 constexpr int kXaRows = 64;
 constexpr int kXaCols = 16;
@@ -291,38 +292,29 @@ __global__ void __launch_bounds__(256) lora_xa_kernel(const float* __restrict__ 
     }
 }
 
-// T[m][j] = sum over chunks z (fixed order) of partial[z][m][j].  With tlo
-// != nullptr it also writes the bf16 A operand of the GEMM's LoRA stages:
-// row m holds ceil(rank/16) blocks of 64, block q = [hi(16) | lo(16) | hi(16) |
+// T[m][j] = sum over chunks z (fixed order) of partial[z][m][j], and the bf16
+// A operand of the single-CTA GEMM's LoRA stages (tlo): row m holds ceil(rank/16) blocks of 64, block q = [hi(16) | lo(16) | hi(16) |
 // 0(16)] of T[m][16q .. 16q+15] * 2^e_m, e_m = row_exp[m] (0 without), hi + lo
 // carrying ~16 bits.
 __global__ void __launch_bounds__(256) lora_xa_reduce_kernel(const float* __restrict__ partial,
                                                              float* __restrict__ t, int M, int rank, int chunks,
                                                              const int* __restrict__ row_exp,
                                                              __nv_bfloat16* __restrict__ tlo) {
+    // one thread per (row, position) of the bf16 operand
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (tlo != nullptr) {
-        // one thread per (row, position) of the bf16 operand
-        const int W = (rank + 15) / 16 * 64;
-        if (i >= M * W) return;
-        const int m = i / W, pq = i % W, p = pq % 64, j = (pq / 64) * 16 + p % 16;
-        float v = 0.0f;
-        if (p < 48 && j < rank) {
-            const int MR = M * rank;
-            for (int z = 0; z < chunks; ++z) v += partial[static_cast<size_t>(z) * MR + m * rank + j];
-            if (p < 16) t[m * rank + j] = v;
-            v *= exp2i(row_exp != nullptr ? row_exp[m] : 0);
-            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-            v = (p >= 16 && p < 32) ? v - __bfloat162float(hi) : __bfloat162float(hi);
-        }
-        tlo[i] = __float2bfloat16_rn(v);
-        return;
+    const int W = (rank + 15) / 16 * 64;
+    if (i >= M * W) return;
+    const int m = i / W, pq = i % W, p = pq % 64, j = (pq / 64) * 16 + p % 16;
+    float v = 0.0f;
+    if (p < 48 && j < rank) {
+        const int MR = M * rank;
+        for (int z = 0; z < chunks; ++z) v += partial[static_cast<size_t>(z) * MR + m * rank + j];
+        if (p < 16) t[m * rank + j] = v;
+        v *= exp2i(row_exp != nullptr ? row_exp[m] : 0);
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        v = (p >= 16 && p < 32) ? v - __bfloat162float(hi) : __bfloat162float(hi);
     }
-    const int MR = M * rank;
-    if (i >= MR) return;
-    float s = 0.0f;
-    for (int z = 0; z < chunks; ++z) s += partial[static_cast<size_t>(z) * MR + i];
-    t[i] = s;
+    tlo[i] = __float2bfloat16_rn(v);
 }
 
 // T = sum over chunks of partial[z][M * rank] for 32 outputs per CTA: warp g
