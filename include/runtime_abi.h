@@ -167,9 +167,9 @@ int spaceslug_lora_train_step(const float* x, const float* dy, float* a, float* 
 /* No counterpart in the reference.  The decode GEMV with the fused LoRA term
  * (device pointers, asynchronous on `stream`, same result as
  * spaceslug_q4gemm_device with the same arguments) for callers that cannot
- * allocate device memory: graph-capturing hosts whose graphs must hold no
- * memory nodes, serving loops that forbid allocation on the hot path, plugin
- * hosts that keep all device memory for themselves.  It allocates nothing: its
+ * allocate device memory: serving loops that forbid allocation on the hot
+ * path (an allocation can stall or synchronise the device), plugin hosts that
+ * keep all device memory for themselves.  It allocates nothing: its
  * only scratch, T = X*A, lives in a fixed 2 KB static device array, so
  * 1 <= m <= 8 and 1 <= rank <= 64; and, as for the decode GEMV itself, K/32
  * must split into 1, 2, 4 or 8 equal slices of at most 32 scale groups (every

@@ -2,12 +2,10 @@
 // callers that cannot allocate device memory.
 //
 // Some callers of this library may not call cudaMalloc (or the stream-ordered
-// cudaMallocAsync the regular entry points use for scratch): a host that
-// captures work into CUDA graphs which must not contain memory nodes, a
-// serving loop that forbids allocation on its hot path (an allocation can
-// stall or synchronise the device), or a plugin host that has reserved all
-// device memory for itself and hands the plugin only its input and output
-// buffers.  This entry point keeps its only scratch, the LoRA projection
+// cudaMallocAsync the regular entry points use for scratch): a serving loop
+// that forbids allocation on its hot path (an allocation can stall or
+// synchronise the device), or a plugin host that has reserved all device
+// memory for itself and hands the plugin only its input and output buffers.  This entry point keeps its only scratch, the LoRA projection
 // T = X * A (at most kMaxRows x kMaxRank floats = 2 KB), in a file-scope
 // static __device__ array, so a call allocates nothing.
 //

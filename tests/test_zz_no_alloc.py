@@ -1,8 +1,8 @@
 """GPU: the no-allocation decode entry point (spaceslug_q4gemv_lora_noalloc).
 
-Callers that cannot allocate device memory (graph-capturing hosts whose graphs
-must hold no memory nodes, allocation-free serving loops, plugin hosts that own
-all device memory) call this entry point instead of spaceslug_q4gemm_device:
+Callers that cannot allocate device memory (allocation-free serving loops,
+where an allocation can stall or synchronise the device, and plugin hosts that
+own all device memory) call this entry point instead of spaceslug_q4gemm_device:
 its LoRA scratch lives in a fixed static device array.  This file sorts last so
 that a stop-at-first-failure run has executed every other test first; it also
 passes on its own in a fresh process.
