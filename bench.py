@@ -47,10 +47,10 @@ DECODE_LAYERS = 24
 DECODE_SWEEP = (1, 2, 4, 8)
 
 # ncu DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
-# q4_gemv_tile_kernel launch per decode M, from the full capture summarised in
-# profiles/decode_tile_kernel.md.
+# q4_gemv_tile_kernel launch per decode M: a full ncu capture (--set full) of
+# the fourth launch of each M in this bench's decode warm-up, caches flushed.
 NCU_TRAFFIC_PER_LAUNCH = {
-    "decode": {1: 10539520, 2: 10559744, 4: 10598144, 8: 10675456},
+    "decode": {1: 10539264, 2: 10560512, 4: 10598656, 8: 10670592},
 }
 
 
