@@ -580,7 +580,8 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     compute stream while band b is all-gathered by NCCL and re-laid out into
     row-major Y) and ShardedGemmPush (GEMM writes into a row-major Y every
     peer has mapped; each finished band is pushed to the peers by copy
-    engines, or by a push kernel on SMs the GEMM leaves free).  The value is
+    engines or by a push kernel on SMs the GEMM leaves free, or every finished
+    tile by the GEMM's own epilogue).  The value is
     the fastest variant (named in the line); the GEMM alone, the NCCL
     all-gather of the whole Y alone and the re-layout alone are timed the
     same way for the breakdown."""
@@ -657,8 +658,8 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     best = (best[0], best[1], best[2], "nccl")
     del y
     torch.cuda.empty_cache()
-    for engine, bands, sms in (("copy", 1, 0), ("copy", 2, 0), ("copy", 4, 0), ("sm", 2, 16), ("sm", 4, 16),
-                               ("sm", 4, 24), ("sm", 8, 16)):
+    for engine, bands, sms in (("epilogue", 1, 0), ("copy", 1, 0), ("copy", 2, 0), ("copy", 4, 0), ("sm", 2, 16),
+                               ("sm", 4, 16), ("sm", 4, 24), ("sm", 8, 16)):
         push = sharding.ShardedGemmPush(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands, engine=engine,
                                         push_sms=sms or 16)
         n0 = session.launch_count()

@@ -226,6 +226,18 @@ int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m,
 int spaceslug_q4_weights_run_strided(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, uint64_t ld_y,
                                      void* stream);
 
+/* spaceslug_q4_weights_run_strided that also stores the same rows and columns
+ * of Y into each of npeers (<= 7) other GPUs' buffers, peer_y[q] pointing at
+ * the place that corresponds to y (host array of device pointers mapped with
+ * spaceslug_ipc_open; same row pitch).  No reference counterpart: the
+ * N-sharded all-gather of Y fused into the GEMM.  The pair kernel pushes each
+ * finished 32 x 32 block from its epilogue while the next tile computes
+ * (16-byte aligned y and peers, K % 128 == 0, N % 4 == 0); other shapes run
+ * the GEMM, then push the whole block.  The caller orders the peers' use of
+ * their buffers around the call (for instance with a collective before and
+ * after it). */
+int spaceslug_q4_weights_run_push(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, uint64_t ld_y,
+                                  float* const* peer_y, uint32_t npeers, void* stream);
 /* Caps the SMs a GEMM launch of this handle occupies (0: all, else >= 2), so
  * that kernels on other streams (an exchange running beside the GEMM) find
  * free SMs.  Decode-sized launches (m <= 8) ignore it. */

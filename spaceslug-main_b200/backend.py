@@ -62,6 +62,8 @@ _SIGNATURES = {
     "spaceslug_shards_relayout": ([_vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, _vp], ctypes.c_int),
     "spaceslug_q4_weights_run_strided": ([_vp, _vp, _vp, _u32, ctypes.c_uint64, _vp], ctypes.c_int),
     "spaceslug_q4_weights_set_sm_budget": ([_vp, _u32], ctypes.c_int),
+    "spaceslug_q4_weights_run_push": ([_vp, _vp, _vp, _u32, ctypes.c_uint64, ctypes.POINTER(_vp), _u32, _vp],
+                                      ctypes.c_int),
     "spaceslug_push_rows": ([_vp, ctypes.POINTER(_vp), _u32, _u32, _u32, ctypes.c_uint64, _u32, _vp], ctypes.c_int),
     "spaceslug_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "spaceslug_ipc_open": ([_vp, ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(_vp), ctypes.POINTER(_vp)],
@@ -384,6 +386,12 @@ class Q4Weights:
     def set_sm_budget(self, sms: int) -> None:
         """At most `sms` SMs for this handle's GEMM launches (0: all)."""
         self.session._call("spaceslug_q4_weights_set_sm_budget", self.handle, sms)
+
+    def run_push(self, x: int, y: int, m: int, ld_y: int, peer_y: list[int], stream: int = 0) -> None:
+        """run_strided that also stores Y's rows to the same places in the peers' buffers."""
+        arr = (_vp * max(1, len(peer_y)))(*peer_y)
+        self.session._call("spaceslug_q4_weights_run_push", self.handle, x, y, m, ld_y, arr, len(peer_y),
+                           stream or None)
 
     def run_strided(self, x: int, y: int, m: int, ld_y: int, stream: int = 0) -> None:
         """Y rows with pitch ld_y floats (this handle's columns only)."""

@@ -32,6 +32,12 @@
 //   * LoRA: the epilogue adds (alpha/r) * sum_r T[m][r] B[r][n] in fp32 (T =
 //     X*A from the projection kernel) to each staged block before it leaves;
 //     with ksplit = 2 each K half adds half of the ranks.
+//   * peer push (N-sharded layers, ksplit = 1): besides the TMA store into
+//     this GPU's Y, the epilogue warp stores each staged block to the same
+//     rows and columns of up to 7 peers' Y (plain 16-byte stores through
+//     NVLink peer mappings), so the exchange of Y runs tile by tile beside
+//     the next tile's main loop.  The accumulator is released before the
+//     pushes, so only the epilogue warps wait for the link.
 //
 // Shared memory per SM and stage carries 32 KB of X written by TMA and read
 // by the MMA plus 10 KB of packed W and scales in and out: about 84 B/clk at
@@ -102,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int* __restrict__ col_exp,
                         const int* __restrict__ row_exp, int M, int N, int K, int ksplit,
                         const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
-                        float lora_scale, int* __restrict__ status) {
+                        float lora_scale, PeerPtrs peers, int npeers, long long ld_y, int* __restrict__ status) {
     using C = PCfg;
     constexpr int ST = kStages;
     constexpr int RT = kRawStages;
@@ -415,6 +421,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     bulk_commit_group();
                 }
+                if (npeers > 0 && mc < M && nx < N) {
+                    // the block to every peer: float4 j = lane + 32 i is row j / 8,
+                    // columns 4 (j % 8) .. +3 (8 lanes write one 128-byte row)
+#pragma unroll 2
+                    for (int i = 0; i < 8; ++i) {
+                        const int j = lane + 32 * i, r = j >> 3, c4 = (j & 7) * 4;
+                        if (mc + r < M && nx + c4 < N) {
+                            const float4 v = *reinterpret_cast<const float4*>(bufp + r * 32 + c4);
+                            const long long at = static_cast<long long>(mc + r) * ld_y + nx + c4;
+#pragma unroll
+                            for (int q = 0; q < kMaxPeers; ++q)  // constant indices: no local copy of the array
+                                if (q < npeers) *reinterpret_cast<float4*>(peers.p[q] + at) = v;
+                        }
+                    }
+                }
                 if (cc + 1 < kEpiChunks) tmem_ld_wait_regs(rv[(cc + 1) & 1]);
             }
         }
@@ -449,7 +470,8 @@ int launch_pair_t(const GemmArgs& a, int pairs, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.tmap_s, a.tmap_y, a.col_exp, a.row_exp, a.M, a.N,
-                           a.K, a.ksplit, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
+                           a.K, a.ksplit, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.peers, a.npeers, a.peer_ld,
+                           a.status);
     return static_cast<int>(e);
 }
 
@@ -486,6 +508,11 @@ int launch_gemm_pair(const GemmArgs& a, int max_pairs, cudaStream_t stream) {
     if (a.ksplit < 1 || a.ksplit > 2 || a.K % (kBK * a.ksplit) != 0) return static_cast<int>(cudaErrorInvalidValue);
     if (a.lora_b != nullptr && (a.lora_t == nullptr || a.rank < 1 || a.rank > 64))
         return static_cast<int>(cudaErrorInvalidValue);
+    if (a.npeers < 0 || a.npeers > kMaxPeers || (a.npeers > 0 && (a.ksplit != 1 || a.peer_ld < a.N || a.peer_ld % 4)))
+        return static_cast<int>(cudaErrorInvalidValue);
+    for (int q = 0; q < a.npeers; ++q)
+        if (a.peers.p[q] == nullptr || (reinterpret_cast<uintptr_t>(a.peers.p[q]) & 15u))
+            return static_cast<int>(cudaErrorInvalidValue);
     const int units = gemm_pair_tiles(a.M, a.N) * a.ksplit;
     const int pairs = units < max_pairs ? units : max_pairs;
     if (pairs < 1) return static_cast<int>(cudaErrorInvalidValue);

@@ -82,6 +82,12 @@ int gemv_chunk_columns();
 // Max co-resident clusters of the GEMV for these parameters (0 on error).
 int gemv_max_active_clusters(int M, int K, int cluster_k, int cols_per_cluster);
 
+// Device pointers of up to kMaxPeers other GPUs' buffers (peer mappings).
+constexpr int kMaxPeers = 7;
+struct PeerPtrs {
+    float* p[kMaxPeers];
+};
+
 struct GemmArgs {
     CUtensorMap tmap_x16;     // [M][K] 16-bit, box 64 x (128 * halves), 128B swizzle
     CUtensorMap tmap_w;       // packed as uint32 [N][K/8]: box 8 x 128 unswizzled (single-CTA), 16 x 128 64B-swizzled (pair)
@@ -106,6 +112,9 @@ struct GemmArgs {
                                     // scales are then the norms and W = RN16(codebook[idx] * norm)
     void* y16 = nullptr;            // single-CTA kernel: fp16 [M][N] output instead of y
     int ksplit = 1;           // pair kernel: 1, or 2 = each tile as two K halves reduce-added into a zeroed Y
+    PeerPtrs peers{};         // pair kernel, ksplit 1: every Y block also stored to these peers' Y ...
+    int npeers = 0;
+    long long peer_ld = 0;    // ... at the same offsets, row pitch peer_ld floats (= Y's)
     int* status;              // kernel status word (0 = ok)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t stream);
@@ -138,10 +147,6 @@ int lora_xa_chunks(int K);
 // partly padding).  HBM-bound copy; float4 when every address is aligned.
 // Push of a pitched fp32 row block to the same offset in peers' buffers
 // (peer-mapped device pointers) by `ctas` CTAs of plain global stores.
-constexpr int kMaxPeers = 7;
-struct PeerPtrs {
-    float* p[kMaxPeers];
-};
 int launch_push_rows(const float* src, const PeerPtrs& peers, int npeers, int rows, int width, long long ld, int ctas,
                      cudaStream_t stream);
 int launch_shards_relayout(const float* gathered, float* y, int parts, int rows, int width, int n_total,

@@ -234,6 +234,8 @@ struct Problem {
     int M, N, K;
     long long ld_y = 0;  // row pitch of Y in floats (0: N)
     int sm_budget = 0;   // SMs the GEMM may occupy (0: all)
+    const q4::PeerPtrs* peers = nullptr;  // Y also stored to these peers' Y (same offsets and pitch)
+    int npeers = 0;
 };
 
 // GEMV launch geometry.  K is split over a cluster of S CTAs (S | G, slice
@@ -345,12 +347,25 @@ bool use_pair_kernel(DeviceCtx& c, const Problem& p, q4::Operand16 op, int* pair
     if (p.sm_budget > 0 && pairs > p.sm_budget / 2) pairs = p.sm_budget / 2;
     if (pairs_out) *pairs_out = pairs;
     const int variant = g_gemm_variant.load();
-    const bool shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && ld % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
+    bool shape_ok = p.K % 128 == 0 && p.N % 4 == 0 && ld % 4 == 0 && aligned16(p.y) && aligned16(p.scales);
+    for (int q = 0; q < p.npeers; ++q) shape_ok = shape_ok && aligned16(p.peers->p[q]);  // 16-byte peer stores
     return p.rank <= 64 && pairs > 0 && shape_ok && (variant == 0 || variant == 2);
 }
 
 void run_problem(const Problem& p, cudaStream_t stream) {
     DeviceCtx& c = ctx_for(current_device());
+    if (p.npeers > 0 && !(p.M > 8 && use_pair_kernel(c, p, operand_type(), nullptr))) {
+        // Only the pair kernel pushes from its epilogue: elsewhere the product
+        // is written here first and then pushed as one block.
+        Problem q = p;
+        q.peers = nullptr;
+        q.npeers = 0;
+        run_problem(q, stream);
+        check_launch(q4::launch_push_rows(p.y, *p.peers, p.npeers, p.M, p.N, p.ld_y ? p.ld_y : p.N,
+                                          2 * c.sm_count, stream),
+                     "push_rows");
+        return;
+    }
     if (p.ld_y != 0 && p.ld_y != p.N && !(p.M > 8 && use_pair_kernel(c, p, operand_type(), nullptr))) {
         // Only the pair kernel (reached for M > 8) stores Y with an arbitrary
         // row pitch: elsewhere the product lands in scratch and one strided
@@ -457,7 +472,7 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     int pairs = 0;
     const int variant = g_gemm_variant.load();
     const bool use_pair = use_pair_kernel(c, p, op, &pairs);
-    const int ksplit = use_pair ? pair_ksplit(p, pairs) : 1;
+    const int ksplit = use_pair && p.npeers == 0 ? pair_ksplit(p, pairs) : 1;  // pushes need whole tiles
     const long long ld_y = p.ld_y ? p.ld_y : p.N;
     if (ld_y != p.N && !use_pair) throw CudaError("strided Y reached a kernel without a row pitch");
     if (ksplit > 1)  // the K halves reduce-add into Y: zero it first (before the cast, so PDL still overlaps)
@@ -495,6 +510,11 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     g.M = p.M; g.N = p.N; g.K = p.K; g.op = op;
     g.lora_b = p.rank > 0 ? p.lora_b : nullptr; g.rank = p.rank; g.lora_scale = lscale;
     g.status = c.status;
+    if (p.npeers > 0) {
+        g.peers = *p.peers;
+        g.npeers = p.npeers;
+        g.peer_ld = ld_y;
+    }
     const int lstages = use_pair ? 0 : (p.rank + 15) / 16;
     Scratch t_op(lstages > 0 ? static_cast<size_t>(p.M) * lstages * 64 * 2 : 0, stream);
     if (p.rank > 0 && use_pair) {
@@ -1078,6 +1098,32 @@ int spaceslug_push_rows(const float* src, float* const* peer_dst, uint32_t npeer
                                           static_cast<int>(width), static_cast<long long>(ld), static_cast<int>(ctas),
                                           static_cast<cudaStream_t>(stream)),
                      "push_rows");
+        return SPACESLUG_OK;
+    });
+}
+
+int spaceslug_q4_weights_run_push(spaceslug_q4_weights* w, const float* x, float* y, uint32_t m, uint64_t ld_y,
+                                  float* const* peer_y, uint32_t npeers, void* stream) {
+    if (!w || !x || !y || (npeers && !peer_y)) return fail(SPACESLUG_INVALID_ARGUMENT, "null pointer");
+    if (m == 0 || m > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "bad m");
+    if (npeers > static_cast<uint32_t>(q4::kMaxPeers)) return fail(SPACESLUG_INVALID_ARGUMENT, "at most 7 peers");
+    if (ld_y < static_cast<uint64_t>(w->N) || ld_y > (uint64_t(1) << 40))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "ld_y must be >= the handle's column count");
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(y) & 3u))
+        return fail(SPACESLUG_INVALID_ARGUMENT, "x must be 16-byte and y 4-byte aligned");
+    q4::PeerPtrs pp{};
+    for (uint32_t q = 0; q < npeers; ++q) {
+        if (!peer_y[q] || (reinterpret_cast<uintptr_t>(peer_y[q]) & 3u))
+            return fail(SPACESLUG_INVALID_ARGUMENT, "null or misaligned peer pointer");
+        pp.p[q] = peer_y[q];
+    }
+    return guarded([&] {
+        if (current_device() != w->device) check(cudaSetDevice(w->device), "cudaSetDevice");
+        Problem p{x, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, y,
+                  static_cast<int>(m), w->N, w->K, static_cast<long long>(ld_y), w->sm_budget};
+        p.peers = &pp;
+        p.npeers = static_cast<int>(npeers);
+        run_problem(p, static_cast<cudaStream_t>(stream));
         return SPACESLUG_OK;
     });
 }

@@ -101,7 +101,7 @@ class ShardedGemm:
             raise ValueError("the weight handle does not hold this rank's column shard")
         self.width = shard_width(n_total, self.world)
         self.device = torch.device(device)
-        self.bands = plan_bands(m, bands)
+        self.bands = plan_bands(m, 1 if engine == "epilogue" else bands)
         self.ys = torch.zeros((m, self.width), dtype=torch.float32, device=self.device)
         self.direct = (self.c1 - self.c0) == self.width
         self.tmp = None if self.direct else torch.empty((m, self.c1 - self.c0), dtype=torch.float32,
@@ -162,6 +162,10 @@ class ShardedGemmPush:
       stores, each element read once and stored to every peer) on
       `push_sms` SMs that the GEMM leaves free
       (spaceslug_q4_weights_set_sm_budget) while a push runs beside it.
+    * engine="epilogue": one GEMM call (spaceslug_q4_weights_run_push) whose
+      epilogue stores every finished 32 x 32 block of Y to the peers as well,
+      so the exchange runs tile by tile beside the next tile's main loop; no
+      bands, no separate push kernel.
 
     Two one-element NCCL all-reduces per call fence the pushes: one before
     the first push (every rank's earlier use of its Y is done) and one after
@@ -172,8 +176,8 @@ class ShardedGemmPush:
     def __init__(self, session, handle, m: int, n_total: int, dist, device, bands: int = 4, group=None,
                  engine: str = "copy", push_sms: int = 16) -> None:
         import torch
-        if engine not in ("copy", "sm"):
-            raise ValueError("engine is 'copy' or 'sm'")
+        if engine not in ("copy", "sm", "epilogue"):
+            raise ValueError("engine is 'copy', 'sm' or 'epilogue'")
         self.torch, self.session, self.h, self.dist, self.group = torch, session, handle, dist, group
         self.engine = engine
         self.world = dist.get_world_size(group)
@@ -201,7 +205,7 @@ class ShardedGemmPush:
         except Exception:
             self._unmap()
             raise
-        n_streams = len(self.peers) if engine == "copy" else min(1, len(self.peers))
+        n_streams = {"copy": len(self.peers), "sm": min(1, len(self.peers)), "epilogue": 0}[engine]
         self.push_streams = [torch.cuda.Stream(device=self.device, priority=-1) for _ in range(n_streams)]
 
     def _unmap(self) -> None:
@@ -243,6 +247,16 @@ class ShardedGemmPush:
             for ps in self.push_streams:
                 ps.wait_event(start)
         yb = self.y.data_ptr()
+        if self.engine == "epilogue":
+            off = 4 * c0
+            self.h.run_push(x.data_ptr(), yb + off, self.m, n, [ptr + off for _, ptr, _ in self.peers],
+                            s0.cuda_stream)
+            if self.peers:
+                self._fence(s0)
+                fin = torch.cuda.Event()
+                fin.record(self.comm)
+                s0.wait_event(fin)
+            return self.y
         sm = self.engine == "sm" and bool(self.peers)
         try:
             for b, (r0, r1) in enumerate(self.bands):

@@ -1,7 +1,8 @@
 """Worker for tests/test_multigpu_gpu.py (one process per GPU under
 torch.distributed.run): N-sharded int4 GEMM (+ LoRA) through the library on
 each rank, exchange of the fp32 Y shards (NCCL all-gather, the banded
-ShardedGemm pipeline, and the copy-engine push of ShardedGemmPush), rank 0 checks the gathered Y against the oracle and
+ShardedGemm pipeline, and the copy-engine, SM and GEMM-epilogue pushes of
+ShardedGemmPush), rank 0 checks the gathered Y against the oracle and
 against an unsharded run on its own GPU."""
 from __future__ import annotations
 
@@ -56,7 +57,7 @@ def main() -> int:
             # (run twice, Y poisoned before each call: the start fence orders the
             # poison before the peers' pushes, the end fence every push before the read)
             yq = {}
-            for engine in ("copy", "sm"):
+            for engine in ("copy", "sm", "epilogue"):
                 push = sharding.ShardedGemmPush(s, h, m, n, dist, dev, bands=2, engine=engine, push_sms=8)
                 for _ in range(2):
                     push.y.fill_(float("nan"))

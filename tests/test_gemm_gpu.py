@@ -232,3 +232,29 @@ def test_gemm_pair_split_k_and_lora_epilogue(session, oracle, cuda, m, n, k, ran
         oracle.lora_add(ref, x[sel], a, b, 2.0 * rank)
     _check(y1[sel], ref, x, scales, k)
     assert session.device_status(0) == 0
+
+
+@pytest.mark.parametrize("m,n,k,c0,c1,ld,rank", [(1100, 4500, 1152, 0, 4096, 4500, 0),    # pair kernel: epilogue push
+                                                 (1100, 4500, 1152, 400, 4500, 4504, 8),  # ... at an offset, LoRA
+                                                 (300, 200, 512, 104, 200, 200, 0),       # single-CTA kernel + push
+                                                 (4, 4096, 1024, 2048, 4096, 4096, 0)])   # decode + push
+def test_run_push_stores_the_same_block_into_every_peer_buffer(session, cuda, m, n, k, c0, c1, ld, rank):
+    """spaceslug_q4_weights_run_push with two 'peer' buffers that live on this
+    GPU: each receives exactly the handle's columns of Y, bit-identical to Y
+    itself and to run_strided, and nothing else of the pitched rows."""
+    import torch
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=n + c0 + 1)
+    x = torch.from_numpy(synth.make_x(m, k, seed=9)).to(cuda)
+    with session.weights(packed, scales, k, n, c0, c1) as h:
+        if rank:
+            h.set_lora(synth.normal(k * rank, 3, 0.02).reshape(k, rank),
+                       synth.normal(rank * n, 4, 0.02).reshape(rank, n), 16.0)  # full B: the handle keeps its columns
+        ref = torch.full((m, ld), 7.0, dtype=torch.float32, device=cuda)
+        h.run_strided(x.data_ptr(), ref.data_ptr() + 4 * c0, m, ld, torch.cuda.current_stream().cuda_stream)
+        bufs = [torch.full((m, ld), 7.0, dtype=torch.float32, device=cuda) for _ in range(3)]
+        h.run_push(x.data_ptr(), bufs[0].data_ptr() + 4 * c0, m, ld,
+                   [bufs[1].data_ptr() + 4 * c0, bufs[2].data_ptr() + 4 * c0], torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+    want = ref.cpu().numpy().view(np.uint32)
+    for b in bufs:
+        assert np.array_equal(b.cpu().numpy().view(np.uint32), want)
