@@ -101,7 +101,7 @@ class ShardedGemm:
             raise ValueError("the weight handle does not hold this rank's column shard")
         self.width = shard_width(n_total, self.world)
         self.device = torch.device(device)
-        self.bands = plan_bands(m, 1 if engine == "epilogue" else bands)
+        self.bands = plan_bands(m, bands)
         self.ys = torch.zeros((m, self.width), dtype=torch.float32, device=self.device)
         self.direct = (self.c1 - self.c0) == self.width
         self.tmp = None if self.direct else torch.empty((m, self.c1 - self.c0), dtype=torch.float32,
@@ -189,7 +189,7 @@ class ShardedGemmPush:
         self.device = torch.device(device)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.push_sms = max(1, min(int(push_sms), self.sm_count - 2))
-        self.bands = plan_bands(m, bands)
+        self.bands = plan_bands(m, 1 if engine == "epilogue" else bands)
         self.y = torch.empty((m, n_total), dtype=torch.float32, device=self.device)
         self.fence = torch.zeros(1, dtype=torch.float32, device=self.device)
         self.comm = torch.cuda.Stream(device=self.device)
@@ -248,6 +248,8 @@ class ShardedGemmPush:
                 ps.wait_event(start)
         yb = self.y.data_ptr()
         if self.engine == "epilogue":
+            if self.peers:
+                s0.wait_event(start)  # the GEMM's pushes start once every rank is done with its Y
             off = 4 * c0
             self.h.run_push(x.data_ptr(), yb + off, self.m, n, [ptr + off for _, ptr, _ in self.peers],
                             s0.cuda_stream)
