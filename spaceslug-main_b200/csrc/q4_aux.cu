@@ -541,6 +541,43 @@ int launch_push_rows(const float* src, const PeerPtrs& peers, int npeers, int ro
     return static_cast<int>(cudaGetLastError());
 }
 
+namespace {
+
+// n floats from src to dst (device memory or mapped pinned host memory on
+// either side), and, when status_src is given, the status word too.  A kernel
+// instead of a copy-engine transfer: for the few kilobytes of a decode call's
+// X and Y, the fixed cost of a copy-engine operation dominates.
+__global__ void __launch_bounds__(256) copy_words_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                                         long long n, int vec, const int* __restrict__ status_src,
+                                                         int* __restrict__ status_dst) {
+    const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    if (vec) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (long long i = i0; i < n / 4; i += stride) d4[i] = s4[i];
+    } else {
+        for (long long i = i0; i < n; i += stride) dst[i] = src[i];
+    }
+    if (status_src != nullptr && i0 == 0) *status_dst = *status_src;
+}
+
+}  // namespace
+
+int launch_copy_words(const float* src, float* dst, long long n, const int* status_src, int* status_dst,
+                      cudaStream_t stream) {
+    if (n < 0 || (n > 0 && (src == nullptr || dst == nullptr)) || ((status_src == nullptr) != (status_dst == nullptr)))
+        return static_cast<int>(cudaErrorInvalidValue);
+    const int vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+    const long long units = vec ? n / 4 : n;
+    long long blocks = (units + 255) / 256;
+    if (blocks < 1) blocks = 1;
+    if (blocks > 1024) blocks = 1024;
+    copy_words_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, n, vec, status_src, status_dst);
+    return static_cast<int>(cudaGetLastError());
+}
+
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream) {
     lora_delta64_kernel<<<M, 64, 0, stream>>>(x, a, b, y, rank);

@@ -149,6 +149,10 @@ int lora_xa_chunks(int K);
 // (peer-mapped device pointers) by `ctas` CTAs of plain global stores.
 int launch_push_rows(const float* src, const PeerPtrs& peers, int npeers, int rows, int width, long long ld, int ctas,
                      cudaStream_t stream);
+// n floats src -> dst by a small kernel (either side device memory or mapped
+// pinned host memory), plus the status word when status_src is given.
+int launch_copy_words(const float* src, float* dst, long long n, const int* status_src, int* status_dst,
+                      cudaStream_t stream);
 int launch_shards_relayout(const float* gathered, float* y, int parts, int rows, int width, int n_total,
                            long long ld_y, cudaStream_t stream);
 // CQ4 activation transform into the code basis, fp16 [M][K] -> fp16 [M][K]:

@@ -61,7 +61,8 @@ struct DeviceCtx {
     std::string init_error;
     int sm_count = 0;
     int* status = nullptr;  // device int, kernels record wait timeouts here
-    int* status_host = nullptr;     // pinned host word the host entry points read `status` into
+    int* status_host = nullptr;     // pinned, mapped host word the host entry points read `status` into
+    int* status_host_dev = nullptr; // its device address
     cudaStream_t stream = nullptr;  // for the synchronous host-pointer entry points
     std::mutex host_mu;             // serialises use of `stream` and `hbuf` by host entry points
     void* hbuf = nullptr;           // device staging of X and Y for spaceslug_q4_weights_run_host (grows)
@@ -107,8 +108,10 @@ DeviceCtx& ctx_for(int device) {
                                              std::to_string(major) + std::to_string(minor));
             check(cudaMalloc(&c.status, sizeof(int)), "cudaMalloc status");
             check(cudaMemset(c.status, 0, sizeof(int)), "cudaMemset status");
-            check(cudaHostAlloc(reinterpret_cast<void**>(&c.status_host), sizeof(int), cudaHostAllocDefault),
+            check(cudaHostAlloc(reinterpret_cast<void**>(&c.status_host), sizeof(int), cudaHostAllocMapped),
                   "cudaHostAlloc status");
+            check(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c.status_host_dev), c.status_host, 0),
+                  "cudaHostGetDevicePointer status");
             *c.status_host = 0;
             check(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate");
             cudaMemPool_t pool;
@@ -547,16 +550,31 @@ void run_problem(const Problem& p, cudaStream_t stream) {
 
 // Reads and clears the status word (synchronises `stream` first).
 // The status word rides on the same stream as the call's own copies, so one
-// synchronisation covers both (no second round trip per call).
-int take_status(DeviceCtx& c, cudaStream_t stream) {
-    check(cudaMemcpyAsync(c.status_host, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream), "read status");
+// synchronisation covers both (no second round trip per call).  With
+// `enqueued`, the call's copy-out kernel has already written it to the mapped
+// host word.
+int take_status(DeviceCtx& c, cudaStream_t stream, bool enqueued = false) {
+    if (!enqueued)
+        check(cudaMemcpyAsync(c.status_host, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream), "read status");
     check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
-    const int st = *c.status_host;
+    const int st = *static_cast<volatile int*>(c.status_host);
     if (st) {
         check(cudaMemsetAsync(c.status, 0, sizeof(int), stream), "clear status");
         check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     }
     return st;
+}
+
+// The address on the current device of a pinned, mapped host buffer (any
+// page-locked allocation under unified addressing), or nullptr for pageable
+// memory.
+void* mapped_device_pointer(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();  // a plain pageable pointer on older drivers
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
 }
 
 // Device staging for a host-pointer call, kept per device and grown on
@@ -1212,13 +1230,26 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
         char* stage = static_cast<char*>(host_staging(c, yoff + yb));
         float* dx = reinterpret_cast<float*>(stage);
         float* dy = reinterpret_cast<float*>(stage + yoff);
-        h2d(dx, x, xb, c.stream);
+        // Pinned (mapped) host buffers move by small kernels over the bus, the
+        // status word with Y; pageable ones by copy-engine transfers.
+        const float* xmap = static_cast<const float*>(mapped_device_pointer(x));
+        float* ymap = static_cast<float*>(mapped_device_pointer(y));
+        if (xmap)
+            check_launch(q4::launch_copy_words(xmap, dx, static_cast<long long>(m) * w->K, nullptr, nullptr, c.stream),
+                         "copy X in");
+        else
+            h2d(dx, x, xb, c.stream);
         Problem p{dx, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, dy,
                   static_cast<int>(m), w->N, w->K};
         p.sm_budget = w->sm_budget;
         run_problem(p, c.stream);
-        d2h(y, dy, yb, c.stream);
-        if (take_status(c, c.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
+        if (ymap)
+            check_launch(q4::launch_copy_words(dy, ymap, static_cast<long long>(m) * w->N, c.status, c.status_host_dev,
+                                               c.stream),
+                         "copy Y out");
+        else
+            d2h(y, dy, yb, c.stream);
+        if (take_status(c, c.stream, ymap != nullptr)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
         return SPACESLUG_OK;
     });
 }

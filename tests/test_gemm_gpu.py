@@ -258,3 +258,24 @@ def test_run_push_stores_the_same_block_into_every_peer_buffer(session, cuda, m,
     want = ref.cpu().numpy().view(np.uint32)
     for b in bufs:
         assert np.array_equal(b.cpu().numpy().view(np.uint32), want)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 1000, 1024), (64, 4500, 1152), (3, 37, 64)])
+def test_run_host_pinned_buffers_match_pageable(session, cuda, m, n, k):
+    """spaceslug_q4_weights_run_host moves pinned (device-mapped) X and Y by
+    small kernels and pageable ones by copy-engine transfers: both give the
+    same Y, bit for bit, and a clean status."""
+    import ctypes
+    import torch
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=n + k)
+    x = synth.make_x(m, k, seed=m + 3)
+    fp = ctypes.POINTER(ctypes.c_float)
+    with session.weights(packed, scales, k, n) as h:
+        y_pageable = h.run_host(x)
+        xh = torch.from_numpy(x).pin_memory()
+        yh = torch.full((m, n), float("nan"), dtype=torch.float32).pin_memory()
+        run_host = session.raw("spaceslug_q4_weights_run_host")
+        for _ in range(2):
+            assert run_host(h.handle, ctypes.cast(xh.data_ptr(), fp), ctypes.cast(yh.data_ptr(), fp), m) == 0
+    assert np.array_equal(yh.numpy().view(np.uint32), y_pageable.view(np.uint32))
+    assert session.device_status(0) == 0
