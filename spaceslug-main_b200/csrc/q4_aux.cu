@@ -547,9 +547,14 @@ namespace {
 // either side), and, when status_src is given, the status word too.  A kernel
 // instead of a copy-engine transfer: for the few kilobytes of a decode call's
 // X and Y, the fixed cost of a copy-engine operation dominates.
+// Launched as a programmatic dependent: it lets its own dependents launch at
+// once (a GEMV after a copy-in starts streaming its weights while X arrives)
+// and waits for its predecessor's writes (a copy-out reads the GEMV's Y).
 __global__ void __launch_bounds__(256) copy_words_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                                          long long n, int vec, const int* __restrict__ status_src,
                                                          int* __restrict__ status_dst) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     if (vec) {
@@ -574,8 +579,16 @@ int launch_copy_words(const float* src, float* dst, long long n, const int* stat
     long long blocks = (units + 255) / 256;
     if (blocks < 1) blocks = 1;
     if (blocks > 1024) blocks = 1024;
-    copy_words_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, n, vec, status_src, status_dst);
-    return static_cast<int>(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, copy_words_kernel, src, dst, n, vec, status_src, status_dst));
 }
 
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
