@@ -442,9 +442,62 @@ def gemm_gpu(args, dist: Dist, torch, session, synth, peaks, name: str, steps: i
            "flops": flops, "launches_per_step": launches, "shape": [cfg.m, cfg.k, cfg.n]}
     if cfg.rank:
         out["lora_flops_excluded"] = 2.0 * cfg.m * cfg.k * cfg.rank + 2.0 * cfg.m * cfg.rank * cfg.n
+    # parity of this output (outside the timed region): sampled rows against the
+    # reference's own cpu_reference, the whole output for configs[0]
+    stream.synchronize()
+    if name == "tiny":
+        from spaceslug_b200 import parity
+        t = np.load(ROOT / "tests" / "golden" / "cfg_tiny.npz")
+        rep = parity.gemm_error_report(y.cpu().numpy(), t["y_ref"], t["x"], 8.0 * float(np.abs(t["scales"]).max()),
+                                       cfg.k)
+        out["parity"] = {"rows": "all", "pass": parity.gemm_passes(rep),
+                         "reference": "cpu_reference output (tests/golden/cfg_tiny.npz)",
+                         **{k_: (round(v, 8) if isinstance(v, float) else v) for k_, v in rep.items()}}
+    else:
+        gold = golden_rows()
+        if gold is not None:
+            sel = torch.from_numpy(gold[f"{name}_rows"]).to(dev)
+            out["parity"] = rows_parity(y[sel].cpu().numpy(), name, cfg.k)
     h.close()
     del flush
     return out
+
+
+def q4_1024_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
+    """The reference's own q4gemm bench case (vulkan-runtime/bench/bench_q4gemm.cpp:36-47,
+    155-162): M = N = K = 1024, A U[-1, 1) seed 0x12345678, int4 seed 0x9abcdef0,
+    scales U[0.5, 1.5) seed 0x13579bdf (its generators, bit-exact), 128 warm-up
+    calls, then the median device time of 15 calls, operands resident as in
+    the reference bench."""
+    dev = torch.device("cuda", dist.local)
+    M = N = K = 1024
+    a = synth.lcg_floats(M * K, 0x12345678, -1.0, 1.0).reshape(M, K)
+    b = synth.lcg_int4(K * N, 0x9ABCDEF0).reshape(K, N)
+    sc = synth.lcg_floats(N * (K // 32), 0x13579BDF, 0.5, 1.5).reshape(N, K // 32)
+    h = session.weights(synth.pack(b), sc, K, N, device=dist.local)
+    x = torch.from_numpy(a).to(dev)
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    fn = lambda: h.run(x.data_ptr(), y.data_ptr(), M, stream.cuda_stream)  # noqa: E731
+    fn()
+    stream.synchronize()
+    g = capture(torch, stream, fn)
+    for _ in range(128):
+        g.replay()
+    times = []
+    with torch.cuda.stream(stream):
+        for _ in range(15):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            times.append((e0, e1))
+    stream.synchronize()
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in times)
+    tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    h.close()
+    return {"us": round(ms * 1e3, 2), "TFLOP/s": round(tflops, 1), "frac_of_bf16_peak": round(tflops / peaks["bf16_tflops"], 4),
+            "protocol": "128 warm-up calls, median of 15 (bench_q4gemm.cpp:44-45)", "shape": [M, K, N]}
 
 
 def upload_gpu(args, dist: Dist, torch, session) -> dict:
@@ -572,33 +625,56 @@ def sgemm_gpu(args, dist: Dist, torch, session) -> dict:
     return out
 
 
-def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
-    """columns of W sharded over the ranks; Y all-gathered over NVLink.
+def golden_rows() -> dict | None:
+    """Reference outputs on sampled rows of configs[2]-[4] (tests/golden/cfg_rows.npz,
+    made from the reference's own cpu_reference by tests/golden/make_config_rows.py)."""
+    p = ROOT / "tests" / "golden" / "cfg_rows.npz"
+    return dict(np.load(p)) if p.is_file() else None
 
-    Timed per step (L2 flushed before each), over row-band counts, the
-    exchanges of the sharding module: ShardedGemm (GEMM of row band b+1 on the
-    compute stream while band b is all-gathered by NCCL and re-laid out into
-    row-major Y) and ShardedGemmPush (GEMM writes into a row-major Y every
-    peer has mapped; each finished band is pushed to the peers by copy
-    engines or by a push kernel on SMs the GEMM leaves free, or every finished
-    tile by the GEMM's own epilogue).  The value is
-    the fastest variant (named in the line); the GEMM alone, the NCCL
-    all-gather of the whole Y alone and the re-layout alone are timed the
-    same way for the breakdown."""
+
+def rows_parity(y_rows: np.ndarray, name: str, k: int) -> dict:
+    """Parity of sampled rows of Y against the committed reference rows: the
+    tensor-core bars (max-abs <= 1e-3 ||x|| ||W|| sqrt(K), normwise <= 2e-3)
+    and, reported beside them, the reference's elementwise criterion."""
+    from spaceslug_b200 import parity
+    gold = golden_rows()
+    if gold is None:
+        return {"unavailable": "tests/golden/cfg_rows.npz is missing"}
+    rep = parity.gemm_error_report_bound(y_rows, gold[f"{name}_y"], float(gold[f"{name}_xinf"]),
+                                         float(gold[f"{name}_wabs"]), k)
+    return {"rows": [int(r) for r in gold[f"{name}_rows"]], "pass": parity.gemm_passes(rep),
+            "reference": "cpu_reference of vulkan-runtime/tests/test_q4gemm.cpp:102-119 (tests/golden/cfg_rows.npz)",
+            **{key: (round(v, 8) if isinstance(v, float) else v) for key, v in rep.items()}}
+
+
+def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
+    """columns of W sharded over the ranks, the full fp32 Y on every rank.
+
+    The headline step is the exchange the library picks for this world size
+    (sharding.choose_exchange / make_sharded), timed per step with the L2
+    flushed (256 MB write) before each step.  For the breakdown the GEMM
+    alone, the NCCL all-gather of the whole Y alone, the SM push of the whole
+    shard alone (its receive bandwidth) and the other exchange forms are timed
+    the same way.  After timing, the chosen exchange runs once more on a Y
+    filled with NaN and every rank checks: all of Y finite, the sampled rows
+    against the reference's own cpu_reference, and a checksum of the whole Y
+    equal on every rank."""
     from spaceslug_b200 import sharding
     dev = torch.device("cuda", dist.local)
     cfg = synth.CONFIGS["mlp70b"]
     w_kn, packed, scales = synth.make_weights(cfg.k, cfg.n, cfg.scale_lo, cfg.scale_hi, 0)
     del w_kn
-    c0, c1 = sharding.shard_columns(cfg.n, dist.world, dist.rank)
+    p = dist.world
+    c0, c1 = sharding.shard_columns(cfg.n, p, dist.rank)
     h = session.weights(packed, scales, cfg.k, cfg.n, c0, c1, device=dist.local)
     del packed, scales
     x = torch.from_numpy(synth.make_x(cfg.m, cfg.k, 0)).to(dev)
-    y = torch.empty((cfg.m, cfg.n), dtype=torch.float32, device=dev)
     ysh = torch.empty((cfg.m, c1 - c0), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(device=dev)
     flush = l2_flush_buffer(torch, dev)
     flops = 2.0 * cfg.m * cfg.n * cfg.k
+    gold = golden_rows()
+    rows = gold["mlp70b_rows"] if gold is not None else np.arange(8)
 
     def timed(fn, steps):
         evs = []
@@ -614,6 +690,10 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
         dist.barrier()
         return dist.max(sum(a.elapsed_time(b) for a, b in evs[args.warmup:]) / steps)
 
+    def checksum(t) -> int:
+        """Order-independent exact checksum of a float32 tensor's bits."""
+        return int(t.view(torch.int32).to(torch.int64).sum().item())
+
     steps = args.steps
     n0 = session.launch_count()
     h.run(x.data_ptr(), ysh.data_ptr(), cfg.m, stream.cuda_stream)
@@ -622,73 +702,101 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     dist.barrier()
     g_ms = timed(lambda: h.run(x.data_ptr(), ysh.data_ptr(), cfg.m, stream.cuda_stream), steps)
     detail = {"gemm_ms": g_ms, "gemm_only_tflops": flops / (g_ms * 1e-3) / 1e12,
-              "per_gpu_frac_gemm": flops / dist.world / (g_ms * 1e-3) / 1e12 / peaks["bf16_tflops"]}
-    if dist.world == 1:
+              "per_gpu_frac_gemm": flops / p / (g_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+              "shard_columns": [c0, c1]}
+    if p == 1:
+        ysh.fill_(float("nan"))
+        h.run(x.data_ptr(), ysh.data_ptr(), cfg.m, stream.cuda_stream)
+        stream.synchronize()
+        par = rows_parity(ysh[torch.from_numpy(rows).to(dev)].cpu().numpy(), "mlp70b", cfg.k)
+        par["all_finite"] = bool(torch.isfinite(ysh).all().item())
+        par["pass"] = bool(par.get("pass", False) and par["all_finite"])
         h.close()
-        detail.update({"ms_per_step": g_ms, "exchange": "none (one GPU)"})
-        return {"value": detail["gemm_only_tflops"], "ms_per_step": g_ms, "detail": detail,
+        target_ms = flops / (peaks["bf16_tflops"] * 1e12) * 1e3
+        detail.update({"ms_per_step": g_ms, "exchange": "none (one GPU)",
+                       "roofline": {"target_ms": target_ms, "frac": target_ms / g_ms,
+                                    "bound": "GEMM at the measured bf16 peak"}})
+        return {"value": detail["gemm_only_tflops"], "ms_per_step": g_ms, "detail": detail, "parity": par,
                 "gpu_launches": gemm_launches * steps}
-    p = dist.world
     width = sharding.shard_width(cfg.n, p)
     recv = (p - 1) * cfg.m * width * 4
-    best = None
-    for bands in (1, 2, 4):
-        piped = sharding.ShardedGemm(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands)
-        n0 = session.launch_count()
-        piped.run(x, y, stream)
-        launches = session.launch_count() - n0
-        stream.synchronize()
-        dist.barrier()
-        t_ms = timed(lambda: piped.run(x, y, stream), steps)
-        detail[f"bands{bands}_ms"] = t_ms
-        if best is None or t_ms < best[1]:
-            best = (bands, t_ms, launches)
-        if bands == 1:
-            g = piped.gathered.view(p * cfg.m, width)
-            ag = timed(lambda: dist.pg.all_gather_into_tensor(g, piped.ys), steps)
-            rl = timed(lambda: session.shards_relayout(g.data_ptr(), y.data_ptr(), p, cfg.m, width, cfg.n, cfg.n,
-                                                       stream.cuda_stream), steps)
-            algbw = p * cfg.m * width * 4 / (ag * 1e-3) / 1e9
-            detail.update({"nccl_allgather_ms": ag, "allgather_algbw_GBs": algbw,
-                           "allgather_busbw_GBs": algbw * (p - 1) / p,
-                           "allgather_recv_bytes_per_gpu": recv, "relayout_ms": rl,
-                           "relayout_GBs": 2 * cfg.m * cfg.n * 4 / (rl * 1e-3) / 1e9})
-        del piped
-        torch.cuda.empty_cache()
-    best = (best[0], best[1], best[2], "nccl")
-    del y
+    # breakdown: the NCCL all-gather of the whole Y alone, and the re-layout
+    piped = sharding.ShardedGemm(session, h, cfg.m, cfg.n, dist.pg, dev, bands=1)
+    g = piped.gathered.view(p * cfg.m, width)
+    y_rm = torch.empty((cfg.m, cfg.n), dtype=torch.float32, device=dev)
+    ag = timed(lambda: dist.pg.all_gather_into_tensor(g, piped.ys), steps)
+    rl = timed(lambda: session.shards_relayout(g.data_ptr(), y_rm.data_ptr(), p, cfg.m, width, cfg.n, cfg.n,
+                                               stream.cuda_stream), steps)
+    detail["nccl_bands1_ms"] = timed(lambda: piped.run(x, y_rm, stream), steps)
+    algbw = p * cfg.m * width * 4 / (ag * 1e-3) / 1e9
+    detail.update({"nccl_allgather_ms": ag, "allgather_algbw_GBs": algbw, "allgather_busbw_GBs": algbw * (p - 1) / p,
+                   "recv_bytes_per_gpu": recv, "relayout_ms": rl})
+    del piped, g, y_rm
     torch.cuda.empty_cache()
-    for engine, bands, sms in (("epilogue", 1, 0), ("copy", 1, 0), ("copy", 2, 0), ("copy", 4, 0), ("sm", 2, 16),
-                               ("sm", 4, 16), ("sm", 4, 24), ("sm", 8, 16)):
-        name = f"push_{engine}_bands{bands}" + (f"_sms{sms}" if engine == "sm" else "")
-        push = None
-        try:  # a failing exchange is reported and the others still measured (every rank takes the same path)
-            push = sharding.ShardedGemmPush(session, h, cfg.m, cfg.n, dist.pg, dev, bands=bands, engine=engine,
-                                            push_sms=sms or 16)
+    chosen = sharding.choose_exchange(p)
+    variants = [dict(chosen)]
+    for alt in ({"engine": "epilogue", "bands": 1, "push_sms": 16}, {"engine": "sm", "bands": 4, "push_sms": 16},
+                {"engine": "sm", "bands": 4, "push_sms": 24}):
+        if alt != chosen:
+            variants.append(alt)
+    result = None
+    for i, v in enumerate(variants):
+        name = f"push_{v['engine']}_bands{v['bands']}" + (f"_sms{v['push_sms']}" if v["engine"] == "sm" else "")
+        ex = None
+        try:  # a failing alternative is reported and the others still measured (every rank takes the same path)
+            ex = sharding.make_sharded(session, h, cfg.m, cfg.n, dist.pg, dev, **v)
             n0 = session.launch_count()
-            push.run(x, stream)
+            ex.run(x, stream)
             launches = session.launch_count() - n0
             stream.synchronize()
             dist.barrier()
-            t_ms = timed(lambda: push.run(x, stream), steps)
+            t_ms = timed(lambda: ex.run(x, stream), steps)
             detail[name + "_ms"] = t_ms
-            if t_ms < best[1]:
-                best = (bands, t_ms, launches, name)
+            if i == 0:
+                # the exchange alone: the whole shard pushed to every peer by
+                # the same SM push kernel, on all SMs, between two barriers
+                cols = c1 - c0
+                yb = ex.y.data_ptr() + 4 * c0
+                peers = [ptr + 4 * c0 for _, ptr, _ in ex.peers]
+                push_ms = timed(lambda: session.push_rows(yb, peers, cfg.m, cols, cfg.n, 2 * 148,
+                                                          stream.cuda_stream), steps)
+                detail["push_alone_ms"] = push_ms
+                detail["push_alone_recv_GBs"] = recv / (push_ms * 1e-3) / 1e9
+                # parity of the exchanged Y on every rank
+                ex.y.fill_(float("nan"))
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                yfull = ex.run(x, stream)
+                stream.synchronize()
+                dist.barrier()
+                par = rows_parity(yfull[torch.from_numpy(rows).to(dev)].cpu().numpy(), "mlp70b", cfg.k)
+                finite = bool(torch.isfinite(yfull).all().item())
+                mine = checksum(yfull)
+                every = [None] * p
+                dist.pg.all_gather_object(every, mine)
+                ok = torch.tensor([1 if (par.get("pass") and finite and len(set(every)) == 1) else 0], device=dev)
+                dist.pg.all_reduce(ok, op=dist.pg.ReduceOp.MIN)
+                par.update({"all_finite": finite, "checksum_equal_on_all_ranks": len(set(every)) == 1,
+                            "checked_on_ranks": p, "pass_on_every_rank": bool(ok.item())})
+                result = (t_ms, launches, name, par)
         except Exception as exc:
             detail[name + "_error"] = str(exc)[:200]
-        if push is not None:
-            push.close()
-        del push
+            if i == 0:
+                raise
+        if ex is not None:
+            ex.close()
+        del ex
         torch.cuda.empty_cache()
-    bands, t_ms, launches, exchange = best
+    t_ms, launches, exchange, par = result
     target_ms = max(flops / p / (peaks["bf16_tflops"] * 1e12), recv / 770e9) * 1e3
-    detail.update({"bands": bands, "exchange": exchange, "ms_per_step": t_ms,
+    detail.update({"bands": chosen["bands"], "exchange": exchange, "exchange_choice": "sharding.choose_exchange",
+                   "ms_per_step": t_ms, "recv_GBs_in_step": recv / (t_ms * 1e-3) / 1e9,
                    "roofline": {"target_ms": target_ms, "frac": target_ms / t_ms,
-                                "bound": "max(GEMM/P at the measured bf16 peak, all-gather receive bytes at "
+                                "bound": "max(GEMM/P at the measured bf16 peak, receive bytes at "
                                          "770 GB/s per direction)"},
                    "y_shape": [cfg.m, cfg.n]})
     h.close()
-    return {"value": flops / (t_ms * 1e-3) / 1e12, "ms_per_step": t_ms, "detail": detail,
+    return {"value": flops / (t_ms * 1e-3) / 1e12, "ms_per_step": t_ms, "detail": detail, "parity": par,
             "gpu_launches": launches * steps}
 
 
@@ -735,11 +843,15 @@ def main() -> None:
                      "gpu_launches": r["gpu_launches"], "clocks": r["clocks"]})
         if dist.world == 1 and not args.no_secondary:
             sec = {}
-            for name in ("prefill", "lora"):
+            for name in ("prefill", "lora", "tiny"):
                 try:
                     sec[name] = gemm_gpu(args, dist, torch, session, synth, peaks, name, steps=10)
                 except Exception as exc:  # report, do not hide
                     sec[name] = {"error": str(exc)}
+            try:
+                sec["q4gemm_1024"] = q4_1024_gpu(args, dist, torch, session, synth, peaks)
+            except Exception as exc:  # report, do not hide
+                sec["q4gemm_1024"] = {"error": str(exc)}
             try:
                 sec["upload"] = upload_gpu(args, dist, torch, session)
             except Exception as exc:  # report, do not hide
@@ -753,14 +865,16 @@ def main() -> None:
             except Exception as exc:  # report, do not hide
                 sec["sgemm"] = {"error": str(exc)}
             line["secondary"] = sec
-        if dist.world > 1 and not args.no_secondary:
-            # the N-sharded config at this world size, beside the decode replicas
+        if not args.no_secondary:
+            # the N-sharded config at this world size (N = 1 included),
+            # beside the decode replicas
+            sec = line.setdefault("secondary", {})
             try:
                 r = mlp70b_gpu(args, dist, torch, session, synth, peaks)
-                line["secondary"] = {"mlp70b": {"TFLOP/s": r["value"], "ms_per_step": r["ms_per_step"],
-                                                "parallelism": f"N-shard x{dist.world}", **r["detail"]}}
+                sec["mlp70b"] = {"TFLOP/s": r["value"], "ms_per_step": r["ms_per_step"],
+                                 "parallelism": f"N-shard x{dist.world}", "parity": r["parity"], **r["detail"]}
             except Exception as exc:  # report, do not hide
-                line["secondary"] = {"mlp70b": {"error": str(exc)}}
+                sec["mlp70b"] = {"error": str(exc)}
         if dist.rank == 0 and dist.world == 1:
             line["cpu_baseline"] = cpu_reference_decode(args.cpu_seconds, threads=1)
     elif args.workload == "mlp70b":
@@ -772,7 +886,7 @@ def main() -> None:
                                 "bands": r["detail"].get("bands", 1),
                                 "exchange": r["detail"].get("exchange", "none"),
                                 "l2": "L2 flushed (256 MB write) before every step"},
-                     "detail": r["detail"]})
+                     "detail": r["detail"], "parity": r["parity"]})
     else:
         r = gemm_gpu(args, dist, torch, session, synth, peaks, args.workload)
         line.update({"value": r["TFLOP/s"], "unit": "TFLOP/s", "ms_per_step": r["ms"], "scaling": "weak",

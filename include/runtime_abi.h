@@ -175,7 +175,9 @@ int spaceslug_lora_train_step(const float* x, const float* dy, float* a, float* 
  * must split into 1, 2, 4 or 8 equal slices of at most 32 scale groups (every
  * K <= 1024 and every multiple of 256 up to 8192 does); other shapes return 1.  The first call on each device
  * sets up the array's address (make it before any stream capture).  All calls
- * on a device share the array: calls that overlap on the GPU race. */
+ * on a device share the array: calls that overlap on the GPU race.  The call
+ * returns before the kernels run, so a kernel wait that runs out of time is
+ * reported by spaceslug_q4_device_status(device), which allocates nothing. */
 int spaceslug_q4gemv_lora_noalloc(const float* x, const uint32_t* packed, const float* scales, const float* lora_a,
                                   const float* lora_b, uint32_t rank, float alpha, float* y, uint32_t m, uint32_t n,
                                   uint32_t k, void* stream);
@@ -199,9 +201,22 @@ int spaceslug_q4_set_gemm_variant(int variant);
  * Returns the previous value, or -1 for an invalid value. */
 int spaceslug_q4_set_decode_variant(int variant);
 
-/* Reads and clears the kernel status word of `device` (0 = no kernel wait
- * has timed out since the last call).  Synchronises the device. */
+/* Reads and clears the kernel status words of `device` (0 = no kernel wait
+ * has timed out since the last call): the word of the regular entry points
+ * and the one of spaceslug_q4gemv_lora_noalloc.  Synchronises the device.
+ * Allocates nothing (a device no regular entry point has run on has no
+ * word of its own yet and reads as 0), so the asynchronous entry points,
+ * the no-allocation one included, report a timeout through this call. */
 int spaceslug_q4_device_status(int device);
+
+/* Test hook (no reference counterpart), current device: sets the time limit
+ * of the decode kernels' bounded waits to wait_limit_ns (0 = the default 2 s)
+ * and, with stall != 0, makes one warp in every CTA of those kernels wait on
+ * a barrier phase that nothing arms, so that the wait runs out, the kernel
+ * records the timeout and returns, and the call reports code 3 (synchronous
+ * entry points) or spaceslug_q4_device_status reports it (asynchronous ones).
+ * Synchronises the device first.  For tests of the timeout path only. */
+int spaceslug_q4_debug_wait_test(uint64_t wait_limit_ns, int stall);
 
 /* Number of kernels this library has launched since load (all devices). */
 uint64_t spaceslug_q4_launch_count(void);

@@ -55,6 +55,7 @@ _SIGNATURES = {
     "spaceslug_q4_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_set_decode_variant": ([ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_device_status": ([ctypes.c_int], ctypes.c_int),
+    "spaceslug_q4_debug_wait_test": ([ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
     "spaceslug_q4_launch_count": ([], ctypes.c_uint64),
     "spaceslug_last_error": ([], ctypes.c_char_p),
     "spaceslug_sgemm": ([_f32p, _f32p, _f32p, _u32, _u32, _u32, _f32p], ctypes.c_int),

@@ -27,6 +27,12 @@ enum KernelStatus : int {
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 
+// The limit the bounded waits below apply, per translation unit (each .cu
+// file that includes this header has its own copy, read only when a wait
+// does not complete at once).  A test shortens it through a file's setter
+// (gemv_tile_set_wait_test) to make a wait run out quickly.
+static __device__ unsigned long long g_wait_limit_ns = kWaitTimeoutNs;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -76,11 +82,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
                                             int code) {
     const unsigned long long t0 = globaltimer_ns();
+    const unsigned long long limit = *static_cast<volatile unsigned long long*>(&g_wait_limit_ns);
 #pragma unroll 1
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        if (globaltimer_ns() - t0 > limit) {
             *abort_flag = 1;
             if (status) atomicCAS(status, 0, code);
             return false;
@@ -106,9 +113,10 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
 // copies already in flight land before the CTA exits.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
     const unsigned long long t0 = globaltimer_ns();
+    const unsigned long long limit = *static_cast<volatile unsigned long long*>(&g_wait_limit_ns);
 #pragma unroll 1
     while (!mbar_try_wait(bar, parity))
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+        if (globaltimer_ns() - t0 > limit) break;
 }
 
 // 4-byte asynchronous global -> shared copy; src_bytes = 0 writes zeros.

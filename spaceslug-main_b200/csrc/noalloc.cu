@@ -19,9 +19,16 @@
 // symbol names a host-side stand-in.  The first call on each device, with that
 // device current, looks up the device address with cudaGetSymbolAddress
 // (and the kernels load); make that first call before any stream capture.
+//
+// A kernel wait that runs out of time (the kernels bound every wait) records
+// a code in a second static word, g_noalloc_status; the call itself is
+// asynchronous and returns before the kernel runs, so the caller learns of a
+// timeout from spaceslug_q4_device_status(device), which reads and clears
+// this word (with cudaMemcpyFromSymbol / cudaMemcpyToSymbol: no allocation).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <mutex>
@@ -46,6 +53,7 @@ static __device__ __align__(256) int g_noalloc_status;  // kernel wait-timeout w
 
 struct DeviceState {
     std::once_flag once;
+    std::atomic<bool> ready{false};  // set once the symbol addresses are known
     cudaError_t err = cudaSuccess;
     float* t = nullptr;
     int* status = nullptr;
@@ -55,6 +63,23 @@ constexpr int kMaxDevices = 64;
 DeviceState g_state[kMaxDevices];
 
 }  // namespace
+
+namespace q4rt {
+// Reads and clears the status word of the no-allocation entry point on
+// `device` (the current device; the caller has synchronised it).  *out is 0
+// when that entry point never ran there.
+cudaError_t noalloc_take_status(int device, int* out) {
+    *out = 0;
+    if (device < 0 || device >= kMaxDevices || !g_state[device].ready.load(std::memory_order_acquire))
+        return cudaSuccess;
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_noalloc_status, sizeof(int));
+    if (e == cudaSuccess && *out != 0) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_noalloc_status, &zero, sizeof(int));
+    }
+    return e;
+}
+}  // namespace q4rt
 
 extern "C" int spaceslug_q4gemv_lora_noalloc(const float* x, const uint32_t* packed, const float* scales,
                                              const float* lora_a, const float* lora_b, uint32_t rank, float alpha,
@@ -85,6 +110,7 @@ extern "C" int spaceslug_q4gemv_lora_noalloc(const float* x, const uint32_t* pac
         if (st.err != cudaSuccess) return;
         st.status = static_cast<int*>(p);
         st.err = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (st.err == cudaSuccess) st.ready.store(true, std::memory_order_release);
     });
     if (st.err != cudaSuccess) return q4rt::set_error(SPACESLUG_RUNTIME_FAILURE, cudaGetErrorString(st.err));
 

@@ -288,11 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         *reinterpret_cast<const uint4*>(smem + C::kROff + r * C::kRBytes + nl * 32 + hh * 16);
                     const float sv = sc * cs;
                     const float2 s2v = make_float2(sv, sv);
-                    const __half2 s2h = __float2half2_rn(sv);
+                    __half2 s2h, s2l;
+                    split_scale_f16(sv, s2h, s2l);
                     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
                     if (lut == nullptr) {
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) out[j] = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                        for (int j = 0; j < 4; ++j) out[j] = dequant_f16x2_or<T16>(words[j], s2v, s2h, s2l);
                     } else {
                         // CQ4: pair (k, k+1) = RN16(codebook[idx] * norm), idx from byte b of the word
 #pragma unroll

@@ -300,11 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int pq = 0; pq < 2; ++pq) {
                     const float2 s2v = make_float2(sc[pq], sc[pq]);
-                    const __half2 s2h = __float2half2_rn(sc[pq]);
+                    __half2 s_hi, s_lo;
+                    split_scale_f16(sc[pq], s_hi, s_lo);
                     const uint32_t words[4] = {q[pq].x, q[pq].y, q[pq].z, q[pq].w};
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const uint4 d = dequant_f16x2_or<T16>(words[j], s2v, s2h);
+                        const uint4 d = dequant_f16x2_or<T16>(words[j], s2v, s_hi, s_lo);
                         v[pq * 16 + j * 4 + 0] = d.x;
                         v[pq * 16 + j * 4 + 1] = d.y;
                         v[pq * 16 + j * 4 + 2] = d.z;

@@ -100,6 +100,12 @@ __host__ __device__ inline GemvSmem gemv_layout(int M, int K, int S, int cols_pe
     return L;
 }
 
+// Test hook (gemv_ring_set_wait_test): when set, consumer warp 0 of every
+// CTA first waits for the second phase of ring stage 0's barrier, which the
+// producer cannot arm before that warp releases the stage, so the bounded
+// wait runs out and the timeout path runs.  Read once per thread at entry.
+static __device__ int g_ring_stall_test = 0;
+
 template <int M>
 __global__ void __launch_bounds__(kGemvThreads, 1)
     q4_gemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ scales,
@@ -128,6 +134,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     auto empty = [&](int s) { return smem_u32(bars + kStages + s); };
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int stall_test = warp == 0 ? *static_cast<volatile int*>(&g_ring_stall_test) : 0;
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(full(s), 1 + 32);  // TMA expect_tx arrival + 32 producer cp.async arrivals
@@ -211,7 +218,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
                 }
         };
         if (C::kPasses == 1) load_x(0);
-        for (int jc = 0; jc < nchunks; ++jc) {
+        bool stalled = false;
+        if (stall_test)  // phase 0 of stage 0 completes; its phase 1 waits on this warp
+            stalled = !(mbar_wait(full(0), 0u, abort_flag, status, kStatusTimeoutGemv) &&
+                        mbar_wait(full(0), 1u, abort_flag, status, kStatusTimeoutGemv));
+        for (int jc = 0; jc < nchunks && !stalled; ++jc) {
             const int s = jc % kStages;
             if (!mbar_wait(full(s), (jc / kStages) & 1u, abort_flag, status, kStatusTimeoutGemv)) break;
             const uint8_t* wst = stage_base + s * L.stage_bytes;
@@ -363,6 +374,12 @@ int gemv_max_active_clusters(int M, int K, int cluster_k, int cols_per_cluster) 
 }
 
 int gemv_chunk_columns() { return kCC; }
+
+int gemv_ring_set_wait_test(unsigned long long limit_ns, int stall) {
+    cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &limit_ns, sizeof(limit_ns));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_ring_stall_test, &stall, sizeof(stall));
+    return static_cast<int>(e);
+}
 
 int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
     switch (a.M) {

@@ -63,6 +63,12 @@ struct TileCfg {
 };
 
 __host__ __device__ inline int tile_warps(int) { return 16; }
+
+// Test hook (gemv_tile_set_wait_test): when set, warp 0 of every CTA also
+// waits for a second phase of its first weight barrier, which nothing arms,
+// so that bounded wait runs out and the timeout path runs (status word,
+// abort flag, the CTA returns).  Read once per warp-0 thread at entry.
+static __device__ int g_tile_stall_test = 0;
 constexpr int kMmaMaxChunksPerThread = 8;  // X conversion: M * kslice / 8 chunks over 512 threads
 
 struct TileLayout {
@@ -190,6 +196,7 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int stall_test = warp == 0 ? *static_cast<volatile int*>(&g_tile_stall_test) : 0;
     if (tid == 0) {
         for (int b = 0; b < L.nbox + 2; ++b) mbar_init(bar + 8u * b, 1);
         *abort_flag = 0;
@@ -236,6 +243,9 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
         // and columns 8o + 2q, 8o + 2q + 1 of each column octet o.
         bool ok = mbar_wait(sfull, 0u, abort_flag, status, kStatusTimeoutGemv) &&
                   mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
+        if (stall_test)  // phase 0 of box 0's barrier completes; phase 1 is never armed
+            ok = ok && mbar_wait(wfull(0), 0u, abort_flag, status, kStatusTimeoutGemv) &&
+                 mbar_wait(wfull(0), 1u, abort_flag, status, kStatusTimeoutGemv);
         float* rmax = reinterpret_cast<float*>(smem + L.misc_off + 16);             // [16 warps][8]
         int* rexp = reinterpret_cast<int*>(smem + L.misc_off + 16 + 16 * 8 * 4);    // [8]
         // X -> per-row exponents and f16 hi/lo planes, in place: chunks of 8 k
@@ -411,6 +421,9 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
 
         bool ok = mbar_wait(sfull, 0u, abort_flag, status, kStatusTimeoutGemv) &&
                   mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
+        if (stall_test)  // phase 0 of box 0's barrier completes; phase 1 is never armed
+            ok = ok && mbar_wait(wfull(0), 0u, abort_flag, status, kStatusTimeoutGemv) &&
+                 mbar_wait(wfull(0), 1u, abort_flag, status, kStatusTimeoutGemv);
         const uint32_t xs = base + L.x_off + j * 32;  // this lane's 8 x of word j in a group
 #pragma unroll 1
         for (int b = warp; b < L.nbox && ok; b += kWarps) {
@@ -569,6 +582,12 @@ int launch_tile_m(const GemvTileArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int gemv_tile_set_wait_test(unsigned long long limit_ns, int stall) {
+    cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &limit_ns, sizeof(limit_ns));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_tile_stall_test, &stall, sizeof(stall));
+    return static_cast<int>(e);
+}
 
 size_t gemv_tile_smem_bytes(int M, int K, int S) { return static_cast<size_t>(tile_layout(M, K, S).bytes); }
 

@@ -29,6 +29,11 @@ struct GemvArgs {
     int* status;             // kernel status word (0 = ok)
 };
 int launch_gemv(const GemvArgs& a, cudaStream_t stream);
+// Test hooks of the decode kernels, for the current device: the wait limit of
+// every bounded wait of that kernel file (ns) and, with stall != 0, one warp
+// per CTA that waits on a barrier phase nothing arms (the wait runs out).
+int gemv_ring_set_wait_test(unsigned long long limit_ns, int stall);
+int gemv_tile_set_wait_test(unsigned long long limit_ns, int stall);
 // Tensor-core decode (M <= 8): col_blocks blocks of <= 128 columns, each a
 // cluster of cluster_k CTAs splitting K into slices of <= 1024.
 struct DecodeArgs {

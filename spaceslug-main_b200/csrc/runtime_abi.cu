@@ -58,6 +58,7 @@ void check_launch(int e, const char* what) {
 struct DeviceCtx {
     std::once_flag once;
     bool ok = false;
+    std::atomic<bool> ready{false};  // ok, published for readers that must not initialise the context
     std::string init_error;
     int sm_count = 0;
     int* status = nullptr;  // device int, kernels record wait timeouts here
@@ -119,6 +120,7 @@ DeviceCtx& ctx_for(int device) {
             uint64_t keep = UINT64_MAX;
             check(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep), "pool threshold");
             c.ok = true;
+            c.ready.store(true, std::memory_order_release);
         } catch (const std::exception& e) {
             c.init_error = e.what();
         }
@@ -622,6 +624,7 @@ void d2h(void* dst, const void* src, size_t bytes, cudaStream_t s) {
 // reuse the GEMV geometry and tensor-map encoding above without touching the
 // per-device context, which allocates on first use.
 namespace q4rt {
+cudaError_t noalloc_take_status(int device, int* out);  // csrc/noalloc.cu
 bool gemv_geometry(int sm_count, int M, int N, int K, int* S, int* clusters, int* cols) {
     DeviceCtx tmp;
     tmp.sm_count = sm_count;
@@ -1450,14 +1453,33 @@ int spaceslug_q4_set_gemm_variant(int variant) {
 }
 
 int spaceslug_q4_device_status(int device) {
+    if (device < 0 || device >= kMaxDevices) return fail(SPACESLUG_INVALID_ARGUMENT, "device ordinal out of range");
     return guarded([&] {
         check(cudaSetDevice(device), "cudaSetDevice");
-        DeviceCtx& c = ctx_for(device);
         check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        // The context's word exists only once a regular entry point ran on the
+        // device; this call does not create the context (it allocates), so a
+        // caller of the no-allocation entry point alone allocates nothing here.
         int st = 0;
-        check(cudaMemcpy(&st, c.status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
-        if (st) check(cudaMemset(c.status, 0, sizeof(int)), "clear status");
-        return st;
+        DeviceCtx& c = g_ctx[device];
+        if (c.ready.load(std::memory_order_acquire)) {
+            check(cudaMemcpy(&st, c.status, sizeof(int), cudaMemcpyDeviceToHost), "read status");
+            if (st) check(cudaMemset(c.status, 0, sizeof(int)), "clear status");
+        }
+        int st_noalloc = 0;
+        check(q4rt::noalloc_take_status(device, &st_noalloc), "read the no-allocation status word");
+        return st != 0 ? st : st_noalloc;
+    });
+}
+
+int spaceslug_q4_debug_wait_test(uint64_t wait_limit_ns, int stall) {
+    return guarded([&] {
+        const unsigned long long lim = wait_limit_ns ? wait_limit_ns : 2000000000ull;
+        const int st = stall ? 1 : 0;
+        check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // no launch in flight sees a half-set hook
+        check(static_cast<cudaError_t>(q4::gemv_tile_set_wait_test(lim, st)), "set the tile GEMV test hook");
+        check(static_cast<cudaError_t>(q4::gemv_ring_set_wait_test(lim, st)), "set the ring GEMV test hook");
+        return SPACESLUG_OK;
     });
 }
 

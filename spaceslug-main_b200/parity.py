@@ -42,11 +42,16 @@ GEMM_NORM_REL_TOL = 2e-3
 
 def gemm_error_report(y, y_ref, x, w_absmax: float, k: int) -> dict:
     """Error metrics of an int4 GEMM output against the double oracle."""
+    x_inf = float(np.max(np.abs(x))) if np.size(x) else 0.0
+    return gemm_error_report_bound(y, y_ref, x_inf, w_absmax, k)
+
+
+def gemm_error_report_bound(y, y_ref, x_inf: float, w_absmax: float, k: int) -> dict:
+    """gemm_error_report with ||x||_inf given (y may hold sampled rows of Y)."""
     y = np.asarray(y, np.float64)
     r = np.asarray(y_ref, np.float64)
     diff = y - r
     max_abs = float(np.max(np.abs(diff))) if diff.size else 0.0
-    x_inf = float(np.max(np.abs(x))) if np.size(x) else 0.0
     abs_bound = GEMM_ABS_FACTOR * x_inf * w_absmax * math.sqrt(k)
     ref_norm = float(np.linalg.norm(r))
     norm_rel = float(np.linalg.norm(diff)) / ref_norm if ref_norm > 0 else float(np.linalg.norm(diff))
@@ -58,3 +63,8 @@ def gemm_error_report(y, y_ref, x, w_absmax: float, k: int) -> dict:
         "elem_rel": elem_rel,
         "finite": bool(np.all(np.isfinite(y))),
     }
+
+
+def gemm_passes(rep: dict) -> bool:
+    """The tensor-core GEMM bars: finite, max-abs within the bound, normwise <= 2e-3."""
+    return bool(rep["finite"] and rep["max_abs"] <= rep["abs_bound"] and rep["norm_rel"] <= GEMM_NORM_REL_TOL)

@@ -288,3 +288,36 @@ class ShardedGemmPush:
             fin.record(self.comm)
             s0.wait_event(fin)
         return self.y
+
+
+# The exchange each world size uses, chosen from measurements of configs[4]
+# (X 4096 x 8192, W 8192 x 28672, fp32 Y of 470 MB) on B200 boxes of this
+# kind, each step timed with the L2 flushed (step times of the fastest
+# variant, in ms, at P = 2 / 4 / 8: 0.82 / 0.71 / 0.77):
+#   P = 2: the GEMM epilogue pushes every finished block to the one peer;
+#   P = 4, 8: banded GEMM with an SM push kernel beside it on 16 / 24 SMs.
+# A P not listed takes the nearest listed one below it.
+EXCHANGE_BY_WORLD = {
+    2: {"engine": "epilogue", "bands": 1, "push_sms": 16},
+    4: {"engine": "sm", "bands": 4, "push_sms": 16},
+    8: {"engine": "sm", "bands": 4, "push_sms": 24},
+}
+
+
+def choose_exchange(world: int) -> dict:
+    """The exchange (engine, bands, push_sms) this library uses for `world` ranks."""
+    if world < 2:
+        return {"engine": "none", "bands": 1, "push_sms": 0}
+    return dict(EXCHANGE_BY_WORLD[max(p for p in EXCHANGE_BY_WORLD if p <= world)])
+
+
+def make_sharded(session, handle, m: int, n_total: int, dist, device, group=None, **override):
+    """The N-sharded GEMM with the exchange choose_exchange picks for this
+    world size (keyword arguments override it).  Returns a ShardedGemmPush;
+    its run(x, stream) returns the full Y on every rank."""
+    ch = choose_exchange(dist.get_world_size(group))
+    ch.update(override)
+    if ch["engine"] == "none":
+        raise ValueError("one rank needs no exchange: run the handle directly")
+    return ShardedGemmPush(session, handle, m, n_total, dist, device, bands=ch["bands"], group=group,
+                           engine=ch["engine"], push_sms=ch["push_sms"])

@@ -50,17 +50,39 @@ def _table():
     return _TABLE
 
 
+def _lcg_chunks(n: int, seed: int):
+    """Yields (offset, states) covering the first n LCG states after `seed`.
+
+    The stream is cut into blocks of _BLOCK states: block b starts from the
+    state reached after b * _BLOCK steps (a short sequential recurrence over
+    the blocks), and state i of a block is A_i * s_b + C_i mod 2^32, computed
+    for 64 blocks at a time in wrapping uint32 arithmetic.
+    """
+    a_tab, c_tab = _table()
+    a32, c32 = a_tab.astype(np.uint32), c_tab.astype(np.uint32)
+    nblocks = (n + _BLOCK - 1) // _BLOCK
+    a_block, c_block = int(a_tab[-1]), int(c_tab[-1])
+    starts = np.empty(max(nblocks, 1), np.uint32)
+    s = seed & _MASK
+    for b in range(nblocks):
+        starts[b] = s
+        s = (a_block * s + c_block) & _MASK
+    step = 64
+    buf = np.empty((step, _BLOCK), np.uint32)
+    for b0 in range(0, nblocks, step):
+        b1 = min(nblocks, b0 + step)
+        out = buf[:b1 - b0]
+        np.multiply(starts[b0:b1, None], a32[None, :], out=out)
+        out += c32[None, :]
+        off = b0 * _BLOCK
+        yield off, out.reshape(-1)[:max(0, min(n - off, (b1 - b0) * _BLOCK))]
+
+
 def lcg_states(n: int, seed: int) -> np.ndarray:
     """The first n LCG states after `seed` (state i = i+1 steps), as uint32."""
-    a_tab, c_tab = _table()
     out = np.empty(n, np.uint32)
-    a_block, c_block = int(a_tab[-1]), int(c_tab[-1])
-    s = seed & _MASK
-    for start in range(0, n, _BLOCK):
-        cnt = min(_BLOCK, n - start)
-        vals = (a_tab[:cnt] * np.uint64(s) + c_tab[:cnt]) & np.uint64(_MASK)
-        out[start:start + cnt] = vals.astype(np.uint32)
-        s = (a_block * s + c_block) & _MASK
+    for off, ch in _lcg_chunks(n, seed):
+        out[off:off + ch.size] = ch
     return out
 
 
@@ -73,8 +95,13 @@ def lcg_floats(n: int, seed: int, lo: float, hi: float) -> np.ndarray:
 
 def lcg_int4(n: int, seed: int) -> np.ndarray:
     """int4 values in [-8, 7], bit-exact with test_q4gemm.cpp:71-80."""
-    r = lcg_states(n, seed) >> np.uint32(8)
-    return ((r % np.uint32(16)).astype(np.int16) - 8).astype(np.int8)
+    v = np.empty(n, np.int8)
+    for off, ch in _lcg_chunks(n, seed):
+        ch >>= np.uint32(8)
+        ch &= np.uint32(15)  # (s >> 8) % 16
+        v[off:off + ch.size] = ch
+    v -= np.int8(8)
+    return v
 
 
 def normal(n: int, seed: int, std: float = 1.0) -> np.ndarray:

@@ -63,6 +63,12 @@ def golden():
     return {name: np.load(GOLDEN / f"{name}.npz") for name in ("ref_generators", "ref_q4gemm_256", "cfg_tiny")}
 
 
+@pytest.fixture(scope="session")
+def golden_rows():
+    """Reference outputs on sampled rows of BASELINE configs[2]-[4] (make_config_rows.py)."""
+    return dict(np.load(GOLDEN / "cfg_rows.npz"))
+
+
 def cuda_ok() -> bool:
     try:
         import torch

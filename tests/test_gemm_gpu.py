@@ -101,6 +101,21 @@ def test_gemm_config3_sampled_rows(session, oracle, cuda):
     assert np.all(np.isfinite(y))
 
 
+@pytest.mark.parametrize("name", ["prefill", "lora", "mlp70b"])
+def test_gemm_full_config_against_reference_rows(session, cuda, golden_rows, name):
+    # BASELINE configs[2], [3] and [4] at their own shapes on one GPU (configs[4]
+    # is X 4096x8192 . W 8192x28672: 117 MB of packed weights, 470 MB of Y),
+    # checked on sampled rows against the reference's own cpu_reference
+    # (tests/golden/cfg_rows.npz, made by tests/golden/make_config_rows.py).
+    inp = synth.make_inputs(name)
+    cfg = synth.CONFIGS[name]
+    y = session.q4gemm(inp.x, inp.packed, inp.scales, cfg.n, inp.lora_a, inp.lora_b, inp.alpha)
+    assert y.shape == (cfg.m, cfg.n) and np.all(np.isfinite(y))
+    rows = golden_rows[f"{name}_rows"]
+    rep = _check(y[rows], golden_rows[f"{name}_y"], inp.x, inp.scales, cfg.k)
+    print(name, rep)
+
+
 def test_gemm_large_magnitudes_do_not_overflow_f16(session, oracle, cuda):
     # activations far outside the f16 range and tiny scales: the power-of-two
     # operand exponents must keep the f16 path exact in range

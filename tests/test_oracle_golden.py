@@ -3,6 +3,7 @@ golden vectors produced by the reference's own code (tests/golden/)."""
 from __future__ import annotations
 
 import hashlib
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -115,3 +116,18 @@ def test_lora_oracle_matches_formula(oracle):
     oracle.lora_add(out, x, a, bb, 8.0)
     ref = (8.0 / r) * (x.astype(np.float64) @ a.astype(np.float64)) @ bb.astype(np.float64)
     assert np.allclose(out, ref, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", ["prefill", "lora", "mlp70b"])
+def test_oracle_matches_reference_rows_of_large_configs(oracle, name):
+    # cfg_rows.npz holds the reference's own cpu_reference (plus the LoRA
+    # restatement for configs[3]) on sampled rows of configs[2]-[4]; the
+    # double-precision restatement rounds to the same float32 values.
+    t = np.load(Path(__file__).resolve().parent / "golden" / "cfg_rows.npz")
+    inp = synth.make_inputs(name)
+    rows = t[f"{name}_rows"][[0, -1]]
+    y = oracle.gemm(np.ascontiguousarray(inp.x[rows]), inp.w_kn, inp.scales)
+    if inp.rank:
+        oracle.lora_add(y, np.ascontiguousarray(inp.x[rows]), inp.lora_a, inp.lora_b, inp.alpha)
+    assert np.array_equal(y.astype(np.float32), t[f"{name}_y"][[0, -1]])
+    assert float(t[f"{name}_xinf"]) == float(np.max(np.abs(inp.x)))
