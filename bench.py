@@ -463,6 +463,42 @@ def gemm_gpu(args, dist: Dist, torch, session, synth, peaks, name: str, steps: i
     return out
 
 
+def lora_backward_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
+    """LoRA training backward on a resident handle (spaceslug_q4_weights_lora_backward:
+    T = X A, G = dY B^T, dB = s T^T dY, dA = s X^T G) at configs[3]'s shape and at a
+    configs[4]-sized one (X 4096 x 8192, dY 4096 x 28672), rank 16.  Device time per
+    call from a CUDA graph, L2 flushed before each call.  The work is bound by HBM:
+    algorithmic bytes = X + dY + A + B read, dA + dB written (fp32)."""
+    dev = torch.device("cuda", dist.local)
+    stream = torch.cuda.Stream(device=dev)
+    flush = l2_flush_buffer(torch, dev)
+    out = {}
+    for name, (m, k, n) in (("configs3", (512, 4096, 4096)), ("configs4_size", (4096, 8192, 28672))):
+        r = 16
+        _, packed, scales = synth.make_weights(k, n, 0.005, 0.02, 1)
+        h = session.weights(packed, scales, k, n, device=dist.local)
+        h.set_lora(synth.normal(k * r, 2, 0.02).reshape(k, r), synth.normal(r * n, 3, 0.02).reshape(r, n), 32.0)
+        x = torch.randn((m, k), device=dev)
+        dy = torch.randn((m, n), device=dev)
+        fn = lambda: h.lora_backward(x.data_ptr(), dy.data_ptr(), m, stream.cuda_stream)  # noqa: E731
+        fn()
+        stream.synchronize()
+        n0 = session.launch_count()
+        g = capture(torch, stream, fn)
+        launches = session.launch_count() - n0
+        time_graph_replays(torch, stream, [g], 3, flush)
+        ms = time_graph_replays(torch, stream, [g], 10, flush)[0] / 10
+        nbytes = 4 * (m * k + m * n + 2 * k * r + 2 * r * n)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"shape_mkn_r": [m, k, n, r], "us": round(ms * 1e3, 1), "GB/s": round(gbs, 1),
+                     "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "launches": launches,
+                     "flops": 4.0 * m * r * (k + n)}
+        del g, x, dy
+        h.close()
+    del flush
+    return out
+
+
 def q4_1024_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
     """The reference's own q4gemm bench case (vulkan-runtime/bench/bench_q4gemm.cpp:36-47,
     155-162): M = N = K = 1024, A U[-1, 1) seed 0x12345678, int4 seed 0x9abcdef0,
@@ -527,7 +563,7 @@ def upload_gpu(args, dist: Dist, torch, session) -> dict:
     t = best(lambda: holder.__setitem__("p", session.q4_pack(b)))
     packed = holder.pop("p")
     out["host_pack_ms"] = round(t * 1e3, 1)
-    out["host_pack_threads"] = "several (std::thread, <= 8)"
+    out["host_threads"] = f"std::thread, the process's CPU affinity count capped at 16 ({min(16, len(os.sched_getaffinity(0)))} here)"
     session.weights(packed[:32], scales[:8, :1].copy(), 32, 8).close()  # a first handle sets up the device context
 
     def create(fn):
@@ -733,18 +769,19 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
                    "recv_bytes_per_gpu": recv, "relayout_ms": rl})
     del piped, g, y_rm
     torch.cuda.empty_cache()
-    chosen = sharding.choose_exchange(p)
+    # the library measures its candidate exchanges on this problem once and
+    # keeps the fastest (sharding.autotune_exchange, before the timed region)
+    tuned = sharding.autotune_exchange(session, h, cfg.m, cfg.n, dist.pg, dev, x, stream=stream)
+    chosen = {key: tuned[key] for key in ("engine", "bands", "push_sms")}
+    detail["exchange_tuning_ms"] = tuned.get("tuning_ms")
+    detail["exchange_table_choice"] = sharding.choose_exchange(p)
     variants = [dict(chosen)]
-    for alt in ({"engine": "epilogue", "bands": 1, "push_sms": 16}, {"engine": "sm", "bands": 4, "push_sms": 16},
-                {"engine": "sm", "bands": 4, "push_sms": 24}):
-        if alt != chosen:
-            variants.append(alt)
     result = None
     for i, v in enumerate(variants):
         name = f"push_{v['engine']}_bands{v['bands']}" + (f"_sms{v['push_sms']}" if v["engine"] == "sm" else "")
         ex = None
         try:  # a failing alternative is reported and the others still measured (every rank takes the same path)
-            ex = sharding.make_sharded(session, h, cfg.m, cfg.n, dist.pg, dev, **v)
+            ex = sharding.make_sharded(session, h, cfg.m, cfg.n, dist.pg, dev, stream=stream, **v)
             n0 = session.launch_count()
             ex.run(x, stream)
             launches = session.launch_count() - n0
@@ -789,7 +826,7 @@ def mlp70b_gpu(args, dist: Dist, torch, session, synth, peaks) -> dict:
         torch.cuda.empty_cache()
     t_ms, launches, exchange, par = result
     target_ms = max(flops / p / (peaks["bf16_tflops"] * 1e12), recv / 770e9) * 1e3
-    detail.update({"bands": chosen["bands"], "exchange": exchange, "exchange_choice": "sharding.choose_exchange",
+    detail.update({"bands": chosen["bands"], "exchange": exchange, "exchange_choice": "sharding.autotune_exchange",
                    "ms_per_step": t_ms, "recv_GBs_in_step": recv / (t_ms * 1e-3) / 1e9,
                    "roofline": {"target_ms": target_ms, "frac": target_ms / t_ms,
                                 "bound": "max(GEMM/P at the measured bf16 peak, receive bytes at "
@@ -852,6 +889,10 @@ def main() -> None:
                 sec["q4gemm_1024"] = q4_1024_gpu(args, dist, torch, session, synth, peaks)
             except Exception as exc:  # report, do not hide
                 sec["q4gemm_1024"] = {"error": str(exc)}
+            try:
+                sec["lora_backward"] = lora_backward_gpu(args, dist, torch, session, synth, peaks)
+            except Exception as exc:  # report, do not hide
+                sec["lora_backward"] = {"error": str(exc)}
             try:
                 sec["upload"] = upload_gpu(args, dist, torch, session)
             except Exception as exc:  # report, do not hide

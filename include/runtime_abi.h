@@ -195,8 +195,9 @@ int spaceslug_q4_set_operand_type(int type);
 int spaceslug_q4_set_gemm_variant(int variant);
 
 /* Decode (M <= 8) kernel selection: 0 = automatic (default), 1 = CUDA-core
- * GEMV with a streamed shared-memory ring, 2 = tensor-core decode, 3 = CUDA-core
- * GEMV with the whole tile resident.  A variant the shape does not allow falls
+ * GEMV with a streamed shared-memory ring, 2 = tcgen05 tensor-core decode,
+ * 3 = CUDA-core GEMV with the whole tile resident, 4 = integer-tensor-core
+ * (mma.sync s8) GEMV with exact int8 limbs of X (K % 1024 == 0).  A variant the shape does not allow falls
  * back to the automatic choice.  Results agree to fp32 summation order.
  * Returns the previous value, or -1 for an invalid value. */
 int spaceslug_q4_set_decode_variant(int variant);
@@ -227,11 +228,13 @@ const char* spaceslug_last_error(void);
 /* fp32 row-major C[m x n] = A[m x k] * B[k x n], host pointers, synchronous:
  * the reference's spaceslug_sgemm (vulkan-runtime/src/api/sgemm_api.h:5-9), same
  * checks (M, N % 64 == 0, K % 32 == 0) and codes; *max_relative_error is set
- * to 0 as the reference does.  A plain library GEMM: cuBLAS SGEMM with fp32
- * FMA (no TF32), cuBLAS loaded on first use. */
+ * to 0 as the reference does.  Computed on the tcgen05 tensor cores with
+ * fp32-level accuracy: each operand split into TF32 hi + lo parts, three TF32
+ * MMAs per product (hi*hi + hi*lo + lo*hi) accumulated in fp32. */
 int spaceslug_sgemm(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
                     float* max_relative_error);
-/* Same product for device pointers, any positive m, n, k, asynchronous on `stream`. */
+/* Same product for device pointers, any positive m, n, k, asynchronous on
+ * `stream`; the TF32 hi/lo planes of the operands take stream-ordered scratch. */
 int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, void* stream);
 
 /* spaceslug_q4_weights_run with a row pitch: Y[i][j] at y[i * ld_y + j] for

@@ -245,7 +245,7 @@ class BackendSession:
         return {v: k for k, v in names.items()}.get(prev, "?")
 
     def set_decode_variant(self, variant: str) -> str:
-        names = {"auto": 0, "gemv": 1, "mma": 2, "tile": 3}
+        names = {"auto": 0, "gemv": 1, "mma": 2, "tile": 3, "imma": 4}
         prev = self.raw("spaceslug_q4_set_decode_variant")(names[variant])
         return {v: k for k, v in names.items()}.get(prev, "?")
 

@@ -32,12 +32,13 @@
 //   * LoRA: the epilogue adds (alpha/r) * sum_r T[m][r] B[r][n] in fp32 (T =
 //     X*A from the projection kernel) to each staged block before it leaves;
 //     with ksplit = 2 each K half adds half of the ranks.
-//   * peer push (N-sharded layers, ksplit = 1): besides the TMA store into
-//     this GPU's Y, the epilogue warp stores each staged block to the same
-//     rows and columns of up to 7 peers' Y (plain 16-byte stores through
-//     NVLink peer mappings), so the exchange of Y runs tile by tile beside
-//     the next tile's main loop.  The accumulator is released before the
-//     pushes, so only the epilogue warps wait for the link.
+//   * peer push (N-sharded layers, ksplit = 1): after the TMA stores of a
+//     tile into this GPU's Y have completed (and the accumulator has gone
+//     back to the MMA), each epilogue warp reads its blocks back from Y (L2)
+//     and stores them to the same rows and columns of up to 7 peers' Y
+//     (plain 16-byte stores through NVLink peer mappings), so the exchange
+//     of Y runs tile by tile beside the next tile's main loop; only the
+//     epilogue warps wait for the link.
 //
 // Shared memory per SM and stage carries 32 KB of X written by TMA and read
 // by the MMA plus 10 KB of packed W and scales in and out: about 84 B/clk at
@@ -108,7 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int* __restrict__ col_exp,
                         const int* __restrict__ row_exp, int M, int N, int K, int ksplit,
                         const float* __restrict__ lora_t, const float* __restrict__ lora_b, int rank,
-                        float lora_scale, PeerPtrs peers, int npeers, long long ld_y, int* __restrict__ status) {
+                        float lora_scale, PeerPtrs peers, int npeers, long long ld_y, const float* y_local,
+                        int* __restrict__ status) {
     using C = PCfg;
     constexpr int ST = kStages;
     constexpr int RT = kRawStages;
@@ -422,22 +424,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     bulk_commit_group();
                 }
-                if (npeers > 0 && mc < M && nx < N) {
-                    // the block to every peer: float4 j = lane + 32 i is row j / 8,
-                    // columns 4 (j % 8) .. +3 (8 lanes write one 128-byte row)
+                if (cc + 1 < kEpiChunks) tmem_ld_wait_regs(rv[(cc + 1) & 1]);
+            }
+            if (npeers > 0 && nx < N) {
+                // The tile's blocks to every peer, after the accumulator went
+                // back to the MMA (the link traffic overlaps the next tile's
+                // main loop): once this warp's bulk stores of the tile have
+                // completed, the blocks are read back from this GPU's Y (L2)
+                // and stored to each peer's Y.  float4 j = lane + 32 i of a
+                // block is row j / 8, columns 4 (j % 8) .. +3 (8 lanes write
+                // one 128-byte row).
+                if (lane == 0) bulk_wait_group_all();
+                __syncwarp();
+                asm volatile("fence.proxy.async.global;" ::: "memory");  // async-proxy writes before generic reads
+#pragma unroll 1
+                for (int cc = 0; cc < kEpiChunks; ++cc) {
+                    const int mc = m0 + (c0 + cc) * 32;
+                    if (mc >= M) break;
 #pragma unroll 2
                     for (int i = 0; i < 8; ++i) {
                         const int j = lane + 32 * i, r = j >> 3, c4 = (j & 7) * 4;
                         if (mc + r < M && nx + c4 < N) {
-                            const float4 v = *reinterpret_cast<const float4*>(bufp + r * 32 + c4);
                             const long long at = static_cast<long long>(mc + r) * ld_y + nx + c4;
+                            const float4 v = *reinterpret_cast<const float4*>(y_local + at);
 #pragma unroll
                             for (int q = 0; q < kMaxPeers; ++q)  // constant indices: no local copy of the array
                                 if (q < npeers) *reinterpret_cast<float4*>(peers.p[q] + at) = v;
                         }
                     }
                 }
-                if (cc + 1 < kEpiChunks) tmem_ld_wait_regs(rv[(cc + 1) & 1]);
             }
         }
         if (lane == 0) bulk_wait_group_all();  // the stores have read their blocks before the CTA exits
@@ -472,7 +487,7 @@ int launch_pair_t(const GemmArgs& a, int pairs, cudaStream_t stream) {
     cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kern, a.tmap_x16, a.tmap_w, a.tmap_s, a.tmap_y, a.col_exp, a.row_exp, a.M, a.N,
                            a.K, a.ksplit, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.peers, a.npeers, a.peer_ld,
-                           a.status);
+                           static_cast<const float*>(a.y), a.status);
     return static_cast<int>(e);
 }
 

@@ -34,6 +34,30 @@ int launch_gemv(const GemvArgs& a, cudaStream_t stream);
 // per CTA that waits on a barrier phase nothing arms (the wait runs out).
 int gemv_ring_set_wait_test(unsigned long long limit_ns, int stall);
 int gemv_tile_set_wait_test(unsigned long long limit_ns, int stall);
+int gemv_imma_set_wait_test(unsigned long long limit_ns, int stall);
+// Integer-tensor-core GEMV (M <= 8, K % 1024 == 0): 16-column tiles, K split
+// over a cluster of cluster_k CTAs, tiles_per_cta tiles and kparts warps per
+// tile in each CTA.  16-byte aligned x, packed and scales.
+struct GemvImmaArgs {
+    CUtensorMap tmap_w;      // packed uint32 [N][K/8], box 32 words x (16 tiles_per_cta), 128B swizzle
+    CUtensorMap tmap_s;      // scales fp32 [N][K/32], box 32 x (16 tiles_per_cta), 128B swizzle
+    const float* x;          // [M][K]
+    float* y;                // [M][N]
+    int M, N, K;
+    int cluster_k;           // S
+    int clusters;            // cluster c holds tiles [c*tiles_total/clusters, (c+1)*tiles_total/clusters)
+    int tiles_total;         // ceil(N / 16)
+    int tiles_per_cta;       // T = ceil(tiles_total / clusters)
+    int kparts;              // P
+    const float* lora_t;     // [M][rank] or nullptr
+    const float* lora_b;     // [rank][N] or nullptr
+    int rank;
+    float lora_scale;
+    int* status;
+};
+bool gemv_imma_geometry(int sm_count, int M, int N, int K, int* S, int* clusters, int* T, int* P);
+size_t gemv_imma_smem_bytes(int M, int K, int S, int T, int P);
+int launch_gemv_imma(const GemvImmaArgs& a, cudaStream_t stream);
 // Tensor-core decode (M <= 8): col_blocks blocks of <= 128 columns, each a
 // cluster of cluster_k CTAs splitting K into slices of <= 1024.
 struct DecodeArgs {
@@ -206,6 +230,26 @@ int launch_lora_backward(const LoraBackwardArgs& a, cudaStream_t stream);
 int launch_sgd(float* p, const float* g, float lr, long long count, cudaStream_t stream);
 int launch_adamw(float* p, const float* g, float* m1, float* m2, float lr, float beta1, float beta2, float eps,
                  float wd, int step, long long count, cudaStream_t stream);
+// fp32 GEMM on tcgen05 with 3xTF32 (sgemm_tc.cu).  The operands are first
+// split into TF32 hi / lo planes in K-major layout ([rows][ld] fp32, K
+// contiguous, ld % 4 == 0): launch_split_planes writes the planes of a
+// row-major [rows][cols] matrix (transpose = false: planes [rows][ld]) or of
+// its transpose (transpose = true: planes [cols][ld]); columns past the
+// source's up to ld are zero.
+int launch_split_planes(const float* src, int rows, int cols, long long ld_src, bool transpose, float* hi, float* lo,
+                        long long ld_out, cudaStream_t stream);
+struct SgemmTcArgs {
+    CUtensorMap tm_ahi, tm_alo;  // A planes [M][ld] fp32, box 32 x 128, 128B swizzle
+    CUtensorMap tm_bhi, tm_blo;  // B^T planes [N][ld] fp32, box 32 x bn, 128B swizzle
+    float* c;                    // C[M][N], row pitch ldc floats: C = alpha * A B
+    int M, N, K;
+    long long ldc;
+    float alpha;
+    int bn;                      // tile columns: sgemm_tc_bn(N)
+    int* status;
+};
+int sgemm_tc_bn(int N);
+int launch_sgemm_tc(const SgemmTcArgs& a, cudaStream_t stream);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream);

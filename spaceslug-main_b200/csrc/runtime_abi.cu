@@ -6,10 +6,8 @@
 // Error behaviour mirrors vulkan-runtime/src/api/lora_delta_api.cpp:42-85:
 // arguments are checked first (return 1), every device failure returns 2, and
 // nothing throws across the ABI (catch (...) -> 2).
-#include <cublas_v2.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
-#include <dlfcn.h>
 
 #include <algorithm>
 #include <array>
@@ -33,7 +31,7 @@ namespace {
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_operand{static_cast<int>(q4::Operand16::kF16)};
-std::atomic<int> g_decode_variant{0};  // 0 auto, 1 ring GEMV, 2 tensor-core decode, 3 whole-tile GEMV
+std::atomic<int> g_decode_variant{0};  // 0 auto, 1 ring GEMV, 2 tcgen05 decode, 3 whole-tile GEMV, 4 IMMA GEMV
 std::atomic<int> g_gemm_variant{0};  // 0 auto, 1 single-CTA 128-row tiles, 2 CTA pair, 3 single-CTA 256-row tiles
 std::once_flag g_operand_env_once;
 
@@ -70,8 +68,6 @@ struct DeviceCtx {
     size_t hbuf_bytes = 0;
     int max_pairs[2] = {-1, -1};    // co-resident CTA pairs of the pair GEMM, per operand type
     std::mutex pair_mu;
-    cublasHandle_t blas = nullptr;  // spaceslug_sgemm (created on first use)
-    std::mutex blas_mu;
 };
 
 constexpr int kMaxDevices = 64;
@@ -140,8 +136,8 @@ std::atomic<int>& decode_variant_init() {
     static std::once_flag once;
     std::call_once(once, [] {
         const char* e = std::getenv("SPACESLUG_Q4_DECODE");
-        const char* names[4] = {"auto", "gemv", "mma", "tile"};
-        for (int i = 0; e && i < 4; ++i)
+        const char* names[5] = {"auto", "gemv", "mma", "tile", "imma"};
+        for (int i = 0; e && i < 5; ++i)
             if (std::strcmp(e, names[i]) == 0) g_decode_variant.store(i);
     });
     return g_decode_variant;
@@ -154,45 +150,6 @@ q4::Operand16 operand_type() {
         if (e && std::strcmp(e, "f16") == 0) g_operand.store(static_cast<int>(q4::Operand16::kF16));
     });
     return static_cast<q4::Operand16>(g_operand.load());
-}
-
-// cuBLAS for the plain fp32 GEMM (spaceslug_sgemm), loaded on first use so the
-// library has no link-time dependency on it.
-struct BlasApi {
-    decltype(&cublasCreate_v2) create = nullptr;
-    decltype(&cublasSetStream_v2) set_stream = nullptr;
-    decltype(&cublasSetMathMode) set_math = nullptr;
-    decltype(&cublasSgemm_v2) sgemm = nullptr;
-};
-const BlasApi& blas_api() {
-    static BlasApi api;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_LOCAL);
-        if (!h) return;
-        api.create = reinterpret_cast<decltype(api.create)>(dlsym(h, "cublasCreate_v2"));
-        api.set_stream = reinterpret_cast<decltype(api.set_stream)>(dlsym(h, "cublasSetStream_v2"));
-        api.set_math = reinterpret_cast<decltype(api.set_math)>(dlsym(h, "cublasSetMathMode"));
-        api.sgemm = reinterpret_cast<decltype(api.sgemm)>(dlsym(h, "cublasSgemm_v2"));
-    });
-    if (!api.create || !api.set_stream || !api.set_math || !api.sgemm) throw CudaError("libcublas.so.12 is unavailable");
-    return api;
-}
-
-// C[m x n] = A[m x k] B[k x n], fp32 row-major, on `stream`: the column-major
-// product C^T = B^T A^T, fp32 FMA (no TF32).
-void run_sgemm(DeviceCtx& c, const float* a, const float* b, float* cm, int m, int n, int k, cudaStream_t stream) {
-    const BlasApi& api = blas_api();
-    std::lock_guard<std::mutex> lk(c.blas_mu);
-    if (!c.blas) {
-        if (api.create(&c.blas) != CUBLAS_STATUS_SUCCESS) throw CudaError("cublasCreate failed");
-        api.set_math(c.blas, CUBLAS_DEFAULT_MATH);
-    }
-    if (api.set_stream(c.blas, stream) != CUBLAS_STATUS_SUCCESS) throw CudaError("cublasSetStream failed");
-    const float one = 1.0f, zero = 0.0f;
-    if (api.sgemm(c.blas, CUBLAS_OP_N, CUBLAS_OP_N, n, m, k, &one, b, n, a, k, &zero, cm, n) != CUBLAS_STATUS_SUCCESS)
-        throw CudaError("cublasSgemm failed");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 // Stream-ordered scratch buffer released on the same stream at scope exit.
@@ -226,6 +183,14 @@ const char* shape_error(const void* x, const void* packed, const void* scales, c
 }
 
 // --------------------------------------------------------------- dispatch --
+// Tensor maps of a weight handle's decode launches (integer-MMA GEMV), encoded
+// once per geometry instead of once per call.
+struct DecodeMapCache {
+    std::mutex mu;
+    int S = 0, T = 0;  // geometry the maps were encoded for (0: none yet)
+    CUtensorMap w{}, s{};
+};
+
 struct Problem {
     const float* x;
     const uint32_t* packed;
@@ -241,6 +206,7 @@ struct Problem {
     int sm_budget = 0;   // SMs the GEMM may occupy (0: all)
     const q4::PeerPtrs* peers = nullptr;  // Y also stored to these peers' Y (same offsets and pitch)
     int npeers = 0;
+    DecodeMapCache* maps = nullptr;       // a weight handle's cached decode tensor maps, or nullptr
 };
 
 // GEMV launch geometry.  K is split over a cluster of S CTAs (S | G, slice
@@ -322,6 +288,45 @@ void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
     if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
 }
 
+// fp32 GEMM C[m x n] (row pitch ldc) = alpha * op(A) op(B) on the tcgen05
+// tensor cores (3xTF32, sgemm_tc.cu).  op(A) is [m x k]: A row-major [m][k]
+// with row pitch lda, or with trans_a A given as [k][m]; op(B) is [k x n]: B
+// row-major [k][n] with row pitch ldb, or with trans_b B given as [n][k].  The
+// operands' TF32 hi / lo planes live in stream-ordered scratch.
+void run_sgemm(const float* a, long long lda, bool trans_a, const float* b, long long ldb, bool trans_b, float* cm,
+               long long ldc, int m, int n, int k, float alpha, int* status, cudaStream_t stream) {
+    const long long ldk = (static_cast<long long>(k) + 3) / 4 * 4;  // plane row pitch: 16-byte rows
+    Scratch pa(static_cast<size_t>(2 * m * ldk) * sizeof(float), stream);
+    Scratch pb(static_cast<size_t>(2 * n * ldk) * sizeof(float), stream);
+    float* ahi = static_cast<float*>(pa.p);
+    float* alo = ahi + static_cast<size_t>(m) * ldk;
+    float* bhi = static_cast<float*>(pb.p);
+    float* blo = bhi + static_cast<size_t>(n) * ldk;
+    if (trans_a)
+        check_launch(q4::launch_split_planes(a, k, m, lda, true, ahi, alo, ldk, stream), "split A");
+    else
+        check_launch(q4::launch_split_planes(a, m, k, lda, false, ahi, alo, ldk, stream), "split A");
+    if (trans_b)
+        check_launch(q4::launch_split_planes(b, n, k, ldb, false, bhi, blo, ldk, stream), "split B");
+    else
+        check_launch(q4::launch_split_planes(b, k, n, ldb, true, bhi, blo, ldk, stream), "split B");
+    q4::SgemmTcArgs g{};
+    g.bn = q4::sgemm_tc_bn(n);
+    const uint64_t rb = static_cast<uint64_t>(ldk) * 4;
+    encode_2d(&g.tm_ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ahi, k, m, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tm_alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, alo, k, m, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tm_bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, bhi, k, n, rb, 32, static_cast<uint32_t>(g.bn),
+              CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tm_blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, blo, k, n, rb, 32, static_cast<uint32_t>(g.bn),
+              CU_TENSOR_MAP_SWIZZLE_128B);
+    g.c = cm;
+    g.M = m; g.N = n; g.K = k;
+    g.ldc = ldc;
+    g.alpha = alpha;
+    g.status = status;
+    check_launch(q4::launch_sgemm_tc(g, stream), "sgemm (tcgen05) launch");
+}
+
 // Co-resident CTA pairs of the pair kernel for operand type `op` (cached).
 int pair_capacity(DeviceCtx& c, q4::Operand16 op) {
     std::lock_guard<std::mutex> lk(c.pair_mu);
@@ -398,10 +403,45 @@ void run_problem(const Problem& p, cudaStream_t stream) {
                      "lora_xa");
     const float lscale = p.rank > 0 ? p.alpha / static_cast<float>(p.rank) : 0.0f;
 
-    // Decode (M <= 8).  Automatic choice: the whole-tile GEMV where the shape
-    // allows it, else the streamed-ring GEMV; the tensor-core decode only on
+    // Decode (M <= 8).  Automatic choice: the integer-tensor-core GEMV where
+    // the shape allows it (K % 1024 == 0, 16-byte aligned operands), else the
+    // whole-tile GEMV, else the streamed-ring GEMV; the tcgen05 decode only on
     // request.
     const int dv = decode_variant_init().load();
+    if (p.M <= 8 && (dv == 0 || dv == 4) && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
+        q4::GemvImmaArgs a{};
+        if (q4::gemv_imma_geometry(c.sm_count, p.M, p.N, p.K, &a.cluster_k, &a.clusters, &a.tiles_per_cta,
+                                   &a.kparts)) {
+            const int K = p.K, N = p.N;
+            const uint32_t rows = static_cast<uint32_t>(16 * a.tiles_per_cta);
+            auto encode = [&](CUtensorMap* mw, CUtensorMap* ms) {
+                encode_2d(mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(K) / 8,
+                          static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, 32, rows, CU_TENSOR_MAP_SWIZZLE_128B);
+                encode_2d(ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.scales, static_cast<uint64_t>(K) / 32,
+                          static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 8, 32, rows, CU_TENSOR_MAP_SWIZZLE_128B);
+            };
+            if (p.maps != nullptr) {
+                std::lock_guard<std::mutex> lk(p.maps->mu);
+                if (p.maps->S != a.cluster_k || p.maps->T != a.tiles_per_cta) {
+                    encode(&p.maps->w, &p.maps->s);
+                    p.maps->S = a.cluster_k;
+                    p.maps->T = a.tiles_per_cta;
+                }
+                a.tmap_w = p.maps->w;
+                a.tmap_s = p.maps->s;
+            } else {
+                encode(&a.tmap_w, &a.tmap_s);
+            }
+            a.x = p.x;
+            a.y = p.y;
+            a.M = p.M; a.N = N; a.K = K;
+            a.tiles_total = (N + 15) / 16;
+            a.lora_t = lora_t; a.lora_b = p.rank > 0 ? p.lora_b : nullptr; a.rank = p.rank; a.lora_scale = lscale;
+            a.status = c.status;
+            check_launch(q4::launch_gemv_imma(a, stream), "gemv imma launch");
+            return;
+        }
+    }
     if (p.M <= 8 && (dv == 0 || dv == 3)) {
         const int S = tile_split(p.M, p.K);
         if (S > 0 && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
@@ -489,9 +529,18 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     Scratch cexp(f16 && p.col_exp == nullptr ? static_cast<size_t>(p.N) * sizeof(int) : 0, stream);
     int* row_exp = static_cast<int*>(rexp.p);
     const int* col_exp = f16 ? (p.col_exp ? p.col_exp : static_cast<int*>(cexp.p)) : nullptr;
-    check_launch(q4::launch_cast_x(p.x, x16.p, row_exp, p.M, p.K, op, stream), "cast_x");
+    // Launches that do not need the cast go first, so that the cast is the
+    // GEMM's direct predecessor and the GEMM's prologue (weights, dequant)
+    // overlaps it through programmatic dependent launch: the per-column
+    // exponents of a stateless call, and the pair kernel's fp32 T = X A (its
+    // epilogue adds (alpha/r) T B).
     if (f16 && p.col_exp == nullptr)
         check_launch(q4::launch_col_exp(p.scales, static_cast<int*>(cexp.p), p.N, p.K, stream), "col_exp");
+    if (p.rank > 0 && use_pair)
+        check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
+                                        static_cast<float*>(t_part.p)),
+                     "lora_xa");
+    check_launch(q4::launch_cast_x(p.x, x16.p, row_exp, p.M, p.K, op, stream), "cast_x");
 
     q4::GemmArgs g{};
     g.ksplit = ksplit;
@@ -523,10 +572,7 @@ void run_problem(const Problem& p, cudaStream_t stream) {
     const int lstages = use_pair ? 0 : (p.rank + 15) / 16;
     Scratch t_op(lstages > 0 ? static_cast<size_t>(p.M) * lstages * 64 * 2 : 0, stream);
     if (p.rank > 0 && use_pair) {
-        // T = X * A in fp32: the pair kernel's epilogue adds (alpha/r) T B
-        check_launch(q4::launch_lora_xa(p.x, p.lora_a, lora_t, p.M, p.K, p.rank, stream,
-                                        static_cast<float*>(t_part.p)),
-                     "lora_xa");
+        // T = X * A in fp32 (launched before the cast, above)
         g.tmap_t = g.tmap_x16;  // never read
         g.lora_t = lora_t;
         g.lora_stages = 0;
@@ -664,6 +710,7 @@ struct spaceslug_q4_weights {
     int rank = 0;
     float alpha = 0.0f;
     int sm_budget = 0;  // SMs a GEMM launch of this handle may occupy (0: all)
+    DecodeMapCache decode_maps;  // tensor maps of its decode launches
     // training state (allocated on first use, reset by set_lora)
     float* lora_da = nullptr;
     float* lora_db = nullptr;
@@ -1059,6 +1106,7 @@ int spaceslug_q4_weights_run(spaceslug_q4_weights* w, const float* x, float* y, 
         Problem p{x, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, y,
                   static_cast<int>(m), w->N, w->K};
         p.sm_budget = w->sm_budget;
+        p.maps = &w->decode_maps;
         run_problem(p, static_cast<cudaStream_t>(stream));
         return SPACESLUG_OK;
     });
@@ -1245,6 +1293,7 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
         Problem p{dx, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, dy,
                   static_cast<int>(m), w->N, w->K};
         p.sm_budget = w->sm_budget;
+        p.maps = &w->decode_maps;
         run_problem(p, c.stream);
         if (ymap)
             check_launch(q4::launch_copy_words(dy, ymap, static_cast<long long>(m) * w->N, c.status, c.status_host_dev,
@@ -1443,7 +1492,7 @@ int spaceslug_q4_set_operand_type(int type) {
 }
 
 int spaceslug_q4_set_decode_variant(int variant) {
-    if (variant < 0 || variant > 3) return -1;
+    if (variant < 0 || variant > 4) return -1;
     return decode_variant_init().exchange(variant);
 }
 
@@ -1479,6 +1528,7 @@ int spaceslug_q4_debug_wait_test(uint64_t wait_limit_ns, int stall) {
         check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // no launch in flight sees a half-set hook
         check(static_cast<cudaError_t>(q4::gemv_tile_set_wait_test(lim, st)), "set the tile GEMV test hook");
         check(static_cast<cudaError_t>(q4::gemv_ring_set_wait_test(lim, st)), "set the ring GEMV test hook");
+        check(static_cast<cudaError_t>(q4::gemv_imma_set_wait_test(lim, st)), "set the IMMA GEMV test hook");
         return SPACESLUG_OK;
     });
 }
@@ -1500,10 +1550,10 @@ int spaceslug_sgemm(const float* a, const float* b, float* c, uint32_t m, uint32
         Scratch da(ab, ctx.stream), db(bb, ctx.stream), dc(cb, ctx.stream);
         q4up::staged_h2d(current_device(), da.p, a, ab, ctx.stream);
         q4up::staged_h2d(current_device(), db.p, b, bb, ctx.stream);
-        run_sgemm(ctx, static_cast<float*>(da.p), static_cast<float*>(db.p), static_cast<float*>(dc.p),
-                  static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), ctx.stream);
+        run_sgemm(static_cast<float*>(da.p), k, false, static_cast<float*>(db.p), n, false, static_cast<float*>(dc.p),
+                  n, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), 1.0f, ctx.status, ctx.stream);
         d2h(c, dc.p, cb, ctx.stream);
-        check(cudaStreamSynchronize(ctx.stream), "cudaStreamSynchronize");
+        if (take_status(ctx, ctx.stream)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
         *max_relative_error = 0.0f;  // the reference reports 0 as well (sgemm_api.cpp:54)
         return SPACESLUG_OK;
     });
@@ -1514,8 +1564,8 @@ int spaceslug_sgemm_device(const float* a, const float* b, float* c, uint32_t m,
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return fail(SPACESLUG_INVALID_ARGUMENT, "dimension too large");
     return guarded([&] {
         DeviceCtx& ctx = ctx_for(current_device());
-        run_sgemm(ctx, a, b, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
-                  static_cast<cudaStream_t>(stream));
+        run_sgemm(a, k, false, b, n, false, c, n, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), 1.0f,
+                  ctx.status, static_cast<cudaStream_t>(stream));
         return SPACESLUG_OK;
     });
 }

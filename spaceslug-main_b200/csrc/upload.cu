@@ -5,6 +5,7 @@
 // the DMA engine drains slot i), and the packing itself can run on the device
 // from the logical int8 matrix, which then only has to cross PCIe as bytes.
 #include <cuda_runtime.h>
+#include <sched.h>
 
 #include <algorithm>
 #include <array>
@@ -31,10 +32,19 @@ void ck(cudaError_t e, const char* what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Host threads for the staging copies and the packer: the CPUs this process
+// may run on (its affinity mask, which a container's CPU set narrows; not the
+// machine's core count), at most 16.
 int copy_threads() {
-    const unsigned hc = std::thread::hardware_concurrency();
-    const int t = hc ? static_cast<int>(hc / 2) : 4;
-    return std::max(1, std::min(8, t));
+    static const int n = [] {
+        cpu_set_t set;
+        CPU_ZERO(&set);
+        int c = 0;
+        if (sched_getaffinity(0, sizeof(set), &set) == 0) c = CPU_COUNT(&set);
+        if (c <= 0) c = static_cast<int>(std::thread::hardware_concurrency());
+        return std::max(1, std::min(16, c));
+    }();
+    return n;
 }
 
 // Runs f(i) for i in [0, parts) on up to `parts` threads (the caller's among them).

@@ -311,11 +311,67 @@ def choose_exchange(world: int) -> dict:
     return dict(EXCHANGE_BY_WORLD[max(p for p in EXCHANGE_BY_WORLD if p <= world)])
 
 
-def make_sharded(session, handle, m: int, n_total: int, dist, device, group=None, **override):
-    """The N-sharded GEMM with the exchange choose_exchange picks for this
-    world size (keyword arguments override it).  Returns a ShardedGemmPush;
-    its run(x, stream) returns the full Y on every rank."""
-    ch = choose_exchange(dist.get_world_size(group))
+CANDIDATES = (
+    {"engine": "epilogue", "bands": 1, "push_sms": 16},
+    {"engine": "sm", "bands": 4, "push_sms": 16},
+    {"engine": "sm", "bands": 4, "push_sms": 24},
+    {"engine": "sm", "bands": 8, "push_sms": 32},
+)
+_tuned: dict = {}
+
+
+def autotune_exchange(session, handle, m: int, n_total: int, dist, device, x, stream=None, group=None,
+                      candidates=CANDIDATES, reps: int = 3) -> dict:
+    """Times each candidate exchange on this problem with every rank and returns
+    the fastest (step time = max over ranks, mean of `reps` calls after one
+    warm-up; ties go to the earlier candidate).  Every rank measures the same
+    candidates in the same order and sees the same maxima, so every rank picks
+    the same one.  The choice is cached per (world, m, n_total, k); the
+    timings are in the returned dict under "tuning_ms"."""
+    import torch
+    world = dist.get_world_size(group)
+    key = (world, m, n_total, handle.k)
+    if key in _tuned:
+        return dict(_tuned[key])
+    dev = torch.device(device)
+    s0 = stream or torch.cuda.current_stream(dev)
+    times = []
+    for cand in candidates:
+        ex = ShardedGemmPush(session, handle, m, n_total, dist, dev, bands=cand["bands"], group=group,
+                             engine=cand["engine"], push_sms=cand["push_sms"])
+        try:
+            ex.run(x, s0)
+            evs = []
+            with torch.cuda.stream(s0):
+                for _ in range(reps):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(s0)
+                    ex.run(x, s0)
+                    b.record(s0)
+                    evs.append((a, b))
+            s0.synchronize()
+            t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / reps], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            times.append(float(t.item()))
+        finally:
+            ex.close()
+    best = min(range(len(candidates)), key=lambda i: (times[i], i))
+    out = dict(candidates[best])
+    out["tuning_ms"] = {f"{c['engine']}_b{c['bands']}_s{c['push_sms']}": round(t, 4) for c, t in zip(candidates, times)}
+    _tuned[key] = out
+    return dict(out)
+
+
+def make_sharded(session, handle, m: int, n_total: int, dist, device, group=None, tune_x=None, stream=None,
+                 **override):
+    """The N-sharded GEMM with the exchange for this world size: measured on
+    the caller's X when tune_x is given (autotune_exchange), else the table
+    choose_exchange; keyword arguments override either.  Returns a
+    ShardedGemmPush; its run(x, stream) returns the full Y on every rank."""
+    if tune_x is not None:
+        ch = autotune_exchange(session, handle, m, n_total, dist, device, tune_x, stream=stream, group=group)
+    else:
+        ch = choose_exchange(dist.get_world_size(group))
     ch.update(override)
     if ch["engine"] == "none":
         raise ValueError("one rank needs no exchange: run the handle directly")

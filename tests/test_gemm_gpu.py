@@ -44,11 +44,11 @@ def test_gemm_config1_against_reference_output(session, cuda, golden, operand):
     y = session.q4gemm(t["x"], t["packed"], t["scales"], 256)
     _check(y, t["y_ref"], t["x"], t["scales"], 64, NORM_TOL[operand], ABS_FACTOR[operand])
     # the reference's own elementwise criterion (test_q4gemm.cpp:376-390,
-    # rel 1e-3 vs max(1, |ref|)) was set for its fp32 GEMM; 16-bit operands
-    # meet it only at the reference test's own data (next test), so here it
-    # is reported, with a bound that follows from the operand precision.
+    # |y - ref| / max(1, |ref|)) at the north_star's 2e-3 for the f16 path:
+    # one f16 rounding of x and one of w = v * s (1.87e-3 expected); bf16
+    # operands (8 bits) are held to their own measured level.
     rel = parity.compare_float_arrays(y, t["y_ref"], tolerance=1e-3)["max_relative_error"]
-    assert rel <= (4e-3 if operand == "f16" else 3e-2), rel
+    assert rel <= (parity.GEMM_NORM_REL_TOL if operand == "f16" else 3e-2), rel
 
 
 def test_gemm_reference_known_answer_case(session, oracle, cuda, golden):

@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 TOL = parity.GEMV_REL_TOL
 
 
-@pytest.fixture(params=["tile", "mma", "gemv"])
+@pytest.fixture(params=["imma", "tile", "mma", "gemv"])
 def decode_variant(request, session):
     prev = session.set_decode_variant(request.param)
     yield request.param
@@ -104,3 +104,57 @@ def test_gemv_resident_weights_and_shards(session, oracle, cuda, decode_weights)
         with session.weights(packed, scales, 4096, 4096, r * 1024, (r + 1) * 1024) as h:
             parts.append(h.run_host(x))
     assert np.array_equal(np.concatenate(parts, axis=1), y)
+
+
+# Shapes for the integer-tensor-core GEMV's geometry: K split over 1, 2 or 4
+# CTAs of a cluster, 1 to 7 tiles of 16 columns per CTA, ragged last tiles.
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (3, 4096, 2048), (8, 512, 1024), (5, 100, 4096),
+                                   (2, 1700, 3072), (7, 11008, 4096), (6, 4001, 8192), (4, 16, 1024)])
+def test_gemv_imma_geometries(session, oracle, cuda, m, n, k):
+    prev = session.set_decode_variant("imma")
+    try:
+        w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=3 * n + k)
+        x = synth.make_x(m, k, seed=m + 40)
+        y = session.q4gemm(x, packed, scales, n)
+    finally:
+        session.set_decode_variant(prev)
+    rep = parity.compare_float_arrays(y, oracle.gemm(x, w_kn, scales), tolerance=TOL)
+    assert rep["status"] == "pass", (m, n, k, rep)
+
+
+def test_gemv_imma_magnitudes_and_zero_rows(session, oracle, cuda):
+    # rows of very different scales (each row and K slice gets its own power
+    # of two), an all-zero row, and tiny group scales
+    m, n, k = 6, 640, 4096
+    w_kn, packed, scales = synth.make_weights(k, n, 1e-6, 4e-6, seed=77)
+    x = synth.make_x(m, k, seed=78)
+    x[0] *= np.float32(1e6)
+    x[1] *= np.float32(1e-6)
+    x[2] = 0.0
+    x[3, :1024] *= np.float32(1e4)  # one K slice far larger than the others
+    prev = session.set_decode_variant("imma")
+    try:
+        y = session.q4gemm(x, packed, scales, n)
+    finally:
+        session.set_decode_variant(prev)
+    ref = oracle.gemm(x, w_kn, scales)
+    assert np.all(y[2] == 0.0)
+    for r in range(m):  # relative to each row's own magnitude
+        rel = np.max(np.abs(y[r] - ref[r])) / max(np.max(np.abs(ref[r])), 1e-300)
+        assert rel <= TOL, (r, rel)
+
+
+def test_gemv_imma_non_finite_row(session, cuda):
+    m, n, k = 3, 256, 1024
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=5)
+    x = synth.make_x(m, k, seed=6)
+    x_ok = x.copy()
+    x[1, 17] = np.inf
+    prev = session.set_decode_variant("imma")
+    try:
+        y = session.q4gemm(x, packed, scales, n)
+        y_ok = session.q4gemm(x_ok, packed, scales, n)
+    finally:
+        session.set_decode_variant(prev)
+    assert np.all(np.isnan(y[1]))  # a row holding inf or NaN gives NaN outputs
+    assert np.array_equal(y[[0, 2]], y_ok[[0, 2]])

@@ -1,6 +1,8 @@
 """GPU: spaceslug_sgemm, the reference's fp32 GEMM ABI
 (vulkan-runtime/src/api/sgemm_api.h:5-9), at its own test case
-(tests/test_sgemm.cpp: 256^3, LCG inputs, |gpu - ref| <= 1e-3 * max(1, |ref|))."""
+(tests/test_sgemm.cpp: 256^3, LCG inputs, |gpu - ref| <= 1e-3 * max(1, |ref|)),
+computed on the tcgen05 tensor cores with three TF32 products per term
+(hi*hi + hi*lo + lo*hi), checked against an fp64 product at 1e-4."""
 from __future__ import annotations
 
 import ctypes
@@ -25,7 +27,8 @@ def test_reference_case(session, cuda):
     _check(session.sgemm(a, b), a, b)
 
 
-@pytest.mark.parametrize("m,n,k", [(64, 64, 32), (128, 192, 96), (1024, 1024, 1024), (64, 4096, 512)])
+@pytest.mark.parametrize("m,n,k", [(64, 64, 32), (128, 192, 96), (1024, 1024, 1024), (64, 4096, 512),
+                                   (2048, 2048, 2048), (256, 64, 8192)])
 def test_shapes(session, cuda, m, n, k):
     rng = np.random.default_rng(m + n + k)
     a = rng.standard_normal((m, k)).astype(np.float32)
@@ -54,3 +57,30 @@ def test_reports_zero_error_like_the_reference(session, cuda):
     f = lambda x: x.ctypes.data_as(ctypes.POINTER(ctypes.c_float))  # noqa: E731
     assert session.raw("spaceslug_sgemm")(f(a), f(b), f(c), 64, 64, 32, ctypes.byref(err)) == 0
     assert err.value == 0.0 and np.all(c == 32.0)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (37, 51, 37), (130, 17, 5), (300, 129, 1000), (5, 2000, 64)])
+def test_device_entry_ragged(session, cuda, m, n, k):
+    # tiles of 128 rows x 16/32/64/128 columns, ragged in every dimension, K not a multiple of 4
+    import torch
+    rng = np.random.default_rng(m * n + k)
+    a = (rng.standard_normal((m, k)) * 3).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    da, db = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    dc = torch.full((m, n), float("nan"), device=cuda)
+    session.sgemm_device(da.data_ptr(), db.data_ptr(), dc.data_ptr(), m, n, k,
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    _check(dc.cpu().numpy(), a, b, 1e-4)
+    assert session.device_status(0) == 0
+
+
+def test_accuracy_is_fp32_level(session, cuda):
+    # 3xTF32 keeps about 22 bits of every operand: normwise error near fp32
+    # GEMM rounding (single-pass TF32 would be ~1e-3 relative)
+    rng = np.random.default_rng(9)
+    a = rng.standard_normal((512, 1024)).astype(np.float32)
+    b = rng.standard_normal((1024, 512)).astype(np.float32)
+    c = session.sgemm(a, b)
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    assert np.linalg.norm(c - ref) / np.linalg.norm(ref) < 1e-5

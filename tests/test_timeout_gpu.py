@@ -32,7 +32,7 @@ def stall(session, cuda):
     session.device_status(0)  # leave no code behind for later tests
 
 
-@pytest.fixture(params=["tile", "gemv"])
+@pytest.fixture(params=["imma", "tile", "gemv"])
 def decode_kernel(request, session):
     prev = session.set_decode_variant(request.param)
     yield request.param
