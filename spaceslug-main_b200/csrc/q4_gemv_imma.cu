@@ -41,6 +41,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "q4_dequant.cuh"
@@ -54,7 +55,7 @@ namespace {
 
 constexpr int kIBoxK = 256;        // k per weight box: one 128-byte row (32 words) per column
 constexpr int kIScaleBoxG = 32;    // scale groups per scale box: one 128-byte row per column
-constexpr int kIMaxWarps = 16;
+constexpr int kIMaxWarps = 14;   // 448 threads: two CTAs per SM at up to 72 registers
 constexpr int kIMaxTiles = 7;      // 16-column tiles per CTA (shared-memory budget)
 constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23
 constexpr int kMagicBits = 0x4B400000;
@@ -65,9 +66,9 @@ constexpr int kMagicBits = 0x4B400000;
 static __device__ int g_imma_stall_test = 0;
 
 struct ImmaLayout {
-    int ks, gs, nbox, nsbox, rows, slots;
-    int w_off, s_off, l_off, red_off, bar_off, misc_off, bytes;
-    int part_off, cpart_off;  // alias the weight region once every warp is done with it
+    int ks, gs, nbox, nsbox, rows, slots, rps;
+    int w_off, s_off, l_off, recv_off, red_off, bar_off, misc_off, bytes;
+    int part_off;  // aliases the weight region once every warp is done with it
 };
 
 __host__ __device__ inline int imma_nb(int M) { return (3 * M + 7) / 8; }
@@ -79,34 +80,23 @@ __host__ __device__ inline ImmaLayout imma_layout(int M, int K, int S, int T, in
     L.nbox = L.ks / kIBoxK;
     L.nsbox = L.gs / kIScaleBoxG;
     L.rows = 16 * T;
+    L.rps = (L.rows + S - 1) / S;  // columns each CTA of the cluster stores
     L.slots = 8 * imma_nb(M);
     L.w_off = 0;
     const int w_bytes = L.nbox * L.rows * 128;
     const int part_bytes = P * T * L.slots * 16 * 4;
-    const int cpart_bytes = M * L.rows * 4;
     L.part_off = 0;
-    L.cpart_off = (part_bytes + 127) / 128 * 128;
-    const int region = w_bytes > L.cpart_off + cpart_bytes ? w_bytes : L.cpart_off + cpart_bytes;
+    const int region = w_bytes > part_bytes ? w_bytes : part_bytes;
     L.s_off = (region + 1023) / 1024 * 1024;                   // 128B-swizzled boxes: 1024-aligned
     L.l_off = L.s_off + L.nsbox * L.rows * 128;                // limb rows [slots][ks] bytes
-    L.red_off = L.l_off + L.slots * L.ks;                      // row maxima [warps][8] u32, exps [8], bad [8]
-    L.bar_off = L.red_off + (kIMaxWarps * 8 + 16) * 4;
-    L.misc_off = L.bar_off + (L.nbox + L.nsbox) * 8;           // abort flag
+    L.recv_off = L.l_off + L.slots * L.ks;                     // [S][M][rps] fp32: the cluster's K-slice sums
+    L.red_off = L.recv_off + S * M * L.rps * 4;                // row maxima [warps][8] u32, exps [8], bad [8]
+    L.bar_off = (L.red_off + (kIMaxWarps * 8 + 16) * 4 + 7) / 8 * 8;
+    L.misc_off = L.bar_off + (L.nbox + L.nsbox + 1) * 8;       // abort flag
     L.bytes = L.misc_off + 16;
     return L;
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ float ldsf(uint32_t addr) { return __uint_as_float(lds32(addr)); }
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-    return v;
-}
 __device__ __forceinline__ void sts64(uint32_t addr, uint32_t a, uint32_t b) {
     asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
 }
@@ -122,12 +112,45 @@ __device__ __forceinline__ uint64_t policy_first() {
 }
 
 // D = A * B + D, int8 x int8 -> int32, m16n8k32 (A row-major, B column-major).
+// Not volatile: a pure function of its operands, which the compiler may
+// schedule (several groups' MMAs in flight at once).
 __device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                            uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// fp32 store into the shared memory of a CTA of the cluster (address from mapa).
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Arrive, with release semantics at cluster scope, on an mbarrier of a CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Bounded wait, with acquire semantics at cluster scope, for phase `parity` of a local mbarrier.
+__device__ __forceinline__ bool mbar_wait_acquire_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                          int* status, int code) {
+    const unsigned long long t0 = globaltimer_ns();
+    const unsigned long long limit = *static_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+#pragma unroll 1
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer_ns() - t0 > limit) {
+            *abort_flag = 1;
+            if (status) atomicCAS(status, 0, code);
+            return false;
+        }
+    }
 }
 
 // Four bytes b0..b3 (byte 0 of each argument) into one word.
@@ -166,6 +189,7 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
     const uint32_t bar = base + L.bar_off;
     auto wfull = [&](int b) { return bar + 8u * b; };
     auto sfull = [&](int b) { return bar + 8u * (L.nbox + b); };
+    const uint32_t recv_full = bar + 8u * (L.nbox + L.nsbox);  // one arrival per CTA of the cluster
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off);
     uint32_t* red = reinterpret_cast<uint32_t*>(smem + L.red_off);  // [kIMaxWarps][8] row-max bits
     int* rexp = reinterpret_cast<int*>(red + kIMaxWarps * 8);        // [8] row exponents
@@ -173,6 +197,7 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
 
     if (tid == 0) {
         for (int b = 0; b < L.nbox + L.nsbox; ++b) mbar_init(bar + 8u * b, 1);
+        mbar_init(recv_full, static_cast<uint32_t>(S));
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -192,23 +217,33 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         }
     }
     pdl_launch_dependents();  // the next launch's CTAs may start streaming their weights
-    pdl_wait();               // X, T and Y may belong to the previous launch until here
+    // every CTA's receive barrier is initialised before any peer arrives on it
+    // (this overlaps the previous launch: it comes before griddepcontrol.wait)
+    if (S > 1) cluster_sync_all();
+    pdl_wait();  // X, T and Y may belong to the previous launch until here
 
     // ---------------------------------------------- X slice -> int8 limbs --
-    // Chunk ch = (row m, 8 consecutive k of the slice).  Pass 1: row maxima.
+    // Chunk ch = (row m, 8 consecutive k of the slice).  A thread's first
+    // kXRegChunks chunks stay in registers between the two passes.
+    constexpr int kXRegChunks = 3;
     const int cpr = L.ks / 8;  // chunks per row
     const int nch = M * cpr;
+    float4 xr[kXRegChunks][2];
     {
         float mx[8];
 #pragma unroll
         for (int m = 0; m < 8; ++m) mx[m] = 0.0f;
-        for (int ch = tid; ch < nch; ch += nthreads) {
+#pragma unroll 1
+        for (int i = 0, ch = tid; ch < nch; ++i, ch += nthreads) {
             const int m = ch / cpr, c = ch - m * cpr;
             const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k0 + 8 * c);
             const float4 a = src[0], b = src[1];
-            // fmaxf drops NaN: a non-finite row is flagged through the sum below
+#pragma unroll
+            for (int j = 0; j < kXRegChunks; ++j)
+                if (i == j) xr[j][0] = a, xr[j][1] = b;
             float cm = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
                              fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+            // fmaxf drops NaN: a non-finite row is flagged through the sum
             const float sum = a.x + a.y + a.z + a.w + b.x + b.y + b.z + b.w;
             if (!isfinite(sum) || !isfinite(cm)) cm = __int_as_float(0x7f800000);  // +inf marks the row
 #pragma unroll
@@ -217,12 +252,13 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         }
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
+            if (m >= M) break;
             const uint32_t r = __reduce_max_sync(0xffffffffu, __float_as_uint(mx[m]));  // |x| >= 0: bits order as floats
             if (lane == 0) red[warp * 8 + m] = r;
         }
     }
     __syncthreads();
-    if (tid < 8) {
+    if (tid < M) {
         uint32_t r = 0;
         for (int w = 0; w < W; ++w) r = max(r, red[w * 8 + tid]);
         const float v = __uint_as_float(r);
@@ -239,28 +275,36 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         rbad[tid] = bad;
     }
     __syncthreads();
-    // Pass 2: convert.  Limb j of row m is slot s = j * M + m: row s of the
-    // limb area, KS bytes; group gg's 32 bytes sit at 32-byte chunk
-    // gg ^ (s & 7), and inside it, 8 bytes per word q of the group: the four
-    // even k (8q, 8q+2, 8q+4, 8q+6) and then the four odd k, the order the
-    // weight registers use.
+    // Limb j of row m is slot s = j * M + m: row s of the limb area, KS bytes;
+    // group gg's 32 bytes sit at 32-byte chunk gg ^ (s & 7), and inside it,
+    // 8 bytes per word q of the group: the four even k (8q, 8q+2, 8q+4, 8q+6)
+    // and then the four odd k, the order the weight registers use.
     const uint32_t lbase = base + L.l_off;
-    for (int ch = tid; ch < nch; ch += nthreads) {
+#pragma unroll 1
+    for (int i = 0, ch = tid; ch < nch; ++i, ch += nthreads) {
         const int m = ch / cpr, c = ch - m * cpr;
-        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k0 + 8 * c);
-        const float4 a = src[0], b = src[1];
+        float4 a, b;
+        if (i < kXRegChunks) {
+#pragma unroll
+            for (int j = 0; j < kXRegChunks; ++j)
+                if (i == j) a = xr[j][0], b = xr[j][1];
+        } else {
+            const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k0 + 8 * c);
+            a = src[0];
+            b = src[1];
+        }
         const float sc = exp2i(rexp[m]);
         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         uint32_t r0[8], r1[8], r2[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int e = 0; e < 8; ++e) {
             // round x * 2^e to an integer R (|R| <= 2^22) by the magic-number add
-            const int R = __float_as_int(__fmaf_rn(v[i], sc, kMagic)) - kMagicBits;
+            const int R = __float_as_int(__fmaf_rn(v[e], sc, kMagic)) - kMagicBits;
             const int R1 = (R + 128) >> 8;   // R = 256 R1 + l,  l in [-128, 127]
             const int R2 = (R1 + 128) >> 8;  // R1 = 256 R2 + m
-            r0[i] = static_cast<uint32_t>(R2);  // high limb (|R2| <= 64)
-            r1[i] = static_cast<uint32_t>(R1);  // byte 0 = middle limb
-            r2[i] = static_cast<uint32_t>(R);   // byte 0 = low limb
+            r0[e] = static_cast<uint32_t>(R2);  // high limb (|R2| <= 64)
+            r1[e] = static_cast<uint32_t>(R1);  // byte 0 = middle limb
+            r2[e] = static_cast<uint32_t>(R);   // byte 0 = low limb
         }
         const int gg = c >> 2, q = c & 3;
         const uint32_t* limbs[3] = {r0, r1, r2};
@@ -291,41 +335,62 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         ok = mbar_wait(wfull(0), 0u, abort_flag, status, kStatusTimeoutGemv) &&
              mbar_wait(wfull(0), 1u, abort_flag, status, kStatusTimeoutGemv) && ok;
     const int gbeg = part * L.gs / P, gend = (part + 1) * L.gs / P;
+    // this warp's weight and scale boxes, all before the loop (which then has
+    // no waits, so its loads and MMAs can be scheduled freely)
+    if (ok && gend > gbeg) {
+        for (int b = gbeg >> 3; b <= (gend - 1) >> 3 && ok; ++b)
+            ok = mbar_wait(wfull(b), 0u, abort_flag, status, kStatusTimeoutGemv);
+        for (int b = gbeg / kIScaleBoxG; b <= (gend - 1) / kIScaleBoxG && ok; ++b)
+            ok = mbar_wait(sfull(b), 0u, abort_flag, status, kStatusTimeoutGemv);
+    }
     const uint32_t ra = static_cast<uint32_t>(tl * 16 + g);  // weight rows (columns) g and g + 8 of the tile
-    const uint32_t wrow_a = base + L.w_off + ra * 128 + q * 4;
-    const uint32_t srow_a = base + L.s_off + ra * 128;
+    const uint8_t* wrow = smem + L.w_off + ra * 128 + q * 4;
+    const uint8_t* srow = smem + L.s_off + ra * 128;
+    const uint8_t* lrow = smem + L.l_off + q * 8;
     const uint32_t sw = static_cast<uint32_t>(g & 7);        // swizzle key of rows ra and ra + 8
-    int have_box = -1, have_sbox = -1;
-#pragma unroll 2
-    for (int gg = gbeg; gg < gend && ok; ++gg) {
-        const int b = gg >> 3, sb = gg / kIScaleBoxG;
-        if (b != have_box) {
-            if (!mbar_wait(wfull(b), 0u, abort_flag, status, kStatusTimeoutGemv)) { ok = false; break; }
-            have_box = b;
-        }
-        if (sb != have_sbox) {
-            if (!mbar_wait(sfull(sb), 0u, abort_flag, status, kStatusTimeoutGemv)) { ok = false; break; }
-            have_sbox = sb;
-        }
-        const uint32_t wchunk = ((static_cast<uint32_t>(gg & 7) ^ sw) << 4);
-        const uint32_t wa = lds32(wrow_a + b * L.rows * 128 + wchunk);
-        const uint32_t wb = lds32(wrow_a + b * L.rows * 128 + 8 * 128 + wchunk);
-        const uint32_t soff = sb * L.rows * 128 + ((static_cast<uint32_t>((gg & 31) >> 2) ^ sw) << 4) + (gg & 3) * 4;
-        const float sa = ldsf(srow_a + soff);
-        const float sbv = ldsf(srow_a + 8 * 128 + soff);
-        // 16 v as signed bytes: even nibbles moved up, odd nibbles in place
-        const uint32_t a0 = (wa << 4) & 0xF0F0F0F0u, a2 = wa & 0xF0F0F0F0u;
-        const uint32_t a1 = (wb << 4) & 0xF0F0F0F0u, a3 = wb & 0xF0F0F0F0u;
+    constexpr int kBatch = 4;                                // groups whose MMAs are in flight together
+    if (ok) {
+#pragma unroll 1
+        for (int gb = gbeg; gb < gend; gb += kBatch) {
+            uint32_t a0[kBatch], a1[kBatch], a2[kBatch], a3[kBatch];
+            float sa[kBatch], sbv[kBatch];
+            uint2 bv[kBatch][NB];
 #pragma unroll
-        for (int t = 0; t < NB; ++t) {
-            const int s = t * 8 + g;  // limb slot of this thread's B fragment (s & 7 == g)
-            const uint2 bv = lds64(lbase + s * L.ks + ((static_cast<uint32_t>(gg) ^ sw) << 5) + q * 8);
-            int d[4] = {kMagicBits, kMagicBits, kMagicBits, kMagicBits};
-            imma_16832(d, a0, a1, a2, a3, bv.x, bv.y);
-            acc[t][0] = fmaf(sa, __int_as_float(d[0]) - kMagic, acc[t][0]);
-            acc[t][1] = fmaf(sa, __int_as_float(d[1]) - kMagic, acc[t][1]);
-            acc[t][2] = fmaf(sbv, __int_as_float(d[2]) - kMagic, acc[t][2]);
-            acc[t][3] = fmaf(sbv, __int_as_float(d[3]) - kMagic, acc[t][3]);
+            for (int u = 0; u < kBatch; ++u) {
+                const int gg = min(gb + u, gend - 1);  // past the end: a repeated group, its result unused
+                const int b = gg >> 3, sb = gg / kIScaleBoxG;
+                const uint32_t wchunk = ((static_cast<uint32_t>(gg & 7) ^ sw) << 4);
+                const uint32_t wa = *reinterpret_cast<const uint32_t*>(wrow + b * L.rows * 128 + wchunk);
+                const uint32_t wb = *reinterpret_cast<const uint32_t*>(wrow + b * L.rows * 128 + 8 * 128 + wchunk);
+                const uint32_t soff =
+                    sb * L.rows * 128 + ((static_cast<uint32_t>((gg & 31) >> 2) ^ sw) << 4) + (gg & 3) * 4;
+                sa[u] = *reinterpret_cast<const float*>(srow + soff);
+                sbv[u] = *reinterpret_cast<const float*>(srow + 8 * 128 + soff);
+                // 16 v as signed bytes: even nibbles moved up, odd nibbles in place
+                a0[u] = (wa << 4) & 0xF0F0F0F0u;
+                a2[u] = wa & 0xF0F0F0F0u;
+                a1[u] = (wb << 4) & 0xF0F0F0F0u;
+                a3[u] = wb & 0xF0F0F0F0u;
+#pragma unroll
+                for (int t = 0; t < NB; ++t) {
+                    const int s = t * 8 + g;  // limb slot of this thread's B fragment (s & 7 == g)
+                    bv[u][t] = *reinterpret_cast<const uint2*>(lrow + s * L.ks + ((static_cast<uint32_t>(gg) ^ sw) << 5));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                const bool live = gb + u < gend;
+#pragma unroll
+                for (int t = 0; t < NB; ++t) {
+                    int d[4] = {kMagicBits, kMagicBits, kMagicBits, kMagicBits};
+                    imma_16832(d, a0[u], a1[u], a2[u], a3[u], bv[u][t].x, bv[u][t].y);
+                    const float fa = live ? sa[u] : 0.0f, fb = live ? sbv[u] : 0.0f;
+                    acc[t][0] = fmaf(fa, __int_as_float(d[0]) - kMagic, acc[t][0]);
+                    acc[t][1] = fmaf(fa, __int_as_float(d[1]) - kMagic, acc[t][1]);
+                    acc[t][2] = fmaf(fb, __int_as_float(d[2]) - kMagic, acc[t][2]);
+                    acc[t][3] = fmaf(fb, __int_as_float(d[3]) - kMagic, acc[t][3]);
+                }
+            }
         }
     }
 
@@ -344,7 +409,9 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
             }
     }
     __syncthreads();
-    float* cpart = reinterpret_cast<float*>(smem + L.cpart_off);  // [M][rows]: this K slice's sums
+    // This K slice's sum of column r of row m goes to CTA r % S of the
+    // cluster (the one that stores it): receive slot [crank][m][r / S].
+    const uint32_t recv_local = base + L.recv_off;
     for (int idx = tid; idx < M * L.rows; idx += nthreads) {
         const int m = idx / L.rows, r = idx - m * L.rows;
         const int tt = r >> 4, c = r & 15;
@@ -357,24 +424,30 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         }
         // y = (65536 h + 256 m + l) / 16 * 2^-e  (the weights entered as 16 v)
         const float v = fmaf(limb[0], 65536.0f, fmaf(limb[1], 256.0f, limb[2]));
-        cpart[idx] = rbad[m] ? __int_as_float(0x7fc00000) : v * exp2i(-rexp[m] - 4);
-    }
-    if (S > 1) {
-        cluster_sync_all();
-    } else {
-        __syncthreads();
-    }
-    cg::cluster_group cluster = cg::this_cluster();
-    // CTA crank stores columns r = crank, crank + S, ... of the cluster's block
-    for (int idx = tid; idx < M * L.rows; idx += nthreads) {
-        const int m = idx / L.rows, r = idx - m * L.rows;
-        if (r % S != crank || r >= ncols) continue;
-        float sum = 0.0f;
-        if (S > 1) {
-            for (int qq = 0; qq < S; ++qq) sum += cluster.map_shared_rank(cpart, qq)[idx];
+        const float val = rbad[m] ? __int_as_float(0x7fc00000) : v * exp2i(-rexp[m] - 4);
+        const int owner = r % S;
+        const uint32_t slot = recv_local + static_cast<uint32_t>(((crank * M + m) * L.rps + r / S) * 4);
+        if (owner == crank) {
+            *reinterpret_cast<float*>(smem + (slot - base)) = val;
         } else {
-            sum = cpart[idx];
+            st_cluster_f32(mapa_shared(slot, static_cast<uint32_t>(owner)), val);
         }
+    }
+    if (S > 1) asm volatile("fence.acq_rel.cluster;" ::: "memory");  // this thread's remote stores before the arrives
+    __syncthreads();
+    if (tid == 0) {
+        for (int o = 0; o < S; ++o)
+            mbar_arrive_release_cluster(S > 1 ? mapa_shared(recv_full, static_cast<uint32_t>(o)) : recv_full);
+    }
+    // every CTA of the cluster has delivered its slice's sums for this CTA's columns
+    mbar_wait_acquire_cluster(recv_full, 0u, abort_flag, status, kStatusTimeoutGemv);
+    const float* recv = reinterpret_cast<const float*>(smem + L.recv_off);
+    for (int idx = tid; idx < M * L.rps; idx += nthreads) {
+        const int m = idx / L.rps, rr = idx - m * L.rps;
+        const int r = rr * S + crank;
+        if (r >= ncols) continue;
+        float sum = 0.0f;
+        for (int j = 0; j < S; ++j) sum += recv[(j * M + m) * L.rps + rr];  // fixed order: deterministic
         const int n = n0 + r;
         if (lora_b != nullptr) {
             float dl = 0.0f;
@@ -383,7 +456,6 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         }
         y[static_cast<size_t>(m) * N + n] = sum;
     }
-    if (S > 1) cluster_sync_all();  // peers may still read this CTA's partial sums
 
     if (tid == 0 && *abort_flag) {
         // copies already issued land before the CTA's shared memory is released
@@ -436,7 +508,7 @@ size_t gemv_imma_smem_bytes(int M, int K, int S, int T, int P) {
 // Geometry: K split over a cluster of S CTAs (slices of whole 1024-k scale
 // boxes), N in 16-column tiles, T tiles per CTA (at most 7, and at most what
 // keeps the CTA within ~110 KB of shared memory so two share an SM), P =
-// floor(16 / T) parts of each slice's groups per tile (one warp each).  With
+// floor(14 / T) parts of each slice's groups per tile (one warp each).  With
 // at most one CTA per SM the clusters share the tiles evenly; a matrix whose
 // tiles do not fit one CTA per SM takes more clusters, in waves.  S (and the
 // cluster count) minimise waves * T * K / S, the work of the busiest SM, ties
@@ -444,11 +516,17 @@ size_t gemv_imma_smem_bytes(int M, int K, int S, int T, int P) {
 bool gemv_imma_geometry(int sm_count, int M, int N, int K, int* S_out, int* clusters_out, int* T_out, int* P_out) {
     if (M < 1 || M > 8 || N < 1 || K <= 0 || K % 1024 != 0 || sm_count < 1) return false;
     constexpr size_t kSmemCap = 110 * 1024;
+    // SPACESLUG_Q4_IMMA_SPLIT=1|2|4 forces the K split (when the shape allows it)
+    static const int forced = [] {
+        const char* e = std::getenv("SPACESLUG_Q4_IMMA_SPLIT");
+        const int v = e ? std::atoi(e) : 0;
+        return (v == 1 || v == 2 || v == 4) ? v : 0;
+    }();
     const int tiles = (N + 15) / 16;
     long long best = -1;
     int bS = 0, bC = 0, bT = 0;
     for (int S = 1; S <= 4; S *= 2) {
-        if (K % (1024 * S) != 0) continue;
+        if (K % (1024 * S) != 0 || (forced != 0 && S != forced)) continue;
         int tfit = 0;
         for (int T = 1; T <= kIMaxTiles; ++T)
             if (gemv_imma_smem_bytes(M, K, S, T, kIMaxWarps / T) <= kSmemCap) tfit = T;

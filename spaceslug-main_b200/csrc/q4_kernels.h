@@ -231,16 +231,16 @@ int launch_sgd(float* p, const float* g, float lr, long long count, cudaStream_t
 int launch_adamw(float* p, const float* g, float* m1, float* m2, float lr, float beta1, float beta2, float eps,
                  float wd, int step, long long count, cudaStream_t stream);
 // fp32 GEMM on tcgen05 with 3xTF32 (sgemm_tc.cu).  The operands are first
-// split into TF32 hi / lo planes in K-major layout ([rows][ld] fp32, K
-// contiguous, ld % 4 == 0): launch_split_planes writes the planes of a
-// row-major [rows][cols] matrix (transpose = false: planes [rows][ld]) or of
-// its transpose (transpose = true: planes [cols][ld]); columns past the
-// source's up to ld are zero.
+// split into TF32 hi / lo planes in K-major layout ([out_rows][ld] fp32, K
+// contiguous): launch_split_planes writes the planes of a row-major
+// [rows][cols] matrix (transpose = false: plane row i = source row i) or of
+// its transpose (transpose = true: plane row i = source column i); rows and
+// columns past the source's, up to out_rows and ld, are zero.
 int launch_split_planes(const float* src, int rows, int cols, long long ld_src, bool transpose, float* hi, float* lo,
-                        long long ld_out, cudaStream_t stream);
+                        int out_rows, long long ld_out, cudaStream_t stream);
 struct SgemmTcArgs {
-    CUtensorMap tm_ahi, tm_alo;  // A planes [M][ld] fp32, box 32 x 128, 128B swizzle
-    CUtensorMap tm_bhi, tm_blo;  // B^T planes [N][ld] fp32, box 32 x bn, 128B swizzle
+    CUtensorMap tm_ahi, tm_alo;  // A planes [M rounded up to 128][ld] fp32 (ld % 32 == 0), box 32 x 128, 128B swizzle
+    CUtensorMap tm_bhi, tm_blo;  // B^T planes [N rounded up to bn][ld] fp32, box 32 x bn, 128B swizzle
     float* c;                    // C[M][N], row pitch ldc floats: C = alpha * A B
     int M, N, K;
     long long ldc;

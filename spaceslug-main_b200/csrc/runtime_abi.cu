@@ -295,29 +295,34 @@ void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
 // operands' TF32 hi / lo planes live in stream-ordered scratch.
 void run_sgemm(const float* a, long long lda, bool trans_a, const float* b, long long ldb, bool trans_b, float* cm,
                long long ldc, int m, int n, int k, float alpha, int* status, cudaStream_t stream) {
-    const long long ldk = (static_cast<long long>(k) + 3) / 4 * 4;  // plane row pitch: 16-byte rows
-    Scratch pa(static_cast<size_t>(2 * m * ldk) * sizeof(float), stream);
-    Scratch pb(static_cast<size_t>(2 * n * ldk) * sizeof(float), stream);
+    // Planes padded to whole TMA boxes (zeros): k to a multiple of 32, the rows
+    // to whole 128-row (A) and bn-row (B) tiles, so every box lies inside its plane.
+    const int bn = q4::sgemm_tc_bn(n);
+    const long long ldk = (static_cast<long long>(k) + 31) / 32 * 32;
+    const int mr = (m + 127) / 128 * 128, nr = (n + bn - 1) / bn * bn;
+    Scratch pa(static_cast<size_t>(2) * mr * ldk * sizeof(float), stream);
+    Scratch pb(static_cast<size_t>(2) * nr * ldk * sizeof(float), stream);
     float* ahi = static_cast<float*>(pa.p);
-    float* alo = ahi + static_cast<size_t>(m) * ldk;
+    float* alo = ahi + static_cast<size_t>(mr) * ldk;
     float* bhi = static_cast<float*>(pb.p);
-    float* blo = bhi + static_cast<size_t>(n) * ldk;
+    float* blo = bhi + static_cast<size_t>(nr) * ldk;
     if (trans_a)
-        check_launch(q4::launch_split_planes(a, k, m, lda, true, ahi, alo, ldk, stream), "split A");
+        check_launch(q4::launch_split_planes(a, k, m, lda, true, ahi, alo, mr, ldk, stream), "split A");
     else
-        check_launch(q4::launch_split_planes(a, m, k, lda, false, ahi, alo, ldk, stream), "split A");
+        check_launch(q4::launch_split_planes(a, m, k, lda, false, ahi, alo, mr, ldk, stream), "split A");
     if (trans_b)
-        check_launch(q4::launch_split_planes(b, n, k, ldb, false, bhi, blo, ldk, stream), "split B");
+        check_launch(q4::launch_split_planes(b, n, k, ldb, false, bhi, blo, nr, ldk, stream), "split B");
     else
-        check_launch(q4::launch_split_planes(b, k, n, ldb, true, bhi, blo, ldk, stream), "split B");
+        check_launch(q4::launch_split_planes(b, k, n, ldb, true, bhi, blo, nr, ldk, stream), "split B");
     q4::SgemmTcArgs g{};
-    g.bn = q4::sgemm_tc_bn(n);
+    g.bn = bn;
     const uint64_t rb = static_cast<uint64_t>(ldk) * 4;
-    encode_2d(&g.tm_ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ahi, k, m, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_2d(&g.tm_alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, alo, k, m, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_2d(&g.tm_bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, bhi, k, n, rb, 32, static_cast<uint32_t>(g.bn),
+    const uint64_t kk = static_cast<uint64_t>(ldk);
+    encode_2d(&g.tm_ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ahi, kk, mr, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tm_alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, alo, kk, mr, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tm_bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, bhi, kk, nr, rb, 32, static_cast<uint32_t>(bn),
               CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_2d(&g.tm_blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, blo, k, n, rb, 32, static_cast<uint32_t>(g.bn),
+    encode_2d(&g.tm_blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, blo, kk, nr, rb, 32, static_cast<uint32_t>(bn),
               CU_TENSOR_MAP_SWIZZLE_128B);
     g.c = cm;
     g.M = m; g.N = n; g.K = k;

@@ -355,11 +355,21 @@ def autotune_exchange(session, handle, m: int, n_total: int, dist, device, x, st
             times.append(float(t.item()))
         finally:
             ex.close()
-    best = min(range(len(candidates)), key=lambda i: (times[i], i))
-    out = dict(candidates[best])
-    out["tuning_ms"] = {f"{c['engine']}_b{c['bands']}_s{c['push_sms']}": round(t, 4) for c, t in zip(candidates, times)}
+    out = pick_fastest(candidates, times)
     _tuned[key] = out
     return dict(out)
+
+
+def pick_fastest(candidates, times) -> dict:
+    """The candidate with the smallest time (ties to the earlier one), with
+    every candidate's time under "tuning_ms"."""
+    if len(candidates) != len(times) or not candidates:
+        raise ValueError("one time per candidate")
+    best = min(range(len(candidates)), key=lambda i: (times[i], i))
+    out = dict(candidates[best])
+    out["tuning_ms"] = {f"{c['engine']}_b{c['bands']}_s{c['push_sms']}": round(float(t), 4)
+                        for c, t in zip(candidates, times)}
+    return out
 
 
 def make_sharded(session, handle, m: int, n_total: int, dist, device, group=None, tune_x=None, stream=None,

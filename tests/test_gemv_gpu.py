@@ -98,12 +98,14 @@ def test_gemv_resident_weights_and_shards(session, oracle, cuda, decode_weights)
     finally:
         full.close()
     assert parity.compare_float_arrays(y, ref, tolerance=TOL)["status"] == "pass"
-    # four column shards reproduce the full result exactly
+    # four column shards reproduce the full result (to fp32 summation order:
+    # the integer-MMA GEMV splits K differently for 1024 and 4096 columns)
     parts = []
     for r in range(4):
         with session.weights(packed, scales, 4096, 4096, r * 1024, (r + 1) * 1024) as h:
             parts.append(h.run_host(x))
-    assert np.array_equal(np.concatenate(parts, axis=1), y)
+    rep = parity.compare_float_arrays(np.concatenate(parts, axis=1), y, tolerance=1e-5)
+    assert rep["status"] == "pass", rep
 
 
 # Shapes for the integer-tensor-core GEMV's geometry: K split over 1, 2 or 4

@@ -86,3 +86,15 @@ def test_plan_bands_cover_rows_in_tile_multiples():
             assert all(a[1] == c[0] for a, c in zip(bands, bands[1:]))
             assert all(r0 % 256 == 0 for r0, _ in bands)
             assert len(bands) == 1 or all(r1 - r0 >= 256 for r0, r1 in bands)
+
+
+def test_exchange_table_and_pick_fastest(pkg):
+    from spaceslug_b200 import sharding
+    assert sharding.choose_exchange(1)["engine"] == "none"
+    assert sharding.choose_exchange(2)["engine"] == "epilogue"
+    assert sharding.choose_exchange(3) == sharding.choose_exchange(2)  # nearest listed size below
+    assert sharding.choose_exchange(16) == sharding.choose_exchange(8)
+    cands = sharding.CANDIDATES
+    best = sharding.pick_fastest(cands, [0.9, 0.7, 0.7, 0.8])
+    assert {k: best[k] for k in ("engine", "bands", "push_sms")} == cands[1]  # tie -> earlier candidate
+    assert len(best["tuning_ms"]) == len(cands)
