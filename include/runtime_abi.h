@@ -194,8 +194,9 @@ int spaceslug_q4_set_operand_type(int type);
  * invalid value. */
 int spaceslug_q4_set_gemm_variant(int variant);
 
-/* Decode (M <= 8) kernel selection: 0 = automatic (default), 1 = CUDA-core
- * GEMV with a streamed shared-memory ring, 2 = tcgen05 tensor-core decode,
+/* Decode (M <= 8) kernel selection: 0 = automatic (default: the whole-tile
+ * GEMV where the shape allows it, else the streamed ring), 1 = CUDA-core GEMV
+ * with a streamed shared-memory ring, 2 = tcgen05 tensor-core decode,
  * 3 = CUDA-core GEMV with the whole tile resident, 4 = integer-tensor-core
  * (mma.sync s8) GEMV with exact int8 limbs of X (K % 1024 == 0).  A variant the shape does not allow falls
  * back to the automatic choice.  Results agree to fp32 summation order.

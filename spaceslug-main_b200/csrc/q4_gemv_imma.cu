@@ -88,11 +88,12 @@ __host__ __device__ inline ImmaLayout imma_layout(int M, int K, int S, int T, in
     L.part_off = 0;
     const int region = w_bytes > part_bytes ? w_bytes : part_bytes;
     L.s_off = (region + 1023) / 1024 * 1024;                   // 128B-swizzled boxes: 1024-aligned
-    L.l_off = L.s_off + L.nsbox * L.rows * 128;                // limb rows [slots][ks] bytes
-    L.recv_off = L.l_off + L.slots * L.ks;                     // [S][M][rps] fp32: the cluster's K-slice sums
+    L.l_off = L.s_off + L.nsbox * L.rows * 128;                // X slice [M][ks] fp32 by TMA, then (in place)
+    const int xl = M * L.ks * 4 > L.slots * L.ks ? M * L.ks * 4 : L.slots * L.ks;  // the limb rows [slots][ks]
+    L.recv_off = L.l_off + xl;                                 // [S][M][rps] fp32: the cluster's K-slice sums
     L.red_off = L.recv_off + S * M * L.rps * 4;                // row maxima [warps][8] u32, exps [8], bad [8]
     L.bar_off = (L.red_off + (kIMaxWarps * 8 + 16) * 4 + 7) / 8 * 8;
-    L.misc_off = L.bar_off + (L.nbox + L.nsbox + 1) * 8;       // abort flag
+    L.misc_off = L.bar_off + (L.nbox + L.nsbox + 2) * 8;       // abort flag
     L.bytes = L.misc_off + 16;
     return L;
 }
@@ -161,7 +162,8 @@ __device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_
 template <int NB>
 __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
     q4_gemv_imma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
-                        const float* __restrict__ x, float* __restrict__ y, int M, int N, int K, int T, int P,
+                        const __grid_constant__ CUtensorMap tmap_x, float* __restrict__ y, int M, int N, int K, int T,
+                        int P,
                         int tiles_total, int clusters, const float* __restrict__ lora_t,
                         const float* __restrict__ lora_b, int rank, float lora_scale, int* __restrict__ status) {
     extern __shared__ uint8_t smem_raw[];
@@ -190,6 +192,7 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
     auto wfull = [&](int b) { return bar + 8u * b; };
     auto sfull = [&](int b) { return bar + 8u * (L.nbox + b); };
     const uint32_t recv_full = bar + 8u * (L.nbox + L.nsbox);  // one arrival per CTA of the cluster
+    const uint32_t xfull = bar + 8u * (L.nbox + L.nsbox + 1);  // the X slice
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off);
     uint32_t* red = reinterpret_cast<uint32_t*>(smem + L.red_off);  // [kIMaxWarps][8] row-max bits
     int* rexp = reinterpret_cast<int*>(red + kIMaxWarps * 8);        // [8] row exponents
@@ -198,6 +201,7 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
     if (tid == 0) {
         for (int b = 0; b < L.nbox + L.nsbox; ++b) mbar_init(bar + 8u * b, 1);
         mbar_init(recv_full, static_cast<uint32_t>(S));
+        mbar_init(xfull, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -206,6 +210,7 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
         // weights and scales do not depend on the previous launch
         tma_prefetch_desc(&tmap_w);
         tma_prefetch_desc(&tmap_s);
+        tma_prefetch_desc(&tmap_x);
         const uint64_t pol = policy_first();
         for (int b = 0; b < L.nsbox; ++b) {
             mbar_arrive_expect_tx(sfull(b), static_cast<uint32_t>(L.rows * 128));
@@ -221,34 +226,46 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
     // (this overlaps the previous launch: it comes before griddepcontrol.wait)
     if (S > 1) cluster_sync_all();
     pdl_wait();  // X, T and Y may belong to the previous launch until here
+    if (tid == 0) {
+        // this CTA's K slice of X: rows 0..M-1, boxes of 256 k
+        mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(M * L.ks * 4));
+        for (int b = 0; b < L.ks / kIBoxK; ++b) tma_load_2d(base + L.l_off + b * kIBoxK * 4 * M, &tmap_x, xfull, k0 + b * kIBoxK, 0);
+    }
 
     // ---------------------------------------------- X slice -> int8 limbs --
-    // Chunk ch = (row m, 8 consecutive k of the slice).  A thread's first
-    // kXRegChunks chunks stay in registers between the two passes.
+    // The slice arrives as boxes [ks/256][M][256] fp32.  Chunk ch = (row m,
+    // 8 consecutive k); a thread holds all its chunks in registers (the
+    // geometry keeps them at <= kXRegChunks), so after the barrier below the
+    // limbs can overwrite the slice in place.
     constexpr int kXRegChunks = 3;
     const int cpr = L.ks / 8;  // chunks per row
     const int nch = M * cpr;
     float4 xr[kXRegChunks][2];
+    bool ok = mbar_wait(xfull, 0u, abort_flag, status, kStatusTimeoutGemv);
     {
         float mx[8];
 #pragma unroll
         for (int m = 0; m < 8; ++m) mx[m] = 0.0f;
-#pragma unroll 1
-        for (int i = 0, ch = tid; ch < nch; ++i, ch += nthreads) {
-            const int m = ch / cpr, c = ch - m * cpr;
-            const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k0 + 8 * c);
-            const float4 a = src[0], b = src[1];
 #pragma unroll
-            for (int j = 0; j < kXRegChunks; ++j)
-                if (i == j) xr[j][0] = a, xr[j][1] = b;
-            float cm = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
-                             fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
-            // fmaxf drops NaN: a non-finite row is flagged through the sum
-            const float sum = a.x + a.y + a.z + a.w + b.x + b.y + b.z + b.w;
-            if (!isfinite(sum) || !isfinite(cm)) cm = __int_as_float(0x7f800000);  // +inf marks the row
+        for (int i = 0; i < kXRegChunks; ++i) {
+            const int ch = tid + i * nthreads;
+            if (ch < nch) {
+                const int m = ch / cpr, c = ch - m * cpr;
+                // k = 8c of row m: box c / 32, row m, element 8 (c % 32)
+                const float4* src =
+                    reinterpret_cast<const float4*>(smem + L.l_off + (((c >> 5) * M + m) * kIBoxK + 8 * (c & 31)) * 4);
+                const float4 a = src[0], b = src[1];
+                xr[i][0] = a;
+                xr[i][1] = b;
+                float cm = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
+                                 fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+                // fmaxf drops NaN: a non-finite row is flagged through the sum
+                const float sum = a.x + a.y + a.z + a.w + b.x + b.y + b.z + b.w;
+                if (!isfinite(sum) || !isfinite(cm)) cm = __int_as_float(0x7f800000);  // +inf marks the row
 #pragma unroll
-            for (int mm = 0; mm < 8; ++mm)
-                if (mm == m) mx[mm] = fmaxf(mx[mm], cm);
+                for (int mm = 0; mm < 8; ++mm)
+                    if (mm == m) mx[mm] = fmaxf(mx[mm], cm);
+            }
         }
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
@@ -280,19 +297,12 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
     // 8 bytes per word q of the group: the four even k (8q, 8q+2, 8q+4, 8q+6)
     // and then the four odd k, the order the weight registers use.
     const uint32_t lbase = base + L.l_off;
-#pragma unroll 1
-    for (int i = 0, ch = tid; ch < nch; ++i, ch += nthreads) {
-        const int m = ch / cpr, c = ch - m * cpr;
-        float4 a, b;
-        if (i < kXRegChunks) {
 #pragma unroll
-            for (int j = 0; j < kXRegChunks; ++j)
-                if (i == j) a = xr[j][0], b = xr[j][1];
-        } else {
-            const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k0 + 8 * c);
-            a = src[0];
-            b = src[1];
-        }
+    for (int i = 0; i < kXRegChunks; ++i) {
+        const int ch = tid + i * nthreads;
+        if (ch >= nch) break;
+        const int m = ch / cpr, c = ch - m * cpr;
+        const float4 a = xr[i][0], b = xr[i][1];
         const float sc = exp2i(rexp[m]);
         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         uint32_t r0[8], r1[8], r2[8];
@@ -330,7 +340,7 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
 #pragma unroll
     for (int t = 0; t < NB; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
     const int tl = warp % T, part = warp / T;
-    bool ok = part < P;
+    ok = ok && part < P;
     if (stall_test)  // phase 0 of box 0's barrier completes; phase 1 is never armed
         ok = mbar_wait(wfull(0), 0u, abort_flag, status, kStatusTimeoutGemv) &&
              mbar_wait(wfull(0), 1u, abort_flag, status, kStatusTimeoutGemv) && ok;
@@ -433,9 +443,9 @@ __global__ void __launch_bounds__(kIMaxWarps * 32, 2)
             st_cluster_f32(mapa_shared(slot, static_cast<uint32_t>(owner)), val);
         }
     }
-    if (S > 1) asm volatile("fence.acq_rel.cluster;" ::: "memory");  // this thread's remote stores before the arrives
-    __syncthreads();
+    __syncthreads();  // every thread's stores of its sums are ordered before thread 0's release below
     if (tid == 0) {
+        if (S > 1) asm volatile("fence.acq_rel.cluster;" ::: "memory");
         for (int o = 0; o < S; ++o)
             mbar_arrive_release_cluster(S > 1 ? mapa_shared(recv_full, static_cast<uint32_t>(o)) : recv_full);
     }
@@ -488,7 +498,7 @@ int launch_imma_nb(const GemvImmaArgs& a, cudaStream_t stream) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    e = cudaLaunchKernelEx(&cfg, kern, a.tmap_w, a.tmap_s, a.x, a.y, a.M, a.N, a.K, a.tiles_per_cta, a.kparts,
+    e = cudaLaunchKernelEx(&cfg, kern, a.tmap_w, a.tmap_s, a.tmap_x, a.y, a.M, a.N, a.K, a.tiles_per_cta, a.kparts,
                            a.tiles_total, a.clusters, a.lora_t, a.lora_b, a.rank, a.lora_scale, a.status);
     return static_cast<int>(e);
 }
@@ -527,9 +537,12 @@ bool gemv_imma_geometry(int sm_count, int M, int N, int K, int* S_out, int* clus
     int bS = 0, bC = 0, bT = 0;
     for (int S = 1; S <= 4; S *= 2) {
         if (K % (1024 * S) != 0 || (forced != 0 && S != forced)) continue;
+        // each thread holds all its chunks of the X slice (<= 3) in registers
         int tfit = 0;
         for (int T = 1; T <= kIMaxTiles; ++T)
-            if (gemv_imma_smem_bytes(M, K, S, T, kIMaxWarps / T) <= kSmemCap) tfit = T;
+            if (gemv_imma_smem_bytes(M, K, S, T, kIMaxWarps / T) <= kSmemCap &&
+                static_cast<long long>(M) * (K / S) / 8 <= 3LL * 32 * T * (kIMaxWarps / T))
+                tfit = T;
         if (tfit == 0) continue;
         int C = sm_count / S;
         if (C < 1) C = 1;
@@ -557,6 +570,9 @@ bool gemv_imma_geometry(int sm_count, int M, int N, int K, int* S_out, int* clus
 }
 
 int launch_gemv_imma(const GemvImmaArgs& a, cudaStream_t stream) {
+    if (static_cast<long long>(a.M) * (a.K / (a.cluster_k > 0 ? a.cluster_k : 1)) / 8 >
+            3LL * 32 * a.tiles_per_cta * a.kparts)
+        return static_cast<int>(cudaErrorInvalidValue);  // X slice chunks must fit the threads' registers
     if (a.M < 1 || a.M > 8 || a.K % (1024 * a.cluster_k) != 0 || a.tiles_per_cta < 1 ||
         a.tiles_per_cta > kIMaxTiles || a.kparts < 1 || a.tiles_per_cta * a.kparts > kIMaxWarps ||
         a.clusters < 1 || static_cast<long long>(a.clusters) * a.tiles_per_cta < a.tiles_total)

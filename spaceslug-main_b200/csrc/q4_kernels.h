@@ -41,7 +41,7 @@ int gemv_imma_set_wait_test(unsigned long long limit_ns, int stall);
 struct GemvImmaArgs {
     CUtensorMap tmap_w;      // packed uint32 [N][K/8], box 32 words x (16 tiles_per_cta), 128B swizzle
     CUtensorMap tmap_s;      // scales fp32 [N][K/32], box 32 x (16 tiles_per_cta), 128B swizzle
-    const float* x;          // [M][K]
+    CUtensorMap tmap_x;      // X fp32 [M][K], box 256 x M, no swizzle
     float* y;                // [M][N]
     int M, N, K;
     int cluster_k;           // S

@@ -408,12 +408,14 @@ void run_problem(const Problem& p, cudaStream_t stream) {
                      "lora_xa");
     const float lscale = p.rank > 0 ? p.alpha / static_cast<float>(p.rank) : 0.0f;
 
-    // Decode (M <= 8).  Automatic choice: the integer-tensor-core GEMV where
-    // the shape allows it (K % 1024 == 0, 16-byte aligned operands), else the
-    // whole-tile GEMV, else the streamed-ring GEMV; the tcgen05 decode only on
-    // request.
+    // Decode (M <= 8).  Automatic choice: the whole-tile GEMV where the shape
+    // allows it, else the streamed-ring GEMV.  The integer-tensor-core GEMV
+    // and the tcgen05 decode run on request only: measured in a 24-layer
+    // CUDA graph at K = N = 4096 they are slower per layer at every M (the
+    // integer-MMA one: 10.4 / 10.7 / 13.2 / 17.0 us at M = 1 / 2 / 4 / 8,
+    // against 4.9 / 5.7 / 9.0 / 11.9 us for the whole-tile GEMV).
     const int dv = decode_variant_init().load();
-    if (p.M <= 8 && (dv == 0 || dv == 4) && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
+    if (p.M <= 8 && dv == 4 && aligned16(p.x) && aligned16(p.packed) && aligned16(p.scales)) {
         q4::GemvImmaArgs a{};
         if (q4::gemv_imma_geometry(c.sm_count, p.M, p.N, p.K, &a.cluster_k, &a.clusters, &a.tiles_per_cta,
                                    &a.kparts)) {
@@ -437,7 +439,9 @@ void run_problem(const Problem& p, cudaStream_t stream) {
             } else {
                 encode(&a.tmap_w, &a.tmap_s);
             }
-            a.x = p.x;
+            encode_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.x, static_cast<uint64_t>(K),
+                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(K) * 4, 256, static_cast<uint32_t>(p.M),
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
             a.y = p.y;
             a.M = p.M; a.N = N; a.K = K;
             a.tiles_total = (N + 15) / 16;

@@ -65,6 +65,11 @@ def main() -> int:
                 torch.cuda.synchronize(dev)
                 yq[engine] = ypush.cpu().numpy()
                 push.close()
+            # the library's measured choice (every rank times the candidates, all pick the same)
+            tuned = sharding.make_sharded(s, h, m, n, dist, dev, tune_x=xd)
+            tuned.y.fill_(float("nan"))
+            yq["tuned"] = tuned.run(xd).cpu().numpy()
+            tuned.close()
         y = sharding.allgather_columns(ys, n, dist).cpu().numpy()
         pad_ok = bool(np.isnan(yp[:, n:]).all())
         yp = yp[:, :n]
