@@ -30,10 +30,13 @@ _i8p = ctypes.POINTER(ctypes.c_int8)
 _u32p = ctypes.POINTER(ctypes.c_uint32)
 
 
-def build(with_reference: bool = True) -> None:
-    """Compile the oracle (and the reference library when its sources exist)."""
+def build(with_reference: bool = True, reference_root: str | None = None) -> None:
+    """Compile the oracle (and the reference library when its sources exist).
+
+    reference_root overrides the Makefile's REF (the reference checkout)."""
     target = "all" if with_reference else "oracle"
-    subprocess.run(["make", "-s", "-C", str(HERE), target], check=True)
+    extra = [f"REF={reference_root}"] if reference_root else []
+    subprocess.run(["make", "-s", "-C", str(HERE), target, *extra], check=True)
 
 
 def _ptr(arr: np.ndarray, typ):
