@@ -18,7 +18,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libspaceslug_b200.so"
 INCLUDE = PKG.parent / "include"
-SOURCES = ["runtime_abi.cu", "q4_gemv.cu", "q4_gemm.cu", "q4_gemm_pair.cu", "q4_decode.cu", "q4_gemv_tile.cu", "q4_gemv_imma.cu", "q4_aux.cu", "noalloc.cu", "upload.cu", "cq4.cu", "lora_train.cu", "sgemm_tc.cu"]
+SOURCES = ["runtime_abi.cu", "q4_gemv.cu", "q4_gemm.cu", "q4_gemm_pair.cu", "q4_decode.cu", "q4_gemv_tile.cu", "q4_gemv_imma.cu", "q4_aux.cu", "noalloc.cu", "upload.cu", "cq4.cu", "lora_train.cu", "sgemm_tc.cu", "lora_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

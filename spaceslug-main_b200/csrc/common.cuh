@@ -431,6 +431,30 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_format, uint32
            | ((m >> 4) << 24);       // M >> 4
 }
 
+// Instruction descriptor for kind::tf32: fp32 accumulate, A and B TF32 (2),
+// both K-major, tile M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t m, uint32_t n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// TF32 rounding (nearest, ties away) of an fp32 value, as fp32 bits: the
+// "hi" part of the hi / lo operand split (lo = x - hi is exact in fp32).
+__device__ __forceinline__ float to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
 __device__ __forceinline__ uint32_t elect_one() {
     uint32_t pred = 0;
     asm volatile(

@@ -227,6 +227,27 @@ struct LoraBackwardArgs {
 };
 size_t lora_backward_scratch_floats(int M, int K, int N, int rank);
 int launch_lora_backward(const LoraBackwardArgs& a, cudaStream_t stream);
+// LoRA gradients on the tcgen05 tensor cores (lora_tc.cu): one pass computes
+// partial[split][row][rp] of D[R x r] = sum over l < L of Aop[row][l] Bop[j][l].
+// tm_a: Aop fp32 with 128B swizzle, rows of D = source rows (mn_major = 0: dims {L, R}, box
+// 32 x 128) or rows of D contiguous in the source (mn_major = 1: dims {R, L}, box 32 x 32); tm_b: the
+// stacked TF32 hi / lo planes of Bop, dims {L, 2 rp}, box 32 x 2 rp.
+struct LoraTcPass {
+    CUtensorMap tm_a, tm_b;
+    float* partial;  // [splits][R][rp]
+    int R, L, splits, mn_major, rp, sm_count;
+    int* status;
+};
+int lora_tc_rp(int rank);                          // padded rank: 8, 16, 32 or 64
+int lora_tc_splits(int R, int L, int sm_count);    // l ranges per 128-row tile
+int launch_lora_tc_pass(const LoraTcPass& p, cudaStream_t stream);
+// sum of the splits in order; mode 0: stacked TF32 planes of the transpose
+// ([2 rp][ld]); mode 1: s * transpose ([r][ld]); mode 2: s * rows ([R][ld]).
+int launch_lora_tc_finalize(const float* src, int splits, int R, int pitch, int r, int rp, float s, int mode,
+                            float* out, long long ld, cudaStream_t stream);
+// stacked TF32 planes of a row-major [r][C] matrix ([2 rp][ld]).
+int launch_lora_tc_stack(const float* src, int r, int C, long long ld_src, int rp, float* plane, long long ld,
+                         cudaStream_t stream);
 int launch_sgd(float* p, const float* g, float lr, long long count, cudaStream_t stream);
 int launch_adamw(float* p, const float* g, float* m1, float* m2, float lr, float beta1, float beta2, float eps,
                  float wd, int step, long long count, cudaStream_t stream);

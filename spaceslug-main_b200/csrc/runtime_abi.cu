@@ -332,6 +332,75 @@ void run_sgemm(const float* a, long long lda, bool trans_a, const float* b, long
     check_launch(q4::launch_sgemm_tc(g, stream), "sgemm (tcgen05) launch");
 }
 
+// The LoRA backward takes the tensor-core passes of lora_tc.cu when the
+// operands suit their TMA maps: X [M][K] and dY [M][N] 16-byte aligned with
+// 16-byte row strides (K, N multiples of 4), every box inside its tensor
+// (M >= 128 rows for the 128-row boxes, K, N >= 32), rank <= 64.
+// SPACESLUG_LORA_BACKWARD=fma keeps the CUDA-core kernels of lora_train.cu.
+bool lora_backward_tc_suits(const q4::LoraBackwardArgs& g) {
+    static const bool fma_only = [] {
+        const char* e = std::getenv("SPACESLUG_LORA_BACKWARD");
+        return e && std::string(e) == "fma";
+    }();
+    return !fma_only && g.M >= 128 && g.K >= 32 && g.N >= 32 && g.K % 4 == 0 && g.N % 4 == 0 && g.rank >= 1 &&
+           g.rank <= 64 && aligned16(g.x) && aligned16(g.dy);
+}
+
+// T = X A, G = dY B^T, dB = s T^T dY, dA = s X^T G as four tcgen05 passes
+// (X, dY, dY, X each streamed once per pass), each followed by the fixed-order
+// sum of its splits.  The narrow operands enter as stacked TF32 hi / lo planes
+// [2 rp][L]: A^T and B by their own small kernels, T^T and G^T written by the
+// finalize step of the pass that made them.
+void run_lora_backward_tc(const q4::LoraBackwardArgs& g, int sm_count, int* status, cudaStream_t s) {
+    const int M = g.M, K = g.K, N = g.N, r = g.rank, rp = q4::lora_tc_rp(r);
+    auto round4 = [](int v) { return (static_cast<long long>(v) + 3) / 4 * 4; };
+    const long long Kp = round4(K), Np = round4(N), Mp = round4(M);
+    const int sT = q4::lora_tc_splits(M, K, sm_count), sG = q4::lora_tc_splits(M, N, sm_count);
+    const int sB = q4::lora_tc_splits(N, M, sm_count), sA = q4::lora_tc_splits(K, M, sm_count);
+    const long long part = std::max(std::max(static_cast<long long>(sT) * M, static_cast<long long>(sG) * M),
+                                    std::max(static_cast<long long>(sB) * N, static_cast<long long>(sA) * K)) * rp;
+    const long long two = 2ll * rp;
+    Scratch sc(static_cast<size_t>(two * (Kp + Np + 2 * Mp) + part) * sizeof(float), s);
+    float* astk = static_cast<float*>(sc.p);
+    float* bstk = astk + two * Kp;
+    float* tstk = bstk + two * Np;
+    float* gstk = tstk + two * Mp;
+    float* partial = gstk + two * Mp;
+    const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+    const uint32_t brows = static_cast<uint32_t>(two);
+    check_launch(q4::launch_lora_tc_finalize(g.lora_a, 1, K, r, r, rp, 1.0f, 0, astk, Kp, s), "lora A planes");
+    check_launch(q4::launch_lora_tc_stack(g.lora_b, r, N, N, rp, bstk, Np, s), "lora B planes");
+    q4::LoraTcPass p{};
+    p.partial = partial;
+    p.rp = rp;
+    p.sm_count = sm_count;
+    p.status = status;
+    auto pass = [&](const float* a, uint64_t a_inner, uint64_t a_outer, bool mn_major, const float* bplane, int R,
+                    int L, int splits, const char* what) {
+        encode_2d(&p.tm_a, F32, a, a_inner, a_outer, a_inner * 4, 32, mn_major ? 32 : 128, SW);
+        encode_2d(&p.tm_b, F32, bplane, static_cast<uint64_t>(L), two, static_cast<uint64_t>(round4(L)) * 4, 32,
+                  brows, SW);
+        p.R = R;
+        p.L = L;
+        p.splits = splits;
+        p.mn_major = mn_major ? 1 : 0;
+        check_launch(q4::launch_lora_tc_pass(p, s), what);
+    };
+    // T = X A: rows m of X (K-major), B operand A^T
+    pass(g.x, K, M, false, astk, M, K, sT, "lora T pass");
+    check_launch(q4::launch_lora_tc_finalize(partial, sT, M, rp, r, rp, 1.0f, 0, tstk, Mp, s), "lora T planes");
+    // G = dY B^T: rows m of dY (K-major), B operand B
+    pass(g.dy, N, M, false, bstk, M, N, sG, "lora G pass");
+    check_launch(q4::launch_lora_tc_finalize(partial, sG, M, rp, r, rp, 1.0f, 0, gstk, Mp, s), "lora G planes");
+    // dB^T = dY^T T: rows n of dY^T (MN-major), B operand T^T
+    pass(g.dy, N, M, true, tstk, N, M, sB, "lora dB pass");
+    check_launch(q4::launch_lora_tc_finalize(partial, sB, N, rp, r, rp, g.scale, 1, g.db, N, s), "lora dB");
+    // dA = X^T G: rows k of X^T (MN-major), B operand G^T
+    pass(g.x, K, M, true, gstk, K, M, sA, "lora dA pass");
+    check_launch(q4::launch_lora_tc_finalize(partial, sA, K, rp, r, rp, g.scale, 2, g.da, r, s), "lora dA");
+}
+
 // Co-resident CTA pairs of the pair kernel for operand type `op` (cached).
 int pair_capacity(DeviceCtx& c, q4::Operand16 op) {
     std::lock_guard<std::mutex> lk(c.pair_mu);
@@ -1429,10 +1498,16 @@ int spaceslug_q4_weights_lora_backward(spaceslug_q4_weights* w, const float* x, 
         const size_t pa = static_cast<size_t>(w->K) * w->rank * 4, pbb = static_cast<size_t>(w->rank) * w->N * 4;
         if (!w->lora_da) check(cudaMalloc(&w->lora_da, pa), "cudaMalloc dA");
         if (!w->lora_db) check(cudaMalloc(&w->lora_db, pbb), "cudaMalloc dB");
-        Scratch sc(q4::lora_backward_scratch_floats(static_cast<int>(m), w->K, w->N, w->rank) * 4, s);
-        q4::LoraBackwardArgs g{x, dy, w->lora_a, w->lora_b, w->lora_da, w->lora_db, static_cast<float*>(sc.p),
+        q4::LoraBackwardArgs g{x, dy, w->lora_a, w->lora_b, w->lora_da, w->lora_db, nullptr,
                                static_cast<int>(m), w->K, w->N, w->rank, w->alpha / static_cast<float>(w->rank)};
-        check_launch(q4::launch_lora_backward(g, s), "lora backward");
+        if (lora_backward_tc_suits(g)) {
+            DeviceCtx& c = ctx_for(w->device);
+            run_lora_backward_tc(g, c.sm_count, c.status, s);
+        } else {
+            Scratch sc(q4::lora_backward_scratch_floats(static_cast<int>(m), w->K, w->N, w->rank) * 4, s);
+            g.scratch = static_cast<float*>(sc.p);
+            check_launch(q4::launch_lora_backward(g, s), "lora backward");
+        }
         return SPACESLUG_OK;
     });
 }

@@ -63,13 +63,6 @@ struct SgCfg {
     static constexpr int kSmemAlloc = kSmem + 1024;  // slack to align the window to 1024
 };
 
-// TF32 rounding (nearest, ties away) of an fp32 value, as fp32 bits.
-__device__ __forceinline__ float to_tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
-
 // hi / lo planes of a row-major [R][C] matrix, same orientation: planes of
 // out_rows (>= R) rows with row pitch ld_out (>= C); the padding is zero.
 __global__ void __launch_bounds__(256) split_kernel(const float* __restrict__ src, int R, int C, long long ld_src,
@@ -111,22 +104,6 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float* __restrict__ 
             lo[static_cast<long long>(c) * ld_out + r] = v - h;
         }
     }
-}
-
-__device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// Instruction descriptor for kind::tf32: fp32 accumulate, A and B TF32 (2),
-// both K-major, tile M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t m, uint32_t n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 template <int BN>

@@ -106,6 +106,62 @@ def test_handle_backward_sgd_adamw(session, cuda, m, k, n, rank, c0, c1):
         assert np.max(np.abs(b2 - p_b)) <= 1e-5
 
 
+@pytest.mark.parametrize("m,k,n,rank,c0,c1", [(512, 4096, 4096, 16, 0, 4096), (300, 1024, 700, 5, 100, 600),
+                                             (200, 512, 384, 64, 0, 384), (333, 2048, 1024, 24, 0, 1024),
+                                             (128, 256, 160, 8, 0, 160)])
+def test_handle_backward_tensor_core_path(session, cuda, m, k, n, rank, c0, c1):
+    # M >= 128 with 16-byte rows: the tcgen05 passes (T, G, dB, dA), against
+    # float64 on the device; ragged tiles, every padded rank (8, 16, 32, 64),
+    # a column shard; a second call is bit-identical (fixed-order split sums)
+    import torch
+    rng = np.random.default_rng(m * 7 + rank)
+    _, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=5)
+    A = rng.standard_normal((k, rank)).astype(np.float32) * np.float32(0.02)
+    B = rng.standard_normal((rank, n)).astype(np.float32) * np.float32(0.02)
+    alpha = 2.0 * rank
+    x = torch.randn((m, k), device=cuda)
+    dy = torch.randn((m, c1 - c0), device=cuda)
+    with session.weights(packed, scales, k, n, c0, c1) as h:
+        h.set_lora(A, B, alpha)
+        h.lora_backward(x.data_ptr(), dy.data_ptr(), m)
+        _, _, da, db = h.get_lora(rank, grads=True)
+        h.lora_backward(x.data_ptr(), dy.data_ptr(), m)
+        _, _, da2, db2 = h.get_lora(rank, grads=True)
+    X, DY = x.double(), dy.double()
+    A64 = torch.from_numpy(A).to(cuda).double()
+    B64 = torch.from_numpy(np.ascontiguousarray(B[:, c0:c1])).to(cuda).double()
+    s = alpha / rank
+    da_ref = (s * X.T @ (DY @ B64.T)).cpu().numpy()
+    db_ref = (s * (X @ A64).T @ DY).cpu().numpy()
+    assert np.max(np.abs(da - da_ref)) <= 1e-5 * np.max(np.abs(da_ref))
+    assert np.max(np.abs(db - db_ref)) <= 1e-5 * np.max(np.abs(db_ref))
+    assert np.array_equal(da, da2) and np.array_equal(db, db2)
+
+
+def test_handle_backward_configs4_size(session, cuda):
+    # the configs[4]-sized backward (X 4096 x 8192, dY 4096 x 28672, rank 16)
+    # against float64 on the device
+    import torch
+    m, k, n, rank = 4096, 8192, 28672, 16
+    rng = np.random.default_rng(44)
+    _, packed, scales = synth.make_weights(k, n, 0.003, 0.01, seed=0)
+    A = rng.standard_normal((k, rank)).astype(np.float32) * np.float32(0.02)
+    B = rng.standard_normal((rank, n)).astype(np.float32) * np.float32(0.02)
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    x = torch.randn((m, k), device=cuda, generator=gen)
+    dy = torch.randn((m, n), device=cuda, generator=gen)
+    with session.weights(packed, scales, k, n) as h:
+        h.set_lora(A, B, 32.0)
+        h.lora_backward(x.data_ptr(), dy.data_ptr(), m)
+        _, _, da, db = h.get_lora(rank, grads=True)
+    X, DY = x.double(), dy.double()
+    s = 32.0 / rank
+    da_ref = (s * X.T @ (DY @ torch.from_numpy(B).to(cuda).double().T)).cpu().numpy()
+    db_ref = (s * (X @ torch.from_numpy(A).to(cuda).double()).T @ DY).cpu().numpy()
+    assert np.max(np.abs(da - da_ref)) <= 1e-5 * np.max(np.abs(da_ref))
+    assert np.max(np.abs(db - db_ref)) <= 1e-5 * np.max(np.abs(db_ref))
+
+
 def test_training_reduces_the_loss(session, cuda):
     # fit the adapter to a teacher adapter through the fused forward (MSE)
     import torch
