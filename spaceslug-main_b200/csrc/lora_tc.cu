@@ -32,7 +32,8 @@
 //  - The accumulator is double-buffered in tensor memory and restarted every
 //    32 l: four epilogue warps add each finished chunk to fp32 sums in
 //    registers with round-to-nearest (the tensor cores accumulate with
-//    truncation, a bias that grows with the contraction length).
+//    truncation, a bias that grows with the contraction length).  Two warps
+//    issue the MMAs, of even and of odd stages.
 //  - Work units are (128-row tile, range of l) pairs.  A persistent grid of
 //    one CTA per SM walks them; each unit writes its partial D to
 //    partial[split][row][RP], and lora_tc_finalize_kernel sums the splits in
@@ -54,7 +55,7 @@ namespace {
 
 constexpr int kLtRows = 128;      // rows of D per unit (the MMA's M)
 constexpr int kLtL = 32;          // contraction elements per stage: one 128-byte fp32 row
-constexpr int kLtThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-3 and 8-9 split, warps 4-7 epilogue
+constexpr int kLtThreads = 352;   // warp 0 TMA, warps 1 and 10 MMA, warps 2-3 and 8-9 split, warps 4-7 epilogue
 constexpr int kLtATile = kLtRows * kLtL * 4;  // 16 KB
 constexpr int kLtSplitWarps = 4;
 
@@ -70,9 +71,10 @@ struct LtCfg {
     static constexpr int kBudget = 222 * 1024;
     static constexpr int kStages = kBudget / kStageBytes > 8 ? 8 : kBudget / kStageBytes;
     static constexpr int kTmemCols = 4 * RP < 32 ? 32 : 4 * RP;  // two chunk buffers of 2RP columns
+    static_assert(kStages > 2, "the epilogue waits on the stages' MMA commits: it must not fall a phase behind");
     static constexpr int kBarOff = kStages * kStageBytes;
-    // full[S], split[S], empty[S], chunk_full[2], chunk_empty[2]; then abort flag, TMEM address
-    static constexpr int kNumBars = 3 * kStages + 4;
+    // full[S], split[S], empty[S], chunk_empty[2]; then abort flag, TMEM address
+    static constexpr int kNumBars = 3 * kStages + 2;
     static constexpr int kSmem = kBarOff + kNumBars * 8 + 16;
     static constexpr int kSmemAlloc = kSmem + 1024;  // slack to align the window to 1024
 };
@@ -84,6 +86,17 @@ __device__ __forceinline__ void lt_unit(int u, int tiles, int splits, int NS, in
     z = u / tiles;
     s0 = static_cast<int>(static_cast<long long>(z) * NS / splits);
     s1 = static_cast<int>(static_cast<long long>(z + 1) * NS / splits);
+}
+
+// Stages this CTA processes in all (every role walks the same sequence).
+__device__ __forceinline__ int lt_total_stages(int tiles, int splits, int NS) {
+    int n = 0;
+    for (int u = blockIdx.x; u < tiles * splits; u += gridDim.x) {
+        int tile, z, s0, s1;
+        lt_unit(u, tiles, splits, NS, tile, z, s0, s1);
+        n += s1 - s0;
+    }
+    return n;
 }
 
 template <int RP, bool MN>
@@ -104,8 +117,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
     auto full = [&](int s) { return bar + 8u * s; };
     auto split = [&](int s) { return bar + 8u * (C::kStages + s); };
     auto empty = [&](int s) { return bar + 8u * (2 * C::kStages + s); };
-    auto chunk_full = [&](int b) { return bar + 8u * (3 * C::kStages + b); };
-    auto chunk_empty = [&](int b) { return bar + 8u * (3 * C::kStages + 2 + b); };
+    auto chunk_empty = [&](int b) { return bar + 8u * (3 * C::kStages + b); };
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kBarOff + C::kNumBars * 8);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOff + C::kNumBars * 8 + 8);
 
@@ -115,10 +127,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
             mbar_init(split(s), kLtSplitWarps);
             mbar_init(empty(s), 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(chunk_full(b), 1);
-            mbar_init(chunk_empty(b), 4);  // one arrival per epilogue warp
-        }
+        for (int b = 0; b < 2; ++b) mbar_init(chunk_empty(b), 4);  // one arrival per epilogue warp
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -170,42 +179,38 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     mbar_drain(full(j % C::kStages), (j / C::kStages) & 1u);
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == 10) {
         if (lane == 0) {
             // -------------------------------------------------------- MMA --
+            // Warp 1 issues the even stages into chunk buffer 0, warp 10 the
+            // odd ones into buffer 1: one thread alone cannot issue the small
+            // MMAs of a 16-KB stage as fast as HBM delivers them.  One commit
+            // per stage tells both the producer (the stage may be refilled) and
+            // the epilogue (the chunk's sums are complete).
+            const int par = warp == 1 ? 0 : 1;
             constexpr uint32_t idesc = umma_idesc_tf32(kLtRows, 2 * RP);
-            int q = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-                int tile, z, s0, s1;
-                lt_unit(u, tiles, splits, NS, tile, z, s0, s1);
-                for (int st = s0; st < s1; ++st, ++q) {
-                    const int s = q % C::kStages, b = q & 1;
-                    if (q >= 2 &&
-                        !mbar_wait(chunk_empty(b), ((q >> 1) - 1) & 1u, abort_flag, status, kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    if (!mbar_wait(split(s), (q / C::kStages) & 1u, abort_flag, status, kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after_sync();
-                    const uint32_t st_base = base + s * C::kStageBytes;
-                    const uint32_t a_hi = st_base + C::kHi, a_lo = st_base + C::kLo, bt = st_base + C::kB;
-                    const uint32_t dacc = tmem + static_cast<uint32_t>(b * 2 * RP);
+            const int total = lt_total_stages(tiles, splits, NS);
+            const uint32_t dacc = tmem + static_cast<uint32_t>(par * 2 * RP);
+            int last = -1;
+            for (int q = par; q < total; q += 2) {
+                const int s = q % C::kStages;
+                if (q >= 2 && !mbar_wait(chunk_empty(par), ((q >> 1) - 1) & 1u, abort_flag, status, kStatusTimeoutMma))
+                    break;
+                if (!mbar_wait(split(s), (q / C::kStages) & 1u, abort_flag, status, kStatusTimeoutMma)) break;
+                tc_fence_after_sync();
+                const uint32_t st_base = base + s * C::kStageBytes;
+                const uint32_t a_hi = st_base + C::kHi, a_lo = st_base + C::kLo, bt = st_base + C::kB;
 #pragma unroll
-                    for (int kk = 0; kk < kLtL / 8; ++kk) {  // 8 tf32 = 32 bytes of each 128-byte row
-                        const uint64_t bd = umma_desc_k_sw128(bt + kk * 32);
-                        umma_tf32_ss(dacc, umma_desc_k_sw128(a_hi + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
-                        umma_tf32_ss(dacc, umma_desc_k_sw128(a_lo + kk * 32), bd, idesc, 1u);
-                    }
-                    umma_commit(empty(s));       // the stage may be refilled once these MMAs complete
-                    umma_commit(chunk_full(b));  // the chunk's sums are in buffer b
+                for (int kk = 0; kk < kLtL / 8; ++kk) {  // 8 tf32 = 32 bytes of each 128-byte row
+                    const uint64_t bd = umma_desc_k_sw128(bt + kk * 32);
+                    umma_tf32_ss(dacc, umma_desc_k_sw128(a_hi + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
+                    umma_tf32_ss(dacc, umma_desc_k_sw128(a_lo + kk * 32), bd, idesc, 1u);
                 }
+                umma_commit(empty(s));
+                last = q;
             }
-            if (*abort_flag && q > 0)  // issued MMAs finish before tensor memory is freed
-                mbar_drain(chunk_full((q - 1) & 1), ((q - 1) >> 1) & 1u);
+            if (*abort_flag && last >= 0)  // issued MMAs finish before tensor memory is freed
+                mbar_drain(empty(last % C::kStages), (last / C::kStages) & 1u);
         }
         __syncwarp();
     } else if (warp >= 4 && warp < 8) {
@@ -223,7 +228,8 @@ __global__ void __launch_bounds__(kLtThreads, 1)
             for (int j = 0; j < RP; ++j) total[j] = 0.0f;
             for (int st = s0; st < s1; ++st, ++q) {
                 const int b = q & 1;
-                if (!mbar_wait_warp(chunk_full(b), (q >> 1) & 1u, abort_flag, status, kStatusTimeoutEpilogue)) {
+                if (!mbar_wait_warp(empty(q % C::kStages), (q / C::kStages) & 1u, abort_flag, status,
+                                    kStatusTimeoutEpilogue)) {
                     ok = false;
                     break;
                 }
@@ -259,7 +265,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     dst[j / 4] = make_float4(total[j], total[j + 1], total[j + 2], total[j + 3]);
             }
         }
-    } else {
+    } else if (warp == 2 || warp == 3 || warp == 8 || warp == 9) {
         // ----------------------------------------------------------- split --
         // Warps 2, 3, 8, 9 write each stage's Aop as K-major TF32 hi and lo
         // tiles (rows of D at 128 B, 16-byte chunk c of row m at c ^ (m & 7)).
