@@ -55,9 +55,16 @@ namespace {
 
 constexpr int kLtRows = 128;      // rows of D per unit (the MMA's M)
 constexpr int kLtL = 32;          // contraction elements per stage: one 128-byte fp32 row
-constexpr int kLtThreads = 352;   // warp 0 TMA, warps 1 and 10 MMA, warps 2-3 and 8-9 split, warps 4-7 epilogue
+// Warps: 0 TMA, 1 and 10 MMA, 4-7 epilogue, split: 2-3 and 8-9, plus 11-14
+// for the transposing split (MN), which costs about twice as much per stage.
+template <bool MN>
+__host__ __device__ constexpr int lt_split_warps() { return MN ? 8 : 4; }
+template <bool MN>
+__host__ __device__ constexpr int lt_threads() { return MN ? 480 : 352; }
+__device__ __forceinline__ int lt_split_index(int warp) {  // split warp -> 0..7, else -1
+    return (warp == 2 || warp == 3) ? warp - 2 : (warp == 8 || warp == 9) ? warp - 6 : warp >= 11 ? warp - 7 : -1;
+}
 constexpr int kLtATile = kLtRows * kLtL * 4;  // 16 KB
-constexpr int kLtSplitWarps = 4;
 
 template <int RP, bool MN>
 struct LtCfg {
@@ -100,7 +107,7 @@ __device__ __forceinline__ int lt_total_stages(int tiles, int splits, int NS) {
 }
 
 template <int RP, bool MN>
-__global__ void __launch_bounds__(kLtThreads, 1)
+__global__ void __launch_bounds__(lt_threads<MN>(), 1)
     lora_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    float* __restrict__ partial, int R, int L, int splits, int* __restrict__ status) {
     using C = LtCfg<RP, MN>;
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(split(s), kLtSplitWarps);
+            mbar_init(split(s), lt_split_warps<MN>());
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) mbar_init(chunk_empty(b), 4);  // one arrival per epilogue warp
@@ -265,11 +272,12 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     dst[j / 4] = make_float4(total[j], total[j + 1], total[j + 2], total[j + 3]);
             }
         }
-    } else if (warp == 2 || warp == 3 || warp == 8 || warp == 9) {
+    } else if (lt_split_index(warp) >= 0) {
         // ----------------------------------------------------------- split --
         // Warps 2, 3, 8, 9 write each stage's Aop as K-major TF32 hi and lo
         // tiles (rows of D at 128 B, 16-byte chunk c of row m at c ^ (m & 7)).
-        const int ct = ((warp < 4) ? warp - 2 : warp - 6) * 32 + lane;  // 0..127
+        constexpr int kSplitThreads = lt_split_warps<MN>() * 32;
+        const int ct = lt_split_index(warp) * 32 + lane;  // 0 .. kSplitThreads - 1
         int q = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -288,8 +296,8 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     // transpose, four 16-byte writes per plane.  A phase of 8 lanes spans 4 c and 2 d, so its
                     // reads hit 8 distinct chunk positions and its writes 4.
 #pragma unroll
-                    for (int rep = 0; rep < 2; ++rep) {
-                        const int k = ct + 128 * rep, p = k >> 3, qq = k & 7;
+                    for (int rep = 0; rep < 256 / kSplitThreads; ++rep) {
+                        const int k = ct + kSplitThreads * rep, p = k >> 3, qq = k & 7;
                         const int c = (qq & 3) + 4 * (p & 7);     // rows 4c..4c+3 of D
                         const int d = (qq >> 2) + 2 * (p >> 3);   // l = 4d..4d+3
                         float4 v[4];
@@ -317,16 +325,16 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     // Loaded K-major already: hi in place, lo at the same offsets (so the same swizzle).
                     float4* hi = reinterpret_cast<float4*>(stage + C::kHi);
                     float4* lo = reinterpret_cast<float4*>(stage + C::kLo);
-                    constexpr int kPer = kLtATile / 16 / (kLtSplitWarps * 32);  // 8 float4 per thread
+                    constexpr int kPer = kLtATile / 16 / kSplitThreads;  // 8 float4 per thread
                     float4 v[kPer];
 #pragma unroll
-                    for (int i = 0; i < kPer; ++i) v[i] = hi[ct + 128 * i];
+                    for (int i = 0; i < kPer; ++i) v[i] = hi[ct + kSplitThreads * i];
 #pragma unroll
                     for (int i = 0; i < kPer; ++i) {
                         const float4 h =
                             make_float4(to_tf32(v[i].x), to_tf32(v[i].y), to_tf32(v[i].z), to_tf32(v[i].w));
-                        hi[ct + 128 * i] = h;
-                        lo[ct + 128 * i] = make_float4(v[i].x - h.x, v[i].y - h.y, v[i].z - h.z, v[i].w - h.w);
+                        hi[ct + kSplitThreads * i] = h;
+                        lo[ct + kSplitThreads * i] = make_float4(v[i].x - h.x, v[i].y - h.y, v[i].z - h.z, v[i].w - h.w);
                     }
                 }
                 fence_proxy_async_smem();  // the MMAs (async proxy) read what these threads wrote
@@ -426,7 +434,7 @@ int launch_pass_rp(const LoraTcPass& p, cudaStream_t stream) {
     if (e != cudaSuccess) return static_cast<int>(e);
     const long long units = static_cast<long long>((p.R + kLtRows - 1) / kLtRows) * p.splits;
     const int grid = static_cast<int>(units < p.sm_count ? units : p.sm_count);
-    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kLtThreads), C::kSmemAlloc, stream, p.tm_a,
+    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(lt_threads<MN>()), C::kSmemAlloc, stream, p.tm_a,
                       p.tm_b, p.partial, p.R, p.L, p.splits, p.status);
 }
 
