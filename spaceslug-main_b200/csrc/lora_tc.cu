@@ -86,39 +86,38 @@ struct LtCfg {
     static constexpr int kSmemAlloc = kSmem + 1024;  // slack to align the window to 1024
 };
 
-// Unit u of a pass: 128-row tile `tile`, split z, stages [s0, s1) of the NS
-// 32-l stages (splits <= NS, so every unit has at least one stage).
-__device__ __forceinline__ void lt_unit(int u, int tiles, int splits, int NS, int& tile, int& z, int& s0, int& s1) {
-    tile = u % tiles;
-    z = u / tiles;
-    s0 = static_cast<int>(static_cast<long long>(z) * NS / splits);
-    s1 = static_cast<int>(static_cast<long long>(z + 1) * NS / splits);
-}
-
-// Stages this CTA processes in all (every role walks the same sequence).
-__device__ __forceinline__ int lt_total_stages(int tiles, int splits, int NS) {
-    int n = 0;
-    for (int u = blockIdx.x; u < tiles * splits; u += gridDim.x) {
-        int tile, z, s0, s1;
-        lt_unit(u, tiles, splits, NS, tile, z, s0, s1);
-        n += s1 - s0;
-    }
-    return n;
+// Unit u of a launch: problem pi, 128-row tile, split z, stages [s0, s1) of
+// the problem's NS 32-l stages (splits <= NS, so every unit has at least one
+// stage).  The first problem's units come first.
+struct LtUnit {
+    int pi, tile, z, s0, s1;
+};
+__device__ __forceinline__ int lt_units(const LoraTcProblem& q) { return (q.R + kLtRows - 1) / kLtRows * q.splits; }
+__device__ __forceinline__ LtUnit lt_unit(const LoraTcPass& P, int u) {
+    LtUnit w;
+    const int u0 = lt_units(P.prob[0]);
+    w.pi = (P.count > 1 && u >= u0) ? 1 : 0;
+    const LoraTcProblem& q = P.prob[w.pi];
+    const int lu = w.pi ? u - u0 : u;
+    const int tiles = (q.R + kLtRows - 1) / kLtRows, NS = (q.L + kLtL - 1) / kLtL;
+    w.tile = lu % tiles;
+    w.z = lu / tiles;
+    w.s0 = static_cast<int>(static_cast<long long>(w.z) * NS / q.splits);
+    w.s1 = static_cast<int>(static_cast<long long>(w.z + 1) * NS / q.splits);
+    return w;
 }
 
 template <int RP, bool MN>
 __global__ void __launch_bounds__(lt_threads<MN>(), 1)
-    lora_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   float* __restrict__ partial, int R, int L, int splits, int* __restrict__ status) {
+    lora_tc_kernel(const __grid_constant__ LoraTcPass P) {
     using C = LtCfg<RP, MN>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // 128B-swizzled tiles need a 1024-aligned window
     uint8_t* smem = smem_raw + (base - raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tiles = (R + kLtRows - 1) / kLtRows;
-    const int units = tiles * splits;
-    const int NS = (L + kLtL - 1) / kLtL;
+    const int units = lt_units(P.prob[0]) + (P.count > 1 ? lt_units(P.prob[1]) : 0);
+    int* status = P.status;
 
     const uint32_t bar = base + C::kBarOff;
     auto full = [&](int s) { return bar + 8u * s; };
@@ -153,15 +152,18 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
     if (warp == 0) {
         if (lane == 0) {
             // --------------------------------------------------- producer --
-            tma_prefetch_desc(&tm_a);
-            tma_prefetch_desc(&tm_b);
+            for (int i = 0; i < P.count; ++i) {
+                tma_prefetch_desc(&P.prob[i].tm_a);
+                tma_prefetch_desc(&P.prob[i].tm_b);
+            }
             int q = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-                int tile, z, s0, s1;
-                lt_unit(u, tiles, splits, NS, tile, z, s0, s1);
-                const int row0 = tile * kLtRows;
-                for (int st = s0; st < s1; ++st, ++q) {
+                const LtUnit w = lt_unit(P, u);
+                const CUtensorMap* tm_a = &P.prob[w.pi].tm_a;
+                const CUtensorMap* tm_b = &P.prob[w.pi].tm_b;
+                const int row0 = w.tile * kLtRows;
+                for (int st = w.s0; st < w.s1; ++st, ++q) {
                     const int s = q % C::kStages;
                     if (q >= C::kStages &&
                         !mbar_wait(empty(s), ((q / C::kStages) - 1) & 1u, abort_flag, status, kStatusTimeoutProducer)) {
@@ -174,11 +176,11 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
                     if constexpr (MN) {
                         // four boxes of 32 rows of D x 32 l (l = the box's row), 4 KB apart
 #pragma unroll
-                        for (int b = 0; b < 4; ++b) tma_load_2d(a + b * 4096, &tm_a, full(s), row0 + 32 * b, l0);
+                        for (int b = 0; b < 4; ++b) tma_load_2d(a + b * 4096, tm_a, full(s), row0 + 32 * b, l0);
                     } else {
-                        tma_load_2d(a, &tm_a, full(s), l0, row0);
+                        tma_load_2d(a, tm_a, full(s), l0, row0);
                     }
-                    tma_load_2d(a + C::kB, &tm_b, full(s), l0, 0);
+                    tma_load_2d(a + C::kB, tm_b, full(s), l0, 0);
                 }
             }
             if (*abort_flag)  // let copies in flight land before the CTA exits
@@ -196,7 +198,11 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
             // the epilogue (the chunk's sums are complete).
             const int par = warp == 1 ? 0 : 1;
             constexpr uint32_t idesc = umma_idesc_tf32(kLtRows, 2 * RP);
-            const int total = lt_total_stages(tiles, splits, NS);
+            int total = 0;
+            for (int u = blockIdx.x; u < units; u += gridDim.x) {
+                const LtUnit w = lt_unit(P, u);
+                total += w.s1 - w.s0;
+            }
             const uint32_t dacc = tmem + static_cast<uint32_t>(par * 2 * RP);
             int last = -1;
             for (int q = par; q < total; q += 2) {
@@ -228,12 +234,12 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
         int q = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-            int tile, z, s0, s1;
-            lt_unit(u, tiles, splits, NS, tile, z, s0, s1);
+            const LtUnit w = lt_unit(P, u);
+            const LoraTcProblem& pb = P.prob[w.pi];
             float total[RP];
 #pragma unroll
             for (int j = 0; j < RP; ++j) total[j] = 0.0f;
-            for (int st = s0; st < s1; ++st, ++q) {
+            for (int st = w.s0; st < w.s1; ++st, ++q) {
                 const int b = q & 1;
                 if (!mbar_wait_warp(empty(q % C::kStages), (q / C::kStages) & 1u, abort_flag, status,
                                     kStatusTimeoutEpilogue)) {
@@ -264,9 +270,9 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
                 if (lane == 0) mbar_arrive(chunk_empty(b));  // buffer b may take chunk q + 2
             }
             if (!ok) break;
-            const int row = tile * kLtRows + quarter * 32 + lane;
-            if (row < R) {
-                float4* dst = reinterpret_cast<float4*>(partial + (static_cast<size_t>(z) * R + row) * RP);
+            const int row = w.tile * kLtRows + quarter * 32 + lane;
+            if (row < pb.R) {
+                float4* dst = reinterpret_cast<float4*>(pb.partial + (static_cast<size_t>(w.z) * pb.R + row) * RP);
 #pragma unroll
                 for (int j = 0; j < RP; j += 4)
                     dst[j / 4] = make_float4(total[j], total[j + 1], total[j + 2], total[j + 3]);
@@ -281,9 +287,8 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
         int q = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-            int tile, z, s0, s1;
-            lt_unit(u, tiles, splits, NS, tile, z, s0, s1);
-            for (int st = s0; st < s1; ++st, ++q) {
+            const LtUnit w = lt_unit(P, u);
+            for (int st = w.s0; st < w.s1; ++st, ++q) {
                 const int s = q % C::kStages;
                 if (!mbar_wait_warp(full(s), (q / C::kStages) & 1u, abort_flag, status, kStatusTimeoutDequant)) {
                     ok = false;
@@ -351,63 +356,59 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
     }
 }
 
+// One or two finalize steps per launch (blocks of the first come first).
+struct LtFinalizeLaunch {
+    LoraTcFinalize f[2];
+    int count, rp, blocks0;
+};
+
 // v[row][j] = sum over z < splits of src[z][row][j] in order z = 0, 1, ...
 // (row pitch `pitch`; columns j >= r read as zero), then
 //   mode 0: stacked TF32 planes of v^T: out[j][row] = hi(v), out[RP + j][row] = lo(v), rows r..RP-1 zero;
 //   mode 1: out[j][row] = s v (r rows, row pitch ld);
-//   mode 2: out[row][j] = s v (row pitch ld).
+//   mode 2: out[row][j] = s v (row pitch ld);
+//   mode 3: as mode 0 for v[row][j] = src[j][row] (a row-major [r][R] source with row pitch `pitch`).
 // One block per 32 rows, transposed through shared memory so both sides stay coalesced.
-__global__ void __launch_bounds__(256) lora_tc_finalize_kernel(const float* __restrict__ src, int splits, int R,
-                                                               int pitch, int r, int RP, float s, int mode,
-                                                               float* __restrict__ out, long long ld) {
+__global__ void __launch_bounds__(256) lora_tc_finalize_kernel(const LtFinalizeLaunch F) {
     __shared__ float tile[32][65];
     pdl_launch_dependents();
     pdl_wait();
-    const int r0 = blockIdx.x * 32;
+    const bool second = F.count > 1 && static_cast<int>(blockIdx.x) >= F.blocks0;
+    const LoraTcFinalize& f = F.f[second ? 1 : 0];
+    const int RP = F.rp, R = f.R, r = f.r, ld_src = f.pitch;
+    const long long ld = f.ld;
+    const int r0 = (static_cast<int>(blockIdx.x) - (second ? F.blocks0 : 0)) * 32;
     for (int i = threadIdx.x; i < 32 * RP; i += 256) {
         const int rr = i / RP, j = i % RP, row = r0 + rr;
         float v = 0.0f;
-        if (row < R && j < r)
-            for (int z = 0; z < splits; ++z) v += src[(static_cast<size_t>(z) * R + row) * pitch + j];
+        if (row < R && j < r) {
+            if (f.mode == 3) {
+                v = f.src[static_cast<size_t>(j) * ld_src + row];
+            } else {
+                for (int z = 0; z < f.splits; ++z) v += f.src[(static_cast<size_t>(z) * R + row) * ld_src + j];
+            }
+        }
         tile[rr][j] = v;
     }
     __syncthreads();
-    if (mode == 0) {
+    if (f.mode == 0 || f.mode == 3) {
         for (int i = threadIdx.x; i < RP * 32; i += 256) {
             const int j = i / 32, rr = i % 32, row = r0 + rr;
             if (row >= R) continue;
             const float v = tile[rr][j], h = to_tf32(v);
-            out[static_cast<size_t>(j) * ld + row] = h;
-            out[static_cast<size_t>(RP + j) * ld + row] = v - h;
+            f.out[static_cast<size_t>(j) * ld + row] = h;
+            f.out[static_cast<size_t>(RP + j) * ld + row] = v - h;
         }
-    } else if (mode == 1) {
+    } else if (f.mode == 1) {
         for (int i = threadIdx.x; i < r * 32; i += 256) {
             const int j = i / 32, rr = i % 32, row = r0 + rr;
-            if (row < R) out[static_cast<size_t>(j) * ld + row] = s * tile[rr][j];
+            if (row < R) f.out[static_cast<size_t>(j) * ld + row] = f.s * tile[rr][j];
         }
     } else {
         for (int i = threadIdx.x; i < 32 * r; i += 256) {
             const int rr = i / r, j = i % r, row = r0 + rr;
-            if (row < R) out[static_cast<size_t>(row) * ld + j] = s * tile[rr][j];
+            if (row < R) f.out[static_cast<size_t>(row) * ld + j] = f.s * tile[rr][j];
         }
-    }
-}
-
-// Stacked TF32 planes of a row-major [r][C] matrix, same orientation:
-// plane[j][c] = hi(src[j][c]), plane[RP + j][c] = lo, rows r..RP-1 zero.
-__global__ void __launch_bounds__(256) lora_tc_stack_kernel(const float* __restrict__ src, int r, int C,
-                                                            long long ld_src, int RP, float* __restrict__ plane,
-                                                            long long ld) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const long long total = static_cast<long long>(RP) * C;
-    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * 256) {
-        const int j = static_cast<int>(i / C);
-        const long long c = i - static_cast<long long>(j) * C;
-        const float v = j < r ? src[static_cast<long long>(j) * ld_src + c] : 0.0f;
-        const float h = to_tf32(v);
-        plane[static_cast<long long>(j) * ld + c] = h;
-        plane[static_cast<long long>(RP + j) * ld + c] = v - h;
     }
 }
 
@@ -432,10 +433,11 @@ int launch_pass_rp(const LoraTcPass& p, cudaStream_t stream) {
     auto kern = lora_tc_kernel<RP, MN>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemAlloc);
     if (e != cudaSuccess) return static_cast<int>(e);
-    const long long units = static_cast<long long>((p.R + kLtRows - 1) / kLtRows) * p.splits;
+    long long units = 0;
+    for (int i = 0; i < p.count; ++i)
+        units += static_cast<long long>((p.prob[i].R + kLtRows - 1) / kLtRows) * p.prob[i].splits;
     const int grid = static_cast<int>(units < p.sm_count ? units : p.sm_count);
-    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(lt_threads<MN>()), C::kSmemAlloc, stream, p.tm_a,
-                      p.tm_b, p.partial, p.R, p.L, p.splits, p.status);
+    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(lt_threads<MN>()), C::kSmemAlloc, stream, p);
 }
 
 }  // namespace
@@ -447,27 +449,46 @@ int lora_tc_rp(int rank) {
     return 64;
 }
 
-int lora_tc_splits(int R, int L, int sm_count) {
-    const int tiles = (R + kLtRows - 1) / kLtRows, NS = (L + kLtL - 1) / kLtL;
-    const int smax = NS < 32 ? NS : 32;
-    int best = 1;
-    long long best_t = LLONG_MAX;
-    for (int S = 1; S <= smax; ++S) {
-        const long long units = static_cast<long long>(tiles) * S;
-        const long long waves = (units + sm_count - 1) / sm_count;
-        // per-CTA stages, plus about two stages of fill and store per unit
-        const long long t = waves * ((NS + S - 1) / S + 2);
-        if (t < best_t) {
-            best_t = t;
-            best = S;
+// Splits chosen together so that the problems' units have about the same
+// number of stages (t) and the launch's units fill whole waves of the SMs:
+// the cost of a candidate is waves x (longest unit + about two stages of
+// fill and store).
+void lora_tc_plan(int count, const int* R, const int* L, int sm_count, int* splits) {
+    int tiles[2], NS[2], nsmax = 1;
+    for (int i = 0; i < count; ++i) {
+        tiles[i] = (R[i] + kLtRows - 1) / kLtRows;
+        NS[i] = (L[i] + kLtL - 1) / kLtL;
+        if (NS[i] > nsmax) nsmax = NS[i];
+        splits[i] = 1;
+    }
+    long long best = LLONG_MAX;
+    for (int t = 1; t <= nsmax; ++t) {
+        int S[2];
+        long long units = 0;
+        int longest = 0;
+        for (int i = 0; i < count; ++i) {
+            S[i] = (NS[i] + t - 1) / t;
+            if (S[i] > 64) S[i] = 64;
+            if (S[i] > NS[i]) S[i] = NS[i];
+            units += static_cast<long long>(tiles[i]) * S[i];
+            const int len = (NS[i] + S[i] - 1) / S[i];
+            if (len > longest) longest = len;
+        }
+        const long long cost = (units + sm_count - 1) / sm_count * (longest + 2);
+        if (cost < best) {
+            best = cost;
+            for (int i = 0; i < count; ++i) splits[i] = S[i];
         }
     }
-    return best;
 }
 
 int launch_lora_tc_pass(const LoraTcPass& p, cudaStream_t stream) {
-    if (p.R < 1 || p.L < 1 || p.splits < 1 || p.splits > (p.L + kLtL - 1) / kLtL || p.sm_count < 1)
-        return static_cast<int>(cudaErrorInvalidValue);
+    if (p.count < 1 || p.count > 2 || p.sm_count < 1) return static_cast<int>(cudaErrorInvalidValue);
+    for (int i = 0; i < p.count; ++i) {
+        const LoraTcProblem& q = p.prob[i];
+        if (q.R < 1 || q.L < 1 || q.splits < 1 || q.splits > (q.L + kLtL - 1) / kLtL || !q.partial)
+            return static_cast<int>(cudaErrorInvalidValue);
+    }
     const bool mn = p.mn_major != 0;
     switch (p.rp) {
         case 8: return mn ? launch_pass_rp<8, true>(p, stream) : launch_pass_rp<8, false>(p, stream);
@@ -478,21 +499,21 @@ int launch_lora_tc_pass(const LoraTcPass& p, cudaStream_t stream) {
     }
 }
 
-int launch_lora_tc_finalize(const float* src, int splits, int R, int pitch, int r, int rp, float s, int mode,
-                            float* out, long long ld, cudaStream_t stream) {
-    if (R < 1 || splits < 1 || r < 1 || r > rp || rp > 64 || mode < 0 || mode > 2)
-        return static_cast<int>(cudaErrorInvalidValue);
-    return launch_pdl(lora_tc_finalize_kernel, dim3(static_cast<unsigned>((R + 31) / 32)), dim3(256), 0, stream, src,
-                      splits, R, pitch, r, rp, s, mode, out, ld);
-}
-
-int launch_lora_tc_stack(const float* src, int r, int C, long long ld_src, int rp, float* plane, long long ld,
-                         cudaStream_t stream) {
-    if (r < 1 || r > rp || C < 1) return static_cast<int>(cudaErrorInvalidValue);
-    long long blocks = (static_cast<long long>(rp) * C + 255) / 256;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    return launch_pdl(lora_tc_stack_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, src, r, C,
-                      ld_src, rp, plane, ld);
+int launch_lora_tc_finalize(const LoraTcFinalize* f, int count, int rp, cudaStream_t stream) {
+    if (count < 1 || count > 2 || rp < 8 || rp > 64) return static_cast<int>(cudaErrorInvalidValue);
+    LtFinalizeLaunch F{};
+    F.count = count;
+    F.rp = rp;
+    int blocks = 0;
+    for (int i = 0; i < count; ++i) {
+        const LoraTcFinalize& q = f[i];
+        if (q.R < 1 || q.splits < 1 || q.r < 1 || q.r > rp || q.mode < 0 || q.mode > 3 || !q.src || !q.out)
+            return static_cast<int>(cudaErrorInvalidValue);
+        F.f[i] = q;
+        if (i == 0) F.blocks0 = (q.R + 31) / 32;
+        blocks += (q.R + 31) / 32;
+    }
+    return launch_pdl(lora_tc_finalize_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, F);
 }
 
 }  // namespace q4

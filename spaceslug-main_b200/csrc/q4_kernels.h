@@ -227,27 +227,40 @@ struct LoraBackwardArgs {
 };
 size_t lora_backward_scratch_floats(int M, int K, int N, int rank);
 int launch_lora_backward(const LoraBackwardArgs& a, cudaStream_t stream);
-// LoRA gradients on the tcgen05 tensor cores (lora_tc.cu): one pass computes
-// partial[split][row][rp] of D[R x r] = sum over l < L of Aop[row][l] Bop[j][l].
-// tm_a: Aop fp32 with 128B swizzle, rows of D = source rows (mn_major = 0: dims {L, R}, box
-// 32 x 128) or rows of D contiguous in the source (mn_major = 1: dims {R, L}, box 32 x 32); tm_b: the
-// stacked TF32 hi / lo planes of Bop, dims {L, 2 rp}, box 32 x 2 rp.
-struct LoraTcPass {
+// LoRA gradients on the tcgen05 tensor cores (lora_tc.cu).  A problem is
+// partial[split][row][rp] of D[R x r] = sum over l < L of Aop[row][l] Bop[j][l];
+// tm_a: Aop fp32 with 128B swizzle, rows of D = source rows (mn_major = 0:
+// dims {L, R}, box 32 x 128) or rows of D contiguous in the source
+// (mn_major = 1: dims {R, L}, box 32 x 32); tm_b: the stacked TF32 hi / lo
+// planes of Bop, dims {L, 2 rp}, box 32 x 2 rp.  One launch walks the work
+// units of one or two problems of the same form.
+struct LoraTcProblem {
     CUtensorMap tm_a, tm_b;
     float* partial;  // [splits][R][rp]
-    int R, L, splits, mn_major, rp, sm_count;
+    int R, L, splits;
+};
+struct LoraTcPass {
+    LoraTcProblem prob[2];
+    int count;  // 1 or 2
+    int mn_major, rp, sm_count;
     int* status;
 };
-int lora_tc_rp(int rank);                          // padded rank: 8, 16, 32 or 64
-int lora_tc_splits(int R, int L, int sm_count);    // l ranges per 128-row tile
+int lora_tc_rp(int rank);  // padded rank: 8, 16, 32 or 64
+// l ranges per 128-row tile for `count` problems sharing one launch
+void lora_tc_plan(int count, const int* R, const int* L, int sm_count, int* splits);
 int launch_lora_tc_pass(const LoraTcPass& p, cudaStream_t stream);
-// sum of the splits in order; mode 0: stacked TF32 planes of the transpose
-// ([2 rp][ld]); mode 1: s * transpose ([r][ld]); mode 2: s * rows ([R][ld]).
-int launch_lora_tc_finalize(const float* src, int splits, int R, int pitch, int r, int rp, float s, int mode,
-                            float* out, long long ld, cudaStream_t stream);
-// stacked TF32 planes of a row-major [r][C] matrix ([2 rp][ld]).
-int launch_lora_tc_stack(const float* src, int r, int C, long long ld_src, int rp, float* plane, long long ld,
-                         cudaStream_t stream);
+// v[row][j] = sum of the splits in order; mode 0: stacked TF32 planes of the
+// transpose ([2 rp][ld]); mode 1: s * transpose ([r][ld]); mode 2: s * rows
+// ([R][ld]); mode 3: stacked planes of a row-major [r][R] source (pitch =
+// its row pitch, splits = 1).
+struct LoraTcFinalize {
+    const float* src;
+    int splits, R, pitch, r, mode;
+    float s;
+    float* out;
+    long long ld;
+};
+int launch_lora_tc_finalize(const LoraTcFinalize* f, int count, int rp, cudaStream_t stream);
 int launch_sgd(float* p, const float* g, float lr, long long count, cudaStream_t stream);
 int launch_adamw(float* p, const float* g, float* m1, float* m2, float lr, float beta1, float beta2, float eps,
                  float wd, int step, long long count, cudaStream_t stream);

@@ -346,59 +346,75 @@ bool lora_backward_tc_suits(const q4::LoraBackwardArgs& g) {
            g.rank <= 64 && aligned16(g.x) && aligned16(g.dy);
 }
 
-// T = X A, G = dY B^T, dB = s T^T dY, dA = s X^T G as four tcgen05 passes
-// (X, dY, dY, X each streamed once per pass), each followed by the fixed-order
-// sum of its splits.  The narrow operands enter as stacked TF32 hi / lo planes
-// [2 rp][L]: A^T and B by their own small kernels, T^T and G^T written by the
-// finalize step of the pass that made them.
+// T = X A, G = dY B^T, dB = s T^T dY, dA = s X^T G as tcgen05 passes, in
+// five launches: the A^T and B planes; the T and G passes (X and dY rows,
+// one launch); their split sums as T^T and G^T planes; the dB and dA passes
+// (dY and X transposed, one launch); their split sums scaled into dB and dA.
+// The narrow operands enter the passes as stacked TF32 hi / lo planes
+// [2 rp][L].
 void run_lora_backward_tc(const q4::LoraBackwardArgs& g, int sm_count, int* status, cudaStream_t s) {
     const int M = g.M, K = g.K, N = g.N, r = g.rank, rp = q4::lora_tc_rp(r);
     auto round4 = [](int v) { return (static_cast<long long>(v) + 3) / 4 * 4; };
     const long long Kp = round4(K), Np = round4(N), Mp = round4(M);
-    const int sT = q4::lora_tc_splits(M, K, sm_count), sG = q4::lora_tc_splits(M, N, sm_count);
-    const int sB = q4::lora_tc_splits(N, M, sm_count), sA = q4::lora_tc_splits(K, M, sm_count);
-    const long long part = std::max(std::max(static_cast<long long>(sT) * M, static_cast<long long>(sG) * M),
-                                    std::max(static_cast<long long>(sB) * N, static_cast<long long>(sA) * K)) * rp;
+    int s1[2], s2[2];
+    {
+        const int R1[2] = {M, M}, L1[2] = {K, N}, R2[2] = {N, K}, L2[2] = {M, M};
+        q4::lora_tc_plan(2, R1, L1, sm_count, s1);
+        q4::lora_tc_plan(2, R2, L2, sm_count, s2);
+    }
+    const long long partA = static_cast<long long>(s1[0]) * M * rp, partB = static_cast<long long>(s1[1]) * M * rp;
+    const long long partC = static_cast<long long>(s2[0]) * N * rp, partD = static_cast<long long>(s2[1]) * K * rp;
+    const long long part = std::max(partA + partB, partC + partD);
     const long long two = 2ll * rp;
     Scratch sc(static_cast<size_t>(two * (Kp + Np + 2 * Mp) + part) * sizeof(float), s);
     float* astk = static_cast<float*>(sc.p);
     float* bstk = astk + two * Kp;
     float* tstk = bstk + two * Np;
     float* gstk = tstk + two * Mp;
-    float* partial = gstk + two * Mp;
+    float* part0 = gstk + two * Mp;
     const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
     const uint32_t brows = static_cast<uint32_t>(two);
-    check_launch(q4::launch_lora_tc_finalize(g.lora_a, 1, K, r, r, rp, 1.0f, 0, astk, Kp, s), "lora A planes");
-    check_launch(q4::launch_lora_tc_stack(g.lora_b, r, N, N, rp, bstk, Np, s), "lora B planes");
+    auto problem = [&](q4::LoraTcProblem& q, const float* a, uint64_t a_inner, uint64_t a_outer, bool mn_major,
+                       const float* bplane, int R, int L, int splits, float* partial) {
+        encode_2d(&q.tm_a, F32, a, a_inner, a_outer, a_inner * 4, 32, mn_major ? 32 : 128, SW);
+        encode_2d(&q.tm_b, F32, bplane, static_cast<uint64_t>(L), two, static_cast<uint64_t>(round4(L)) * 4, 32,
+                  brows, SW);
+        q.partial = partial;
+        q.R = R;
+        q.L = L;
+        q.splits = splits;
+    };
+    q4::LoraTcFinalize f[2];
+    // A^T planes (A is [K][r]: its rows are the planes' columns) and B planes
+    f[0] = {g.lora_a, 1, K, r, r, 0, 1.0f, astk, Kp};
+    f[1] = {g.lora_b, 1, N, N, r, 3, 1.0f, bstk, Np};
+    check_launch(q4::launch_lora_tc_finalize(f, 2, rp, s), "lora A / B planes");
     q4::LoraTcPass p{};
-    p.partial = partial;
+    p.count = 2;
     p.rp = rp;
     p.sm_count = sm_count;
     p.status = status;
-    auto pass = [&](const float* a, uint64_t a_inner, uint64_t a_outer, bool mn_major, const float* bplane, int R,
-                    int L, int splits, const char* what) {
-        encode_2d(&p.tm_a, F32, a, a_inner, a_outer, a_inner * 4, 32, mn_major ? 32 : 128, SW);
-        encode_2d(&p.tm_b, F32, bplane, static_cast<uint64_t>(L), two, static_cast<uint64_t>(round4(L)) * 4, 32,
-                  brows, SW);
-        p.R = R;
-        p.L = L;
-        p.splits = splits;
-        p.mn_major = mn_major ? 1 : 0;
-        check_launch(q4::launch_lora_tc_pass(p, s), what);
-    };
-    // T = X A: rows m of X (K-major), B operand A^T
-    pass(g.x, K, M, false, astk, M, K, sT, "lora T pass");
-    check_launch(q4::launch_lora_tc_finalize(partial, sT, M, rp, r, rp, 1.0f, 0, tstk, Mp, s), "lora T planes");
-    // G = dY B^T: rows m of dY (K-major), B operand B
-    pass(g.dy, N, M, false, bstk, M, N, sG, "lora G pass");
-    check_launch(q4::launch_lora_tc_finalize(partial, sG, M, rp, r, rp, 1.0f, 0, gstk, Mp, s), "lora G planes");
-    // dB^T = dY^T T: rows n of dY^T (MN-major), B operand T^T
-    pass(g.dy, N, M, true, tstk, N, M, sB, "lora dB pass");
-    check_launch(q4::launch_lora_tc_finalize(partial, sB, N, rp, r, rp, g.scale, 1, g.db, N, s), "lora dB");
-    // dA = X^T G: rows k of X^T (MN-major), B operand G^T
-    pass(g.x, K, M, true, gstk, K, M, sA, "lora dA pass");
-    check_launch(q4::launch_lora_tc_finalize(partial, sA, K, rp, r, rp, g.scale, 2, g.da, r, s), "lora dA");
+    // T = X A (rows m of X, B operand A^T) and G = dY B^T (rows m of dY, B operand B)
+    float* partT = part0;
+    float* partG = part0 + partA;
+    problem(p.prob[0], g.x, K, M, false, astk, M, K, s1[0], partT);
+    problem(p.prob[1], g.dy, N, M, false, bstk, M, N, s1[1], partG);
+    p.mn_major = 0;
+    check_launch(q4::launch_lora_tc_pass(p, s), "lora T / G pass");
+    f[0] = {partT, s1[0], M, rp, r, 0, 1.0f, tstk, Mp};
+    f[1] = {partG, s1[1], M, rp, r, 0, 1.0f, gstk, Mp};
+    check_launch(q4::launch_lora_tc_finalize(f, 2, rp, s), "lora T / G planes");
+    // dB^T = dY^T T (rows n of dY^T, B operand T^T) and dA = X^T G (rows k of X^T, B operand G^T)
+    float* partB2 = part0;
+    float* partA2 = part0 + partC;
+    problem(p.prob[0], g.dy, N, M, true, tstk, N, M, s2[0], partB2);
+    problem(p.prob[1], g.x, K, M, true, gstk, K, M, s2[1], partA2);
+    p.mn_major = 1;
+    check_launch(q4::launch_lora_tc_pass(p, s), "lora dB / dA pass");
+    f[0] = {partB2, s2[0], N, rp, r, 1, g.scale, g.db, N};
+    f[1] = {partA2, s2[1], K, rp, r, 2, g.scale, g.da, r};
+    check_launch(q4::launch_lora_tc_finalize(f, 2, rp, s), "lora dB / dA");
 }
 
 // Co-resident CTA pairs of the pair kernel for operand type `op` (cached).
