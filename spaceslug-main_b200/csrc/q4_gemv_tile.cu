@@ -53,13 +53,16 @@ constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row
 // CTAs share an SM).
 template <int M>
 struct TileCfg {
-    // M >= 7 multiplies on the tensor cores with mma.sync (see below): its
-    // cost does not grow with M, but every CTA first converts all of X into
-    // f16 hi/lo planes (~3.8 us at M = 8), so it only breaks even with the
-    // fp32 path (M FMAs per weight) at M = 8 and loses at M = 4.
-    static constexpr bool kMma = M >= 7;
+    // M >= 5 multiplies on the tensor cores with mma.sync (see below): its
+    // loop costs the same at every M (3.6 us per layer in a 24-layer graph at
+    // K = N = 4096), but every CTA first converts all of X into f16 hi/lo
+    // planes (1.4 us at M = 4, 2.1 us at M = 8), so it ties with the fp32
+    // path (M FMAs per weight: 5.0 us at M = 4) at M = 4 and wins above.
+    static constexpr bool kMma = M >= 5;
     static constexpr int kWarps = 16;
     static constexpr int kThreads = kWarps * 32;
+    // X conversion of the mma path: float4 per thread and row (M * kslice <= 32768)
+    static constexpr int kConvPerRow = (16 + M - 1) / M;
 };
 
 __host__ __device__ inline int tile_warps(int) { return 16; }
@@ -69,7 +72,6 @@ __host__ __device__ inline int tile_warps(int) { return 16; }
 // so that bounded wait runs out and the timeout path runs (status word,
 // abort flag, the CTA returns).  Read once per warp-0 thread at entry.
 static __device__ int g_tile_stall_test = 0;
-constexpr int kMmaMaxChunksPerThread = 8;  // X conversion: M * kslice / 8 chunks over 512 threads
 
 struct TileLayout {
     int kslice, nbox, nsbox;
@@ -246,47 +248,37 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
         if (stall_test)  // phase 0 of box 0's barrier completes; phase 1 is never armed
             ok = ok && mbar_wait(wfull(0), 0u, abort_flag, status, kStatusTimeoutGemv) &&
                  mbar_wait(wfull(0), 1u, abort_flag, status, kStatusTimeoutGemv);
-        float* rmax = reinterpret_cast<float*>(smem + L.misc_off + 16);             // [16 warps][8]
+        uint32_t* rmax = reinterpret_cast<uint32_t*>(smem + L.misc_off + 16);     // [16 warps][8], float bits
         int* rexp = reinterpret_cast<int*>(smem + L.misc_off + 16 + 16 * 8 * 4);    // [8]
-        // X -> per-row exponents and f16 hi/lo planes, in place: chunks of 8 k
-        // are read into registers, the CTA syncs, and the planes are written
-        // with chunk c of row m at position c ^ (m & 7) (conflict-free reads).
-        const int cpr = L.kslice / 8;  // chunks per row
-        const int nch = M * cpr;
-        float xv[kMmaMaxChunksPerThread][8];
-        float mx[8];
+        // X -> per-row exponents and f16 hi/lo planes, in place.  Thread t
+        // takes float4 t, t + 512, ... of each row (consecutive threads,
+        // consecutive 16 bytes), keeps them in registers for the row maxima
+        // (|x| as bits: unsigned order = float order; one redux per row and
+        // warp), and after two barriers writes each as 8 bytes of the planes,
+        // with 8-k chunk c of row m at position c ^ (m & 7).
+        constexpr int kPerRow = TileCfg<M>::kConvPerRow;  // float4 per thread and row
+        const int f4_row = L.kslice / 4;
+        float4 xv[M][kPerRow];
+        const float4* xf = reinterpret_cast<const float4*>(smem + L.x_off);
 #pragma unroll
-        for (int m = 0; m < 8; ++m) mx[m] = 0.0f;
-        const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
+        for (int m = 0; m < M; ++m) {
+            uint32_t mb = 0;
 #pragma unroll
-        for (int i = 0; i < kMmaMaxChunksPerThread; ++i) {
-            const int ch = tid + i * kThreads;
-            if (ch < nch && ok) {
-                const float4 a = *reinterpret_cast<const float4*>(xf + ch * 8);
-                const float4 b = *reinterpret_cast<const float4*>(xf + ch * 8 + 4);
-                xv[i][0] = a.x; xv[i][1] = a.y; xv[i][2] = a.z; xv[i][3] = a.w;
-                xv[i][4] = b.x; xv[i][5] = b.y; xv[i][6] = b.z; xv[i][7] = b.w;
-                float cm = 0.0f;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) cm = fmaxf(cm, fabsf(xv[i][e]));
-                const int m = ch / cpr;
-#pragma unroll
-                for (int mm = 0; mm < 8; ++mm) mx[mm] = (mm == m) ? fmaxf(mx[mm], cm) : mx[mm];
+            for (int i = 0; i < kPerRow; ++i) {
+                const int f = tid + i * kThreads;
+                xv[m][i] = (f < f4_row && ok) ? xf[m * f4_row + f] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                const uint32_t a = __float_as_uint(fmaxf(fmaxf(fabsf(xv[m][i].x), fabsf(xv[m][i].y)),
+                                                         fmaxf(fabsf(xv[m][i].z), fabsf(xv[m][i].w))));
+                mb = a > mb ? a : mb;
             }
+            mb = __reduce_max_sync(0xffffffffu, mb);
+            if (lane == 0) rmax[warp * 8 + m] = mb;
         }
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], off));
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int m = 0; m < 8; ++m) rmax[warp * 8 + m] = mx[m];
-        }
-        __syncthreads();  // every chunk is in registers; every warp's row maxima are out
-        if (tid < 8) {
-            float v = 0.0f;
-            for (int w16 = 0; w16 < kWarps; ++w16) v = fmaxf(v, rmax[w16 * 8 + tid]);
+        __syncthreads();  // every warp's row maxima are out; X is in registers
+        if (tid < M) {
+            uint32_t vb = 0;
+            for (int w16 = 0; w16 < kWarps; ++w16) vb = rmax[w16 * 8 + tid] > vb ? rmax[w16 * 8 + tid] : vb;
+            const float v = __uint_as_float(vb);
             int e = 0;
             if (v > 0.0f && isfinite(v)) {
                 int e2;
@@ -297,28 +289,31 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
             rexp[tid] = e;
         }
         __syncthreads();
-        const uint32_t hi_plane = base + L.x_off, lo_plane = hi_plane + M * L.kslice * 2;
+        uint8_t* hi_plane = smem + L.x_off;
+        uint8_t* lo_plane = hi_plane + M * L.kslice * 2;
+        const int cpr = L.kslice / 8;  // 8-k chunks per row
 #pragma unroll
-        for (int i = 0; i < kMmaMaxChunksPerThread; ++i) {
-            const int ch = tid + i * kThreads;
-            if (ch < nch && ok) {
-                const int m = ch / cpr, c = ch % cpr;
-                const float sc = exp2i(rexp[m]);
-                uint32_t hw[4], lw[4];
+        for (int m = 0; m < M; ++m) {
+            const float sc = exp2i(rexp[m]);
+            const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float a0 = xv[i][2 * e] * sc, a1 = xv[i][2 * e + 1] * sc;
-                    const __half2 hh = __floats2half2_rn(a0, a1);
-                    const float2 hf = __half22float2(hh);
-                    const __half2 ll = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
-                    hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
-                    lw[e] = *reinterpret_cast<const uint32_t*>(&ll);
+            for (int i = 0; i < kPerRow; ++i) {
+                const int f = tid + i * kThreads;
+                if (f < f4_row && ok) {
+                    const float2 a01 = __fmul2_rn(make_float2(xv[m][i].x, xv[m][i].y), sc2);
+                    const float2 a23 = __fmul2_rn(make_float2(xv[m][i].z, xv[m][i].w), sc2);
+                    const __half2 h01 = __float22half2_rn(a01), h23 = __float22half2_rn(a23);
+                    const float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
+                    const float2 r01 = __fadd2_rn(a01, make_float2(-b01.x, -b01.y));
+                    const float2 r23 = __fadd2_rn(a23, make_float2(-b23.x, -b23.y));
+                    const __half2 l01 = __float22half2_rn(r01), l23 = __float22half2_rn(r23);
+                    const int c = f >> 1;
+                    const int pos = (m * cpr + (c ^ (m & 7))) * 16 + (f & 1) * 8;
+                    *reinterpret_cast<uint2*>(hi_plane + pos) =
+                        make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+                    *reinterpret_cast<uint2*>(lo_plane + pos) =
+                        make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
                 }
-                const uint32_t pos = static_cast<uint32_t>(m * cpr + (c ^ (m & 7))) * 16;
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(hi_plane + pos), "r"(hw[0]), "r"(hw[1]),
-                             "r"(hw[2]), "r"(hw[3]) : "memory");
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(lo_plane + pos), "r"(lw[0]), "r"(lw[1]),
-                             "r"(lw[2]), "r"(lw[3]) : "memory");
             }
         }
         __syncthreads();
@@ -594,8 +589,8 @@ size_t gemv_tile_smem_bytes(int M, int K, int S) { return static_cast<size_t>(ti
 bool gemv_tile_supported(int M, int K, int S) {
     if (M < 1 || M > 8 || S < 1 || S > 8 || (S & (S - 1)) != 0) return false;
     if (K <= 0 || K % (kTBoxK * S) != 0) return false;
-    // the mma path (M >= 7) converts X with at most 8 chunks of 8 k per thread
-    if (M >= 7 && static_cast<long long>(M) * (K / S) > 8LL * kMmaMaxChunksPerThread * 512) return false;
+    // the mma path (M >= 5) holds at most 16 float4 of X per thread while converting it
+    if (M >= 5 && static_cast<long long>(M) * (K / S) > 16LL * 4 * 512) return false;
     return gemv_tile_smem_bytes(M, K, S) <= 227 * 1024;
 }
 
