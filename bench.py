@@ -843,7 +843,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "lora", "tiny", "mlp70b"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "lora", "tiny", "mlp70b", "lora_backward"],
+                    default="decode")
     ap.add_argument("--no-secondary", action="store_true", help="skip the prefill/lora figures")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()
@@ -928,6 +929,14 @@ def main() -> None:
                                 "exchange": r["detail"].get("exchange", "none"),
                                 "l2": "L2 flushed (256 MB write) before every step"},
                      "detail": r["detail"], "parity": r["parity"]})
+    elif args.workload == "lora_backward":
+        r = lora_backward_gpu(args, dist, torch, session, synth, peaks)
+        big = r["configs4_size"]
+        line.update({"value": big["GB/s"], "unit": "GB/s", "ms_per_step": big["us"] / 1e3, "scaling": "weak",
+                     "dtype": "f32 (3xTF32-accurate tcgen05)",
+                     "config": {"workload": "LoRA backward (T, G, dB, dA) at configs[4]'s size, rank 16",
+                                "l2": "L2 flushed (256 MB write) before every step", "parallelism": "single GPU"},
+                     "detail": r})
     else:
         r = gemm_gpu(args, dist, torch, session, synth, peaks, args.workload)
         line.update({"value": r["TFLOP/s"], "unit": "TFLOP/s", "ms_per_step": r["ms"], "scaling": "weak",
