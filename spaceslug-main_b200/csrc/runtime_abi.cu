@@ -1375,10 +1375,14 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
         char* stage = static_cast<char*>(host_staging(c, yoff + yb));
         float* dx = reinterpret_cast<float*>(stage);
         float* dy = reinterpret_cast<float*>(stage + yoff);
-        // Pinned (mapped) host buffers move by small kernels over the bus, the
-        // status word with Y; pageable ones by copy-engine transfers.
-        const float* xmap = static_cast<const float*>(mapped_device_pointer(x));
-        float* ymap = static_cast<float*>(mapped_device_pointer(y));
+        // Small pinned (mapped) host buffers move by copy kernels over the bus,
+        // the status word with Y: a copy-engine transfer of a few kilobytes
+        // costs ~8 us.  Pageable buffers, and pinned ones above
+        // kZeroCopyMaxBytes (prefill-sized X and Y, where the copy engine's
+        // bandwidth matters more than its latency), take copy-engine transfers.
+        constexpr size_t kZeroCopyMaxBytes = size_t(1) << 20;
+        const float* xmap = xb <= kZeroCopyMaxBytes ? static_cast<const float*>(mapped_device_pointer(x)) : nullptr;
+        float* ymap = yb <= kZeroCopyMaxBytes ? static_cast<float*>(mapped_device_pointer(y)) : nullptr;
         if (xmap)
             check_launch(q4::launch_copy_words(xmap, dx, static_cast<long long>(m) * w->K, nullptr, nullptr, c.stream),
                          "copy X in");

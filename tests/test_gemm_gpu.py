@@ -275,11 +275,13 @@ def test_run_push_stores_the_same_block_into_every_peer_buffer(session, cuda, m,
         assert np.array_equal(b.cpu().numpy().view(np.uint32), want)
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 1000, 1024), (64, 4500, 1152), (3, 37, 64)])
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 1000, 1024), (64, 4500, 1152), (3, 37, 64),
+                                   (512, 1024, 1024)])
 def test_run_host_pinned_buffers_match_pageable(session, cuda, m, n, k):
-    """spaceslug_q4_weights_run_host moves pinned (device-mapped) X and Y by
-    small kernels and pageable ones by copy-engine transfers: both give the
-    same Y, bit for bit, and a clean status."""
+    """spaceslug_q4_weights_run_host moves pinned (device-mapped) X and Y of at
+    most 1 MiB by small kernels, and pageable or larger ones by copy-engine
+    transfers (the last case: 2 MiB each): all give the same Y, bit for bit,
+    and a clean status."""
     import ctypes
     import torch
     w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=n + k)
