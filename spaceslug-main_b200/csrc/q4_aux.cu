@@ -402,6 +402,57 @@ int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t
     return static_cast<int>(cudaGetLastError());
 }
 
+namespace {
+
+// Y[m][n] += s * sum_j T[m][j] B[j][n], the LoRA term of a split-K GEMM whose
+// K halves left it out (the term is then added once, after both halves, in
+// the same fp32 form as the GEMM epilogue's: d = sum over j in order, y += s d).
+// Block (x, m): row m, columns [1024 x, 1024 x + 1024), four per thread.
+__global__ void __launch_bounds__(256) lora_add_kernel(const float* __restrict__ t, const float* __restrict__ b,
+                                                       float* __restrict__ y, int N, long long ld, int rank, float s,
+                                                       int vec4) {
+    __shared__ float ts[64];
+    const int m = blockIdx.y;
+    if (threadIdx.x < rank) ts[threadIdx.x] = t[static_cast<size_t>(m) * rank + threadIdx.x];
+    __syncthreads();
+    const int n0 = blockIdx.x * 1024 + threadIdx.x * 4;
+    float* yr = y + static_cast<size_t>(m) * ld;
+    if (vec4 && n0 + 4 <= N) {
+        float4 d = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j = 0; j < rank; ++j) {
+            const float4 bv = *reinterpret_cast<const float4*>(b + static_cast<size_t>(j) * N + n0);
+            d.x = fmaf(ts[j], bv.x, d.x);
+            d.y = fmaf(ts[j], bv.y, d.y);
+            d.z = fmaf(ts[j], bv.z, d.z);
+            d.w = fmaf(ts[j], bv.w, d.w);
+        }
+        float4 v = *reinterpret_cast<float4*>(yr + n0);
+        v.x = fmaf(s, d.x, v.x);
+        v.y = fmaf(s, d.y, v.y);
+        v.z = fmaf(s, d.z, v.z);
+        v.w = fmaf(s, d.w, v.w);
+        *reinterpret_cast<float4*>(yr + n0) = v;
+    } else {
+        for (int n = n0; n < n0 + 4 && n < N; ++n) {
+            float d = 0.0f;
+            for (int j = 0; j < rank; ++j) d = fmaf(ts[j], b[static_cast<size_t>(j) * N + n], d);
+            yr[n] = fmaf(s, d, yr[n]);
+        }
+    }
+}
+
+}  // namespace
+
+int launch_lora_add(const float* t, const float* b, float* y, int M, int N, long long ld, int rank, float s,
+                    cudaStream_t stream) {
+    if (M < 1 || N < 1 || rank < 1 || rank > 64 || ld < N) return static_cast<int>(cudaErrorInvalidValue);
+    const bool vec4 = N % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+    const dim3 grid(static_cast<unsigned>((N + 1023) / 1024), static_cast<unsigned>(M));
+    lora_add_kernel<<<grid, 256, 0, stream>>>(t, b, y, N, ld, rank, s, vec4 ? 1 : 0);
+    return static_cast<int>(cudaGetLastError());
+}
+
 int lora_xa_chunks(int K) { return (K + kXaChunk - 1) / kXaChunk; }
 
 int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,

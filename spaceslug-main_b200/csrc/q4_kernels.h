@@ -171,6 +171,10 @@ int launch_pack(const int8_t* b_kn, uint32_t* packed, int K, int N, cudaStream_t
 int launch_lora_xa(const float* x, const float* a, float* t, int M, int K, int rank, cudaStream_t stream,
                    float* partial = nullptr, const int* row_exp = nullptr, uint16_t* t_op_bits = nullptr);
 int lora_xa_chunks(int K);
+// Y[m][n] (row pitch ld) += s * T[m][:] . B[:][n] (B [rank][N], rank <= 64):
+// the LoRA term of a split-K GEMM that left it out of its epilogue.
+int launch_lora_add(const float* t, const float* b, float* y, int M, int N, long long ld, int rank, float s,
+                    cudaStream_t stream);
 // All-gathered column shards [parts][rows][width] (rank-major) -> rows
 // [rows][ld_y] of row-major Y, columns [0, n_total) (the last shard may be
 // partly padding).  HBM-bound copy; float4 when every address is aligned.
