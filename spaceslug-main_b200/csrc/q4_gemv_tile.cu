@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(TileCfg<M>::kThreads, (M <= 2 ? 2 : 1))
             const uint8_t* wcol = smem + L.w_off + b * kTSlot * 128 + g * 128;  // column 8o + g at + o * 1024
             const uint8_t* sbx = smem + L.s_off + (b >> 2) * kTSlot * 128;
             const int schunk0 = (b & 3) * 2;
-#pragma unroll 2
+#pragma unroll  // all eight groups in flight: 3.26 against 3.6 us per layer with two (M = 8, in the graph)
             for (int t = 0; t < 8; ++t) {
                 // A fragments of this 32-k group: chunks c0 .. c0 + 3 of the row
                 const uint32_t c0 = static_cast<uint32_t>(b * 32 + t * 4);
