@@ -33,6 +33,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "common.cuh"
@@ -550,8 +551,18 @@ int launch_tile_m(const GemvTileArgs& a, cudaStream_t stream) {
     const TileLayout L = tile_layout(M, a.K, a.cluster_k);
     const size_t smem = static_cast<size_t>(L.bytes);
     auto kern = q4_gemv_tile_kernel<M>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    // The shared-memory allowance is set once per device (to the largest
+    // layout this kernel takes), not per call: the attribute call costs about
+    // a microsecond of host time, a fifth of a layer at M = 1.
+    static std::atomic<bool> attr_done[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_cast<int>(e);
+    if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        if (dev >= 0 && dev < 64) attr_done[dev].store(true, std::memory_order_release);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(a.col_blocks * a.cluster_k));
     cfg.blockDim = dim3(TileCfg<M>::kThreads);

@@ -208,12 +208,19 @@ const char* shape_error(const void* x, const void* packed, const void* scales, c
 }
 
 // --------------------------------------------------------------- dispatch --
-// Tensor maps of a weight handle's decode launches (integer-MMA GEMV), encoded
-// once per geometry instead of once per call.
+// Tensor maps of a weight handle's decode launches, encoded once per
+// geometry instead of once per call: the integer-MMA GEMV's weight and scale
+// maps, the whole-tile GEMV's, and the tile GEMV's last X map (the host-pointer
+// calls stage X in a per-device buffer, so its address repeats call after call).
 struct DecodeMapCache {
     std::mutex mu;
-    int S = 0, T = 0;  // geometry the maps were encoded for (0: none yet)
+    int S = 0, T = 0;  // geometry the integer-MMA maps were encoded for (0: none yet)
     CUtensorMap w{}, s{};
+    uint32_t tile_rows = 0;  // box rows the whole-tile maps were encoded for (0: none yet)
+    CUtensorMap tile_w{}, tile_s{};
+    const void* x_ptr = nullptr;  // the X the cached X map describes, with its M and K split
+    int x_m = 0, x_split = 0;
+    CUtensorMap tile_x{};
 };
 
 struct Problem {
@@ -568,15 +575,38 @@ void run_problem(const Problem& p, cudaStream_t stream) {
             const int K = p.K, N = p.N;
             a.col_blocks = q4::gemv_tile_col_blocks(N, c.sm_count);
             const uint32_t rows = static_cast<uint32_t>(q4::gemv_tile_box_rows(N, a.col_blocks));
-            encode_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(K) / 8,
-                      static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, 32, rows, CU_TENSOR_MAP_SWIZZLE_128B);
-            encode_2d(&a.tmap_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.scales, static_cast<uint64_t>(K) / 32,
-                      static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 8,
-                      static_cast<uint32_t>(q4::gemv_tile_scale_box_groups()), rows, CU_TENSOR_MAP_SWIZZLE_128B);
+            auto encode_ws = [&](CUtensorMap* mw, CUtensorMap* ms) {
+                encode_2d(mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.packed, static_cast<uint64_t>(K) / 8,
+                          static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 2, 32, rows, CU_TENSOR_MAP_SWIZZLE_128B);
+                encode_2d(ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.scales, static_cast<uint64_t>(K) / 32,
+                          static_cast<uint64_t>(N), static_cast<uint64_t>(K) / 8,
+                          static_cast<uint32_t>(q4::gemv_tile_scale_box_groups()), rows, CU_TENSOR_MAP_SWIZZLE_128B);
+            };
             const int bk = q4::gemv_tile_box_k();
-            encode_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.x, static_cast<uint64_t>(bk),
-                      static_cast<uint64_t>(p.M) * (K / bk), static_cast<uint64_t>(bk) * 4,
-                      static_cast<uint32_t>(bk), static_cast<uint32_t>(K / S / bk), CU_TENSOR_MAP_SWIZZLE_NONE);
+            auto encode_x = [&](CUtensorMap* mx) {
+                encode_2d(mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.x, static_cast<uint64_t>(bk),
+                          static_cast<uint64_t>(p.M) * (K / bk), static_cast<uint64_t>(bk) * 4,
+                          static_cast<uint32_t>(bk), static_cast<uint32_t>(K / S / bk), CU_TENSOR_MAP_SWIZZLE_NONE);
+            };
+            if (p.maps != nullptr) {
+                std::lock_guard<std::mutex> lk(p.maps->mu);
+                if (p.maps->tile_rows != rows) {
+                    encode_ws(&p.maps->tile_w, &p.maps->tile_s);
+                    p.maps->tile_rows = rows;
+                }
+                if (p.maps->x_ptr != p.x || p.maps->x_m != p.M || p.maps->x_split != S) {
+                    encode_x(&p.maps->tile_x);
+                    p.maps->x_ptr = p.x;
+                    p.maps->x_m = p.M;
+                    p.maps->x_split = S;
+                }
+                a.tmap_w = p.maps->tile_w;
+                a.tmap_s = p.maps->tile_s;
+                a.tmap_x = p.maps->tile_x;
+            } else {
+                encode_ws(&a.tmap_w, &a.tmap_s);
+                encode_x(&a.tmap_x);
+            }
             a.y = p.y;
             a.M = p.M; a.N = N; a.K = K;
             a.cluster_k = S;
