@@ -290,16 +290,19 @@ class ShardedGemmPush:
         return self.y
 
 
-# The exchange each world size uses, chosen from measurements of configs[4]
-# (X 4096 x 8192, W 8192 x 28672, fp32 Y of 470 MB) on B200 boxes of this
-# kind, each step timed with the L2 flushed (step times of the fastest
-# variant, in ms, at P = 2 / 4 / 8: 0.82 / 0.71 / 0.77):
-#   P = 2: the GEMM epilogue pushes every finished block to the one peer;
-#   P = 4, 8: banded GEMM with an SM push kernel beside it on 16 / 24 SMs.
+# The exchange each world size uses when the caller gives no X to time
+# candidates on, chosen from measurements of configs[4] (X 4096 x 8192,
+# W 8192 x 28672, fp32 Y of 470 MB) on B200 boxes of this kind, each step
+# timed with the L2 flushed:
+#   P = 2, 4: the GEMM epilogue pushes every finished block to the peers once
+#     the accumulator is back with the MMA (0.82 / 0.67 ms per step; the SM
+#     push: 1.00 / 0.73 ms);
+#   P = 8: banded GEMM with an SM push kernel beside it on 24 SMs (0.77 ms,
+#     measured before the epilogue push handed the accumulator back first).
 # A P not listed takes the nearest listed one below it.
 EXCHANGE_BY_WORLD = {
     2: {"engine": "epilogue", "bands": 1, "push_sms": 16},
-    4: {"engine": "sm", "bands": 4, "push_sms": 16},
+    4: {"engine": "epilogue", "bands": 1, "push_sms": 16},
     8: {"engine": "sm", "bands": 4, "push_sms": 24},
 }
 
