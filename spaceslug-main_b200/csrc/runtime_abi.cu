@@ -67,6 +67,7 @@ struct DeviceCtx {
     std::mutex host_mu;             // serialises use of `stream` and `hbuf` by host entry points
     void* hbuf = nullptr;           // device staging of X and Y for spaceslug_q4_weights_run_host (grows)
     size_t hbuf_bytes = 0;
+    uint64_t hbuf_gen = 0;          // bumped whenever hbuf is replaced (graphs of host calls name it)
     int max_pairs[2] = {-1, -1};    // co-resident CTA pairs of the pair GEMM, per operand type
     std::mutex pair_mu;
     cudaStream_t aux = nullptr;     // lowest-priority helper stream for work forked off a call (lazy)
@@ -812,6 +813,7 @@ void* host_staging(DeviceCtx& c, size_t bytes) {
         const size_t want = std::max(bytes, static_cast<size_t>(1) << 20);
         check(cudaMalloc(&c.hbuf, want), "cudaMalloc host-call staging");
         c.hbuf_bytes = want;
+        ++c.hbuf_gen;
     }
     return c.hbuf;
 }
@@ -885,12 +887,34 @@ struct spaceslug_q4_weights {
     float alpha = 0.0f;
     int sm_budget = 0;  // SMs a GEMM launch of this handle may occupy (0: all)
     DecodeMapCache decode_maps;  // tensor maps of its decode launches
+    // Host-pointer calls with small pinned X and Y, captured once as a CUDA
+    // graph (copy in, GEMV, copy out) and replayed: one graph launch instead
+    // of three kernel launches per call.  Keyed by everything the captured
+    // launches name; set_lora and destroy drop them.
+    struct HostGraph {
+        const float* x;
+        float* y;
+        const float* xmap;
+        float* ymap;
+        uint32_t m;
+        int variant;
+        uint64_t gen;
+        cudaGraphExec_t exec;
+    };
+
+    std::vector<HostGraph> host_graphs;
     // training state (allocated on first use, reset by set_lora)
     float* lora_da = nullptr;
     float* lora_db = nullptr;
     float* adam = nullptr;  // first and second moments of A then of B: 2 * (K*r + r*N)
     int adam_step = 0;
 };
+
+// Caller holds the device's host_mu (or owns the handle exclusively).
+void drop_host_graphs(spaceslug_q4_weights* w) {
+    for (auto& g : w->host_graphs) cudaGraphExecDestroy(g.exec);
+    w->host_graphs.clear();
+}
 
 // CQ4 (Cactus-Quants) matrix on one device: the indices repacked to the q4
 // nibble order ([N][K/2] bytes), the norms expanded to one value per 32-k
@@ -1248,6 +1272,12 @@ int spaceslug_q4_weights_set_lora(spaceslug_q4_weights* w, const float* lora_a, 
         return fail(SPACESLUG_INVALID_ARGUMENT, "LoRA needs A, B and a finite alpha");
     return guarded([&] {
         check(cudaSetDevice(w->device), "cudaSetDevice");
+        {
+            // graphs of host calls name the old adapter's buffers and scale
+            DeviceCtx& c = ctx_for(w->device);
+            std::lock_guard<std::mutex> lk(c.host_mu);
+            drop_host_graphs(w);
+        }
         cudaFree(w->lora_a);
         cudaFree(w->lora_b);
         cudaFree(w->lora_da);
@@ -1463,22 +1493,69 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
         constexpr size_t kZeroCopyMaxBytes = size_t(1) << 20;
         const float* xmap = xb <= kZeroCopyMaxBytes ? static_cast<const float*>(mapped_device_pointer(x)) : nullptr;
         float* ymap = yb <= kZeroCopyMaxBytes ? static_cast<float*>(mapped_device_pointer(y)) : nullptr;
-        if (xmap)
-            check_launch(q4::launch_copy_words(xmap, dx, static_cast<long long>(m) * w->K, nullptr, nullptr, c.stream),
-                         "copy X in");
-        else
-            h2d(dx, x, xb, c.stream);
-        Problem p{dx, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, dy,
-                  static_cast<int>(m), w->N, w->K};
-        p.sm_budget = w->sm_budget;
-        p.maps = &w->decode_maps;
-        run_problem(p, c.stream);
-        if (ymap)
-            check_launch(q4::launch_copy_words(dy, ymap, static_cast<long long>(m) * w->N, c.status, c.status_host_dev,
-                                               c.stream),
-                         "copy Y out");
-        else
-            d2h(y, dy, yb, c.stream);
+        auto issue = [&] {
+            if (xmap)
+                check_launch(q4::launch_copy_words(xmap, dx, static_cast<long long>(m) * w->K, nullptr, nullptr,
+                                                   c.stream),
+                             "copy X in");
+            else
+                h2d(dx, x, xb, c.stream);
+            Problem p{dx, w->packed, w->scales, w->col_exp, w->lora_a, w->lora_b, w->rank, w->alpha, dy,
+                      static_cast<int>(m), w->N, w->K};
+            p.sm_budget = w->sm_budget;
+            p.maps = &w->decode_maps;
+            run_problem(p, c.stream);
+            if (ymap)
+                check_launch(q4::launch_copy_words(dy, ymap, static_cast<long long>(m) * w->N, c.status,
+                                                   c.status_host_dev, c.stream),
+                             "copy Y out");
+            else
+                d2h(y, dy, yb, c.stream);
+        };
+        const int variant = decode_variant_init().load();
+        if (xmap && ymap && m <= 8) {
+            // decode-sized call with pinned buffers: replay (or capture) its graph
+            cudaGraphExec_t exec = nullptr;
+            for (auto& g : w->host_graphs)
+                if (g.x == x && g.y == y && g.xmap == xmap && g.ymap == ymap && g.m == m && g.variant == variant &&
+                    g.gen == c.hbuf_gen) {
+                    exec = g.exec;
+                    break;
+                }
+            if (exec == nullptr) {
+                // Capture once; anything the capture does not take (it should
+                // take all of it) falls back to direct launches for this call.
+                cudaGraph_t graph = nullptr;
+                bool captured = false;
+                if (cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+                    try {
+                        issue();
+                        captured = true;
+                    } catch (...) {
+                    }
+                    if (cudaStreamEndCapture(c.stream, &graph) != cudaSuccess) captured = false;
+                    if (captured && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+                        captured = false;
+                        exec = nullptr;
+                    }
+                    if (graph) cudaGraphDestroy(graph);
+                }
+                cudaGetLastError();  // a failed capture leaves no sticky error behind
+                if (captured) {
+                    if (w->host_graphs.size() >= 8) {  // keep the most recent few buffer pairs
+                        cudaGraphExecDestroy(w->host_graphs.front().exec);
+                        w->host_graphs.erase(w->host_graphs.begin());
+                    }
+                    w->host_graphs.push_back({x, y, xmap, ymap, m, variant, c.hbuf_gen, exec});
+                }
+            }
+            if (exec != nullptr)
+                check(cudaGraphLaunch(exec, c.stream), "cudaGraphLaunch");
+            else
+                issue();
+        } else {
+            issue();
+        }
         if (take_status(c, c.stream, ymap != nullptr)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
         return SPACESLUG_OK;
     });
@@ -1487,6 +1564,11 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
 int spaceslug_q4_weights_destroy(spaceslug_q4_weights* w) {
     if (!w) return fail(SPACESLUG_INVALID_ARGUMENT, "null handle");
     cudaSetDevice(w->device);
+    {
+        DeviceCtx& c = g_ctx[w->device];
+        std::lock_guard<std::mutex> lk(c.host_mu);
+        drop_host_graphs(w);
+    }
     cudaFree(w->packed);
     cudaFree(w->scales);
     cudaFree(w->col_exp);
