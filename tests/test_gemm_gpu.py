@@ -275,6 +275,45 @@ def test_run_push_stores_the_same_block_into_every_peer_buffer(session, cuda, m,
         assert np.array_equal(b.cpu().numpy().view(np.uint32), want)
 
 
+def test_run_host_pinned_replays_follow_adapter_and_variant(session, oracle, cuda):
+    """Decode-sized host calls with pinned X and Y replay a captured graph:
+    after set_lora (new adapter, new scale) and a decode-variant switch the
+    replays must give the new results, equal to the pageable path's."""
+    import ctypes
+    import torch
+    m, n, k, rank = 2, 512, 1024, 8
+    w_kn, packed, scales = synth.make_weights(k, n, 0.005, 0.02, seed=21)
+    x = synth.make_x(m, k, seed=22)
+    fp = ctypes.POINTER(ctypes.c_float)
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.empty((m, n), dtype=torch.float32).pin_memory()
+    run_host = session.raw("spaceslug_q4_weights_run_host")
+    with session.weights(packed, scales, k, n) as h:
+        def pinned():
+            assert run_host(h.handle, ctypes.cast(xh.data_ptr(), fp), ctypes.cast(yh.data_ptr(), fp), m) == 0
+            return yh.numpy().copy()
+        base = [pinned() for _ in range(2)]
+        assert np.array_equal(base[0], base[1]) and np.array_equal(base[0], h.run_host(x))
+        for seed, alpha in ((23, 16.0), (24, 4.0)):
+            a = synth.normal(k * rank, seed, 0.02).reshape(k, rank)
+            b = synth.normal(rank * n, seed + 100, 0.02).reshape(rank, n)
+            h.set_lora(a, b, alpha)
+            got = [pinned() for _ in range(2)]
+            assert np.array_equal(got[0], got[1]) and np.array_equal(got[0], h.run_host(x))
+            ref = oracle.gemm(x, w_kn, scales)
+            oracle.lora_add(ref, x, a, b, alpha)
+            rep = parity.compare_float_arrays(got[0], ref, tolerance=parity.GEMV_REL_TOL)
+            assert rep["status"] == "pass", rep
+        prev = session.set_decode_variant("gemv")
+        try:
+            ring = pinned()
+            assert np.array_equal(ring, h.run_host(x))
+        finally:
+            session.set_decode_variant(prev)
+        assert np.array_equal(pinned(), got[0])
+    assert session.device_status(0) == 0
+
+
 @pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 1000, 1024), (64, 4500, 1152), (3, 37, 64),
                                    (512, 1024, 1024)])
 def test_run_host_pinned_buffers_match_pageable(session, cuda, m, n, k):
