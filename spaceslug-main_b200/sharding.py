@@ -297,13 +297,14 @@ class ShardedGemmPush:
 #   P = 2, 4: the GEMM epilogue pushes every finished block to the peers once
 #     the accumulator is back with the MMA (0.82 / 0.67 ms per step; the SM
 #     push: 1.00 / 0.73 ms);
-#   P = 8: banded GEMM with an SM push kernel beside it on 24 SMs (0.77 ms,
-#     measured before the epilogue push handed the accumulator back first).
+#   P = 8: banded GEMM with an SM push kernel beside it (0.776 ms on 16 SMs,
+#     0.786 on 24; the epilogue push 0.788): bound by the 411 MB of Y each GPU
+#     receives.
 # A P not listed takes the nearest listed one below it.
 EXCHANGE_BY_WORLD = {
     2: {"engine": "epilogue", "bands": 1, "push_sms": 16},
     4: {"engine": "epilogue", "bands": 1, "push_sms": 16},
-    8: {"engine": "sm", "bands": 4, "push_sms": 24},
+    8: {"engine": "sm", "bands": 4, "push_sms": 16},
 }
 
 
