@@ -14,16 +14,14 @@
 // lora_tc_kernel<RP, MN> runs all four:
 //
 //  - Aop is TMA-loaded in tiles of 128 rows x 32 l straight from X or dY,
-//    either with the rows of D as the source's rows (T and G: l contiguous)
-//    or with the rows of D contiguous in the source (dB reads dY^T and dA
-//    reads X^T: four 32 x 32 boxes per tile).
-//  - Four split warps turn each loaded tile into TF32 hi (rounded to nearest)
-//    and lo = x - hi (exact in fp32) in shared memory, K-major and
-//    128-byte-swizzled for the MMA: in place for the first kind; for the
-//    second, through 4 x 4 register transposes from the loaded tile into two
-//    further tiles (the MMA's MN-major TF32 operand form needs another
-//    swizzle layout, so the transpose happens here).  Neither the split nor a
-//    transpose ever passes through HBM.
+//    either with the rows of D as the source's rows (T and G: l contiguous,
+//    a K-major operand, 128-byte swizzle) or with the rows of D contiguous in
+//    the source (dB reads dY^T and dA reads X^T: four boxes of 32 rows x 32 l,
+//    an MN-major operand in the 128-byte swizzle of 32-byte atoms, the
+//    swizzled layout MN-major TF32 operands take).  No transpose anywhere.
+//  - Four split warps turn each loaded tile into TF32 hi (rounded to nearest,
+//    in place) and lo = x - hi (exact in fp32, same offsets in a second tile):
+//    the split is elementwise, so it keeps whichever layout the tile has.
 //  - Bop is prepared once per contraction as stacked planes [2RP][L]: rows
 //    0..RP-1 its TF32 hi parts, rows RP..2RP-1 its lo parts, rows >= r zero.
 //    Two MMAs per 8 l, Aop_hi x [B_hi; B_lo] and Aop_lo x [B_hi; B_lo]
@@ -55,24 +53,21 @@ namespace {
 
 constexpr int kLtRows = 128;      // rows of D per unit (the MMA's M)
 constexpr int kLtL = 32;          // contraction elements per stage: one 128-byte fp32 row
-// Warps: 0 TMA, 1 and 10 MMA, 4-7 epilogue, split: 2-3 and 8-9, plus 11-14
-// for the transposing split (MN), which costs about twice as much per stage.
-template <bool MN>
-__host__ __device__ constexpr int lt_split_warps() { return MN ? 8 : 4; }
-template <bool MN>
-__host__ __device__ constexpr int lt_threads() { return MN ? 480 : 352; }
-__device__ __forceinline__ int lt_split_index(int warp) {  // split warp -> 0..7, else -1
-    return (warp == 2 || warp == 3) ? warp - 2 : (warp == 8 || warp == 9) ? warp - 6 : warp >= 11 ? warp - 7 : -1;
+// Warps: 0 TMA, 1 and 10 MMA, 2-3 and 8-9 split, 4-7 epilogue.
+constexpr int kLtSplitWarps = 4;
+constexpr int kLtThreads = 352;
+__device__ __forceinline__ int lt_split_index(int warp) {  // split warp -> 0..3, else -1
+    return (warp == 2 || warp == 3) ? warp - 2 : (warp == 8 || warp == 9) ? warp - 6 : -1;
 }
 constexpr int kLtATile = kLtRows * kLtL * 4;  // 16 KB
+constexpr int kLtMnBox = 32 * kLtL * 4;       // one MN-major box: 32 rows of D x 32 l, 4 KB
 
 template <int RP, bool MN>
 struct LtCfg {
     static constexpr int kBTile = 2 * RP * kLtL * 4;  // stacked hi / lo rows of Bop
     static constexpr int kBTileAligned = (kBTile + 1023) / 1024 * 1024;
-    // stage: [loaded Aop (MN only)] [Aop hi] [Aop lo] [Bop]; without MN the hi tile is the loaded one
-    static constexpr int kHi = MN ? kLtATile : 0;
-    static constexpr int kLo = kHi + kLtATile;
+    // stage: [Aop as loaded, then its hi part] [Aop lo] [Bop]
+    static constexpr int kLo = kLtATile;
     static constexpr int kB = kLo + kLtATile;
     static constexpr int kStageBytes = kB + kBTileAligned;
     static constexpr int kBudget = 222 * 1024;
@@ -108,7 +103,7 @@ __device__ __forceinline__ LtUnit lt_unit(const LoraTcPass& P, int u) {
 }
 
 template <int RP, bool MN>
-__global__ void __launch_bounds__(lt_threads<MN>(), 1)
+__global__ void __launch_bounds__(kLtThreads, 1)
     lora_tc_kernel(const __grid_constant__ LoraTcPass P) {
     using C = LtCfg<RP, MN>;
     extern __shared__ uint8_t smem_raw[];
@@ -130,7 +125,7 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
     if (tid == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(split(s), lt_split_warps<MN>());
+            mbar_init(split(s), kLtSplitWarps);
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) mbar_init(chunk_empty(b), 4);  // one arrival per epilogue warp
@@ -176,7 +171,7 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
                     if constexpr (MN) {
                         // four boxes of 32 rows of D x 32 l (l = the box's row), 4 KB apart
 #pragma unroll
-                        for (int b = 0; b < 4; ++b) tma_load_2d(a + b * 4096, tm_a, full(s), row0 + 32 * b, l0);
+                        for (int b = 0; b < 4; ++b) tma_load_2d(a + b * kLtMnBox, tm_a, full(s), row0 + 32 * b, l0);
                     } else {
                         tma_load_2d(a, tm_a, full(s), l0, row0);
                     }
@@ -197,7 +192,7 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
             // per stage tells both the producer (the stage may be refilled) and
             // the epilogue (the chunk's sums are complete).
             const int par = warp == 1 ? 0 : 1;
-            constexpr uint32_t idesc = umma_idesc_tf32(kLtRows, 2 * RP);
+            constexpr uint32_t idesc = umma_idesc_tf32(kLtRows, 2 * RP, MN);
             int total = 0;
             for (int u = blockIdx.x; u < units; u += gridDim.x) {
                 const LtUnit w = lt_unit(P, u);
@@ -212,12 +207,16 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
                 if (!mbar_wait(split(s), (q / C::kStages) & 1u, abort_flag, status, kStatusTimeoutMma)) break;
                 tc_fence_after_sync();
                 const uint32_t st_base = base + s * C::kStageBytes;
-                const uint32_t a_hi = st_base + C::kHi, a_lo = st_base + C::kLo, bt = st_base + C::kB;
+                const uint32_t a_hi = st_base, a_lo = st_base + C::kLo, bt = st_base + C::kB;
 #pragma unroll
-                for (int kk = 0; kk < kLtL / 8; ++kk) {  // 8 tf32 = 32 bytes of each 128-byte row
+                for (int kk = 0; kk < kLtL / 8; ++kk) {  // K = 8: 32 bytes of each K-major row, 8 rows of MN-major
                     const uint64_t bd = umma_desc_k_sw128(bt + kk * 32);
-                    umma_tf32_ss(dacc, umma_desc_k_sw128(a_hi + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
-                    umma_tf32_ss(dacc, umma_desc_k_sw128(a_lo + kk * 32), bd, idesc, 1u);
+                    const uint64_t ah = MN ? umma_desc_mn_sw128_32b(a_hi + kk * 1024, kLtMnBox)
+                                           : umma_desc_k_sw128(a_hi + kk * 32);
+                    const uint64_t al = MN ? umma_desc_mn_sw128_32b(a_lo + kk * 1024, kLtMnBox)
+                                           : umma_desc_k_sw128(a_lo + kk * 32);
+                    umma_tf32_ss(dacc, ah, bd, idesc, kk > 0 ? 1u : 0u);
+                    umma_tf32_ss(dacc, al, bd, idesc, 1u);
                 }
                 umma_commit(empty(s));
                 last = q;
@@ -280,9 +279,9 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
         }
     } else if (lt_split_index(warp) >= 0) {
         // ----------------------------------------------------------- split --
-        // Warps 2, 3, 8, 9 write each stage's Aop as K-major TF32 hi and lo
-        // tiles (rows of D at 128 B, 16-byte chunk c of row m at c ^ (m & 7)).
-        constexpr int kSplitThreads = lt_split_warps<MN>() * 32;
+        // Warps 2, 3, 8, 9 overwrite each stage's loaded Aop tile with its TF32
+        // hi parts and write the lo parts at the same offsets of the next tile.
+        constexpr int kSplitThreads = kLtSplitWarps * 32;
         const int ct = lt_split_index(warp) * 32 + lane;  // 0 .. kSplitThreads - 1
         int q = 0;
         bool ok = true;
@@ -295,52 +294,17 @@ __global__ void __launch_bounds__(lt_threads<MN>(), 1)
                     break;
                 }
                 uint8_t* stage = smem + s * C::kStageBytes;
-                if constexpr (MN) {
-                    // Loaded: box b (rows 32b..32b+31 of D) at 4 KB b, l at 128 B l, chunk (row / 4 % 8) ^ (l & 7).
-                    // Each thread moves two 4 x 4 blocks (rows 4c.., l 4d..): four 16-byte reads, a register
-                    // transpose, four 16-byte writes per plane.  A phase of 8 lanes spans 4 c and 2 d, so its
-                    // reads hit 8 distinct chunk positions and its writes 4.
+                float4* hi = reinterpret_cast<float4*>(stage);
+                float4* lo = reinterpret_cast<float4*>(stage + C::kLo);
+                constexpr int kPer = kLtATile / 16 / kSplitThreads;  // 8 float4 per thread
+                float4 v[kPer];
 #pragma unroll
-                    for (int rep = 0; rep < 256 / kSplitThreads; ++rep) {
-                        const int k = ct + kSplitThreads * rep, p = k >> 3, qq = k & 7;
-                        const int c = (qq & 3) + 4 * (p & 7);     // rows 4c..4c+3 of D
-                        const int d = (qq >> 2) + 2 * (p >> 3);   // l = 4d..4d+3
-                        float4 v[4];
+                for (int i = 0; i < kPer; ++i) v[i] = hi[ct + kSplitThreads * i];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int l = 4 * d + i;
-                            v[i] = *reinterpret_cast<const float4*>(stage + 4096 * (c >> 3) + 128 * l +
-                                                                    (((c & 7) ^ (l & 7)) << 4));
-                        }
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) {
-                            const int row = 4 * c + jj;
-                            const float4 x = jj == 0   ? make_float4(v[0].x, v[1].x, v[2].x, v[3].x)
-                                             : jj == 1 ? make_float4(v[0].y, v[1].y, v[2].y, v[3].y)
-                                             : jj == 2 ? make_float4(v[0].z, v[1].z, v[2].z, v[3].z)
-                                                       : make_float4(v[0].w, v[1].w, v[2].w, v[3].w);
-                            const float4 h = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
-                            const int off = 128 * row + ((d ^ (row & 7)) << 4);
-                            *reinterpret_cast<float4*>(stage + C::kHi + off) = h;
-                            *reinterpret_cast<float4*>(stage + C::kLo + off) =
-                                make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-                        }
-                    }
-                } else {
-                    // Loaded K-major already: hi in place, lo at the same offsets (so the same swizzle).
-                    float4* hi = reinterpret_cast<float4*>(stage + C::kHi);
-                    float4* lo = reinterpret_cast<float4*>(stage + C::kLo);
-                    constexpr int kPer = kLtATile / 16 / kSplitThreads;  // 8 float4 per thread
-                    float4 v[kPer];
-#pragma unroll
-                    for (int i = 0; i < kPer; ++i) v[i] = hi[ct + kSplitThreads * i];
-#pragma unroll
-                    for (int i = 0; i < kPer; ++i) {
-                        const float4 h =
-                            make_float4(to_tf32(v[i].x), to_tf32(v[i].y), to_tf32(v[i].z), to_tf32(v[i].w));
-                        hi[ct + kSplitThreads * i] = h;
-                        lo[ct + kSplitThreads * i] = make_float4(v[i].x - h.x, v[i].y - h.y, v[i].z - h.z, v[i].w - h.w);
-                    }
+                for (int i = 0; i < kPer; ++i) {
+                    const float4 h = make_float4(to_tf32(v[i].x), to_tf32(v[i].y), to_tf32(v[i].z), to_tf32(v[i].w));
+                    hi[ct + kSplitThreads * i] = h;
+                    lo[ct + kSplitThreads * i] = make_float4(v[i].x - h.x, v[i].y - h.y, v[i].z - h.z, v[i].w - h.w);
                 }
                 fence_proxy_async_smem();  // the MMAs (async proxy) read what these threads wrote
                 __syncwarp();
@@ -437,7 +401,7 @@ int launch_pass_rp(const LoraTcPass& p, cudaStream_t stream) {
     for (int i = 0; i < p.count; ++i)
         units += static_cast<long long>((p.prob[i].R + kLtRows - 1) / kLtRows) * p.prob[i].splits;
     const int grid = static_cast<int>(units < p.sm_count ? units : p.sm_count);
-    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(lt_threads<MN>()), C::kSmemAlloc, stream, p);
+    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kLtThreads), C::kSmemAlloc, stream, p);
 }
 
 }  // namespace
