@@ -421,23 +421,6 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t addr) {
     return d;
 }
 
-// Shared-memory descriptor of an MN-major TF32 operand as TMA writes it with
-// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B from boxes of 32 fp32 along M (128 B)
-// by k rows: 32-byte atoms swizzled within each 128-byte row over an 8-row
-// pattern (layout type SWIZZLE_128B_BASE32B, the swizzled form MN-major TF32
-// operands take).  LBO = distance between 32-element groups along M (one
-// box); SBO = 512 B, the distance between the two 4-row halves of one K = 8
-// step (measured: 1024 gives wrong products).
-__device__ __forceinline__ uint64_t umma_desc_mn_sw128_32b(uint32_t addr, uint32_t lbo) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);         // start address   [0,14)
-    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;    // LBO             [16,30)
-    d |= static_cast<uint64_t>(512u >> 4) << 32;               // SBO = 512 B     [32,46)
-    d |= static_cast<uint64_t>(1u) << 46;                      // version = 1     [46,48)
-    d |= static_cast<uint64_t>(1u) << 61;                      // 128B_BASE32B    [61,64)
-    return d;
-}
-
 // Instruction descriptor for kind::f16: fp32 accumulate, A and B of the same
 // 16-bit type (0 = f16, 1 = bf16), both K-major, tile M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_format, uint32_t m, uint32_t n) {
@@ -449,9 +432,20 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t ab_format, uint32
 }
 
 // Instruction descriptor for kind::tf32: fp32 accumulate, A and B TF32 (2),
-// B K-major, A K-major or (a_mn_major) MN-major, tile M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t m, uint32_t n, bool a_mn_major = false) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((n >> 3) << 17) | ((m >> 4) << 24);
+// both K-major, tile M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t m, uint32_t n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// kind::tf32 MMA with A (M = 128 rows in the 128 lanes, one element per column) in tensor memory.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 __device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,

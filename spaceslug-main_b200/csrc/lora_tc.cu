@@ -15,13 +15,18 @@
 //
 //  - Aop is TMA-loaded in tiles of 128 rows x 32 l straight from X or dY,
 //    either with the rows of D as the source's rows (T and G: l contiguous,
-//    a K-major operand, 128-byte swizzle) or with the rows of D contiguous in
-//    the source (dB reads dY^T and dA reads X^T: four boxes of 32 rows x 32 l,
-//    an MN-major operand in the 128-byte swizzle of 32-byte atoms, the
-//    swizzled layout MN-major TF32 operands take).  No transpose anywhere.
-//  - Four split warps turn each loaded tile into TF32 hi (rounded to nearest,
-//    in place) and lo = x - hi (exact in fp32, same offsets in a second tile):
-//    the split is elementwise, so it keeps whichever layout the tile has.
+//    one 128-byte-swizzled box) or with the rows of D contiguous in the
+//    source (dB reads dY^T and dA reads X^T: four unswizzled boxes of 32 rows
+//    x 32 l).
+//  - Four split warps, one per tensor-memory lane quarter, give each row of
+//    the tile to one thread: it reads the row's 32 values from shared memory
+//    (a 128-byte swizzled row, or one 4-byte column of the four boxes:
+//    conflict-free either way), forms TF32 hi (rounded to nearest) and
+//    lo = x - hi (exact in fp32) and stores both into tensor memory, where
+//    the MMAs read them as the A operand (row = lane).  So the transpose of
+//    the second kind costs nothing, and shared memory carries each tile once
+//    in (TMA) and once out (the split) instead of also holding the hi / lo
+//    tiles for the MMA to read.
 //  - Bop is prepared once per contraction as stacked planes [2RP][L]: rows
 //    0..RP-1 its TF32 hi parts, rows RP..2RP-1 its lo parts, rows >= r zero.
 //    Two MMAs per 8 l, Aop_hi x [B_hi; B_lo] and Aop_lo x [B_hi; B_lo]
@@ -61,18 +66,23 @@ __device__ __forceinline__ int lt_split_index(int warp) {  // split warp -> 0..3
 }
 constexpr int kLtATile = kLtRows * kLtL * 4;  // 16 KB
 constexpr int kLtMnBox = 32 * kLtL * 4;       // one MN-major box: 32 rows of D x 32 l, 4 KB
+constexpr int kLtTmemCols = 512;              // the whole of tensor memory (one CTA per SM)
 
 template <int RP, bool MN>
 struct LtCfg {
     static constexpr int kBTile = 2 * RP * kLtL * 4;  // stacked hi / lo rows of Bop
     static constexpr int kBTileAligned = (kBTile + 1023) / 1024 * 1024;
-    // stage: [Aop as loaded, then its hi part] [Aop lo] [Bop]
-    static constexpr int kLo = kLtATile;
-    static constexpr int kB = kLo + kLtATile;
+    // shared-memory stage: [Aop as loaded] [Bop]
+    static constexpr int kB = kLtATile;
     static constexpr int kStageBytes = kB + kBTileAligned;
     static constexpr int kBudget = 222 * 1024;
-    static constexpr int kStages = kBudget / kStageBytes > 8 ? 8 : kBudget / kStageBytes;
-    static constexpr int kTmemCols = 4 * RP < 32 ? 32 : 4 * RP;  // two chunk buffers of 2RP columns
+    static constexpr int kSmemStages = kBudget / kStageBytes;
+    // tensor memory: columns [0, 4RP) two accumulator chunk buffers of 2RP columns;
+    // from kACol on, per stage 64 columns: 32 of Aop hi (one l per column), 32 of Aop lo
+    static constexpr int kACol = 4 * RP < 64 ? 64 : 4 * RP;
+    static constexpr int kTmemStages = (kLtTmemCols - kACol) / 64;
+    static constexpr int kStages0 = kSmemStages < kTmemStages ? kSmemStages : kTmemStages;
+    static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
     static_assert(kStages > 2, "the epilogue waits on the stages' MMA commits: it must not fall a phase behind");
     static constexpr int kBarOff = kStages * kStageBytes;
     // full[S], split[S], empty[S], chunk_empty[2]; then abort flag, TMEM address
@@ -133,7 +143,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
         fence_mbarrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+        tmem_alloc(smem_u32(tmem_slot), kLtTmemCols);
         tmem_relinquish();
     }
     tc_fence_before_sync();
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
             // per stage tells both the producer (the stage may be refilled) and
             // the epilogue (the chunk's sums are complete).
             const int par = warp == 1 ? 0 : 1;
-            constexpr uint32_t idesc = umma_idesc_tf32(kLtRows, 2 * RP, MN);
+            constexpr uint32_t idesc = umma_idesc_tf32(kLtRows, 2 * RP);
             int total = 0;
             for (int u = blockIdx.x; u < units; u += gridDim.x) {
                 const LtUnit w = lt_unit(P, u);
@@ -206,17 +216,13 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     break;
                 if (!mbar_wait(split(s), (q / C::kStages) & 1u, abort_flag, status, kStatusTimeoutMma)) break;
                 tc_fence_after_sync();
-                const uint32_t st_base = base + s * C::kStageBytes;
-                const uint32_t a_hi = st_base, a_lo = st_base + C::kLo, bt = st_base + C::kB;
+                const uint32_t bt = base + s * C::kStageBytes + C::kB;
+                const uint32_t a_hi = tmem + static_cast<uint32_t>(C::kACol + 64 * s), a_lo = a_hi + 32;
 #pragma unroll
-                for (int kk = 0; kk < kLtL / 8; ++kk) {  // K = 8: 32 bytes of each K-major row, 8 rows of MN-major
+                for (int kk = 0; kk < kLtL / 8; ++kk) {  // K = 8: 8 columns of A, 32 bytes of each B row
                     const uint64_t bd = umma_desc_k_sw128(bt + kk * 32);
-                    const uint64_t ah = MN ? umma_desc_mn_sw128_32b(a_hi + kk * 1024, kLtMnBox)
-                                           : umma_desc_k_sw128(a_hi + kk * 32);
-                    const uint64_t al = MN ? umma_desc_mn_sw128_32b(a_lo + kk * 1024, kLtMnBox)
-                                           : umma_desc_k_sw128(a_lo + kk * 32);
-                    umma_tf32_ss(dacc, ah, bd, idesc, kk > 0 ? 1u : 0u);
-                    umma_tf32_ss(dacc, al, bd, idesc, 1u);
+                    umma_tf32_ts(dacc, a_hi + 8 * kk, bd, idesc, kk > 0 ? 1u : 0u);
+                    umma_tf32_ts(dacc, a_lo + 8 * kk, bd, idesc, 1u);
                 }
                 umma_commit(empty(s));
                 last = q;
@@ -279,10 +285,10 @@ __global__ void __launch_bounds__(kLtThreads, 1)
         }
     } else if (lt_split_index(warp) >= 0) {
         // ----------------------------------------------------------- split --
-        // Warps 2, 3, 8, 9 overwrite each stage's loaded Aop tile with its TF32
-        // hi parts and write the lo parts at the same offsets of the next tile.
-        constexpr int kSplitThreads = kLtSplitWarps * 32;
-        const int ct = lt_split_index(warp) * 32 + lane;  // 0 .. kSplitThreads - 1
+        // Warps 2, 3, 8, 9 (lane quarters 2, 3, 0, 1): thread <-> row 32 (warp % 4) + lane
+        // of the tile, whose hi and lo parts go to its tensor-memory lane.
+        const int quarter = warp & 3, row = quarter * 32 + lane;
+        const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         int q = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -293,20 +299,37 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     ok = false;
                     break;
                 }
-                uint8_t* stage = smem + s * C::kStageBytes;
-                float4* hi = reinterpret_cast<float4*>(stage);
-                float4* lo = reinterpret_cast<float4*>(stage + C::kLo);
-                constexpr int kPer = kLtATile / 16 / kSplitThreads;  // 8 float4 per thread
-                float4 v[kPer];
+                tc_fence_after_sync();  // the MMAs that last read this stage's tensor memory have completed
+                const uint8_t* stage = smem + s * C::kStageBytes;
+                float v[kLtL];
+                if constexpr (MN) {
+                    // box quarter, l at 128 B l, this row at 4 B lane: a warp reads one 128-byte row
+                    const float* col = reinterpret_cast<const float*>(stage + kLtMnBox * quarter) + lane;
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) v[i] = hi[ct + kSplitThreads * i];
+                    for (int l = 0; l < kLtL; ++l) v[l] = col[32 * l];
+                } else {
+                    // 128-byte row `row`, 16-byte chunk c at c ^ (row & 7)
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) {
-                    const float4 h = make_float4(to_tf32(v[i].x), to_tf32(v[i].y), to_tf32(v[i].z), to_tf32(v[i].w));
-                    hi[ct + kSplitThreads * i] = h;
-                    lo[ct + kSplitThreads * i] = make_float4(v[i].x - h.x, v[i].y - h.y, v[i].z - h.z, v[i].w - h.w);
+                    for (int c = 0; c < kLtL / 4; ++c) {
+                        const float4 f = *reinterpret_cast<const float4*>(stage + 128 * row + ((c ^ (row & 7)) << 4));
+                        v[4 * c] = f.x;
+                        v[4 * c + 1] = f.y;
+                        v[4 * c + 2] = f.z;
+                        v[4 * c + 3] = f.w;
+                    }
                 }
-                fence_proxy_async_smem();  // the MMAs (async proxy) read what these threads wrote
+                uint32_t hi[kLtL], lo[kLtL];
+#pragma unroll
+                for (int l = 0; l < kLtL; ++l) {
+                    const float h = to_tf32(v[l]);
+                    hi[l] = __float_as_uint(h);
+                    lo[l] = __float_as_uint(v[l] - h);
+                }
+                const uint32_t col = t_lane + static_cast<uint32_t>(C::kACol + 64 * s);
+                tmem_st32(col, hi);
+                tmem_st32(col + 32, lo);
+                tmem_st_wait();
+                tc_fence_before_sync();  // the MMAs (issued after the barrier) read what these threads stored
                 __syncwarp();
                 if (lane == 0) mbar_arrive(split(s));
             }
@@ -316,7 +339,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after_sync();
-        tmem_dealloc(tmem, C::kTmemCols);
+        tmem_dealloc(tmem, kLtTmemCols);
     }
 }
 
