@@ -16,11 +16,11 @@
 //  - Aop is TMA-loaded in tiles of 128 rows x 32 l straight from X or dY,
 //    either with the rows of D as the source's rows (T and G: l contiguous,
 //    one 128-byte-swizzled box) or with the rows of D contiguous in the
-//    source (dB reads dY^T and dA reads X^T: four unswizzled boxes of 32 rows
-//    x 32 l).
+//    source (dB reads dY^T and dA reads X^T: one unswizzled box of 32 l x 128
+//    rows, 512 contiguous bytes per l).
 //  - Four split warps, one per tensor-memory lane quarter, give each row of
 //    the tile to one thread: it reads the row's 32 values from shared memory
-//    (a 128-byte swizzled row, or one 4-byte column of the four boxes:
+//    (a 128-byte swizzled row, or one 4-byte column of the l-major box:
 //    conflict-free either way), forms TF32 hi (rounded to nearest) and
 //    lo = x - hi (exact in fp32) and stores both into tensor memory, where
 //    the MMAs read them as the A operand (row = lane).  So the transpose of
@@ -65,7 +65,6 @@ __device__ __forceinline__ int lt_split_index(int warp) {  // split warp -> 0..3
     return (warp == 2 || warp == 3) ? warp - 2 : (warp == 8 || warp == 9) ? warp - 6 : -1;
 }
 constexpr int kLtATile = kLtRows * kLtL * 4;  // 16 KB
-constexpr int kLtMnBox = 32 * kLtL * 4;       // one MN-major box: 32 rows of D x 32 l, 4 KB
 constexpr int kLtTmemCols = 512;              // the whole of tensor memory (one CTA per SM)
 
 template <int RP, bool MN>
@@ -179,11 +178,9 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                     mbar_arrive_expect_tx(full(s), static_cast<uint32_t>(kLtATile + C::kBTile));
                     const int l0 = st * kLtL;
                     if constexpr (MN) {
-                        // four boxes of 32 rows of D x 32 l (l = the box's row), 4 KB apart
-#pragma unroll
-                        for (int b = 0; b < 4; ++b) tma_load_2d(a + b * kLtMnBox, tm_a, full(s), row0 + 32 * b, l0);
+                        tma_load_2d(a, tm_a, full(s), row0, l0);  // [32 l][128 rows of D], 512-byte rows
                     } else {
-                        tma_load_2d(a, tm_a, full(s), l0, row0);
+                        tma_load_2d(a, tm_a, full(s), l0, row0);  // [128 rows][32 l], 128-byte swizzled rows
                     }
                     tma_load_2d(a + C::kB, tm_b, full(s), l0, 0);
                 }
@@ -303,10 +300,10 @@ __global__ void __launch_bounds__(kLtThreads, 1)
                 const uint8_t* stage = smem + s * C::kStageBytes;
                 float v[kLtL];
                 if constexpr (MN) {
-                    // box quarter, l at 128 B l, this row at 4 B lane: a warp reads one 128-byte row
-                    const float* col = reinterpret_cast<const float*>(stage + kLtMnBox * quarter) + lane;
+                    // l at 512 B l, this row at 4 B row: a warp reads 128 consecutive bytes
+                    const float* col = reinterpret_cast<const float*>(stage) + row;
 #pragma unroll
-                    for (int l = 0; l < kLtL; ++l) v[l] = col[32 * l];
+                    for (int l = 0; l < kLtL; ++l) v[l] = col[kLtRows * l];
                 } else {
                     // 128-byte row `row`, 16-byte chunk c at c ^ (row & 7)
 #pragma unroll

@@ -410,8 +410,8 @@ void run_lora_backward_tc(const q4::LoraBackwardArgs& g, int sm_count, int* stat
     const uint32_t brows = static_cast<uint32_t>(two);
     auto problem = [&](q4::LoraTcProblem& q, const float* a, uint64_t a_inner, uint64_t a_outer, bool mn_major,
                        const float* bplane, int R, int L, int splits, float* partial) {
-        // MN-major: unswizzled boxes of 32 rows of D (contiguous) x 32 l
-        encode_2d(&q.tm_a, F32, a, a_inner, a_outer, a_inner * 4, 32, mn_major ? 32 : 128,
+        // K-major: 32 l x 128 rows of D, 128-byte swizzle; MN-major: 128 rows of D (contiguous) x 32 l, unswizzled
+        encode_2d(&q.tm_a, F32, a, a_inner, a_outer, a_inner * 4, mn_major ? 128 : 32, mn_major ? 32 : 128,
                   mn_major ? CU_TENSOR_MAP_SWIZZLE_NONE : SW);
         encode_2d(&q.tm_b, F32, bplane, static_cast<uint64_t>(L), two, static_cast<uint64_t>(round4(L)) * 4, 32,
                   brows, SW);
