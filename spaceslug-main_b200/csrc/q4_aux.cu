@@ -601,9 +601,14 @@ namespace {
 // Launched as a programmatic dependent: it lets its own dependents launch at
 // once (a GEMV after a copy-in starts streaming its weights while X arrives)
 // and waits for its predecessor's writes (a copy-out reads the GEMV's Y).
+// With done_flag (a mapped host word) the last CTA to finish publishes the
+// status word and then sets done_flag to 1, after every CTA's stores are
+// visible to the host: the host can wait on that word instead of a stream
+// synchronisation.  done_count is a device counter that is 0 between launches.
 __global__ void __launch_bounds__(256) copy_words_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                                          long long n, int vec, const int* __restrict__ status_src,
-                                                         int* __restrict__ status_dst) {
+                                                         int* __restrict__ status_dst, int* done_flag,
+                                                         unsigned* done_count) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -615,14 +620,30 @@ __global__ void __launch_bounds__(256) copy_words_kernel(const float* __restrict
     } else {
         for (long long i = i0; i < n; i += stride) dst[i] = src[i];
     }
-    if (status_src != nullptr && i0 == 0) *status_dst = *status_src;
+    if (done_flag == nullptr) {
+        if (status_src != nullptr && i0 == 0) *status_dst = *status_src;
+        return;
+    }
+    // Release at device scope per CTA; the last CTA acquires every CTA's
+    // stores through the counter and orders them (cumulatively) before the
+    // completion word with one system-scope fence.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(done_count, 1u) == gridDim.x - 1) {
+        __threadfence();
+        if (status_src != nullptr) *status_dst = *status_src;
+        *done_count = 0;
+        __threadfence_system();
+        *reinterpret_cast<volatile int*>(done_flag) = 1;
+    }
 }
 
 }  // namespace
 
 int launch_copy_words(const float* src, float* dst, long long n, const int* status_src, int* status_dst,
-                      cudaStream_t stream) {
-    if (n < 0 || (n > 0 && (src == nullptr || dst == nullptr)) || ((status_src == nullptr) != (status_dst == nullptr)))
+                      cudaStream_t stream, int* done_flag, unsigned* done_count) {
+    if (n < 0 || (n > 0 && (src == nullptr || dst == nullptr)) || ((status_src == nullptr) != (status_dst == nullptr)) ||
+        ((done_flag == nullptr) != (done_count == nullptr)))
         return static_cast<int>(cudaErrorInvalidValue);
     const int vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
                     (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
@@ -639,7 +660,8 @@ int launch_copy_words(const float* src, float* dst, long long n, const int* stat
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return static_cast<int>(cudaLaunchKernelEx(&cfg, copy_words_kernel, src, dst, n, vec, status_src, status_dst));
+    return static_cast<int>(
+        cudaLaunchKernelEx(&cfg, copy_words_kernel, src, dst, n, vec, status_src, status_dst, done_flag, done_count));
 }
 
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,

@@ -183,9 +183,12 @@ int launch_lora_add(const float* t, const float* b, float* y, int M, int N, long
 int launch_push_rows(const float* src, const PeerPtrs& peers, int npeers, int rows, int width, long long ld, int ctas,
                      cudaStream_t stream);
 // n floats src -> dst by a small kernel (either side device memory or mapped
-// pinned host memory), plus the status word when status_src is given.
+// pinned host memory), plus the status word when status_src is given.  With
+// done_flag (mapped host word) and done_count (device counter, 0 between
+// launches), the last CTA sets *done_flag = 1 once every store is visible to
+// the host.
 int launch_copy_words(const float* src, float* dst, long long n, const int* status_src, int* status_dst,
-                      cudaStream_t stream);
+                      cudaStream_t stream, int* done_flag = nullptr, unsigned* done_count = nullptr);
 int launch_shards_relayout(const float* gathered, float* y, int parts, int rows, int width, int n_total,
                            long long ld_y, cudaStream_t stream);
 // CQ4 activation transform into the code basis, fp16 [M][K] -> fp16 [M][K]:

@@ -13,6 +13,7 @@
 #include <memory>
 #include <array>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -63,6 +64,9 @@ struct DeviceCtx {
     int* status = nullptr;  // device int, kernels record wait timeouts here
     int* status_host = nullptr;     // pinned, mapped host word the host entry points read `status` into
     int* status_host_dev = nullptr; // its device address
+    int* done_host = nullptr;       // pinned, mapped word a host call's last kernel sets when it is done
+    int* done_host_dev = nullptr;   // its device address
+    unsigned* done_count = nullptr; // device counter of the CTAs of that kernel that have finished
     cudaStream_t stream = nullptr;  // for the synchronous host-pointer entry points
     std::mutex host_mu;             // serialises use of `stream` and `hbuf` by host entry points
     void* hbuf = nullptr;           // device staging of X and Y for spaceslug_q4_weights_run_host (grows)
@@ -131,11 +135,17 @@ DeviceCtx& ctx_for(int device) {
                                              std::to_string(major) + std::to_string(minor));
             check(cudaMalloc(&c.status, sizeof(int)), "cudaMalloc status");
             check(cudaMemset(c.status, 0, sizeof(int)), "cudaMemset status");
-            check(cudaHostAlloc(reinterpret_cast<void**>(&c.status_host), sizeof(int), cudaHostAllocMapped),
+            // status word at 0, completion word 64 bytes on
+            check(cudaHostAlloc(reinterpret_cast<void**>(&c.status_host), 128, cudaHostAllocMapped),
                   "cudaHostAlloc status");
             check(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c.status_host_dev), c.status_host, 0),
                   "cudaHostGetDevicePointer status");
             *c.status_host = 0;
+            c.done_host = c.status_host + 16;
+            c.done_host_dev = c.status_host_dev + 16;
+            *c.done_host = 0;
+            check(cudaMalloc(reinterpret_cast<void**>(&c.done_count), sizeof(unsigned)), "cudaMalloc done count");
+            check(cudaMemset(c.done_count, 0, sizeof(unsigned)), "cudaMemset done count");
             check(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate");
             cudaMemPool_t pool;
             check(cudaDeviceGetDefaultMemPool(&pool, device), "default mem pool");
@@ -778,10 +788,35 @@ void run_problem(const Problem& p, cudaStream_t stream) {
 // synchronisation covers both (no second round trip per call).  With
 // `enqueued`, the call's copy-out kernel has already written it to the mapped
 // host word.
-int take_status(DeviceCtx& c, cudaStream_t stream, bool enqueued = false) {
+// Waits until a host call's last kernel has set c.done_host (it does so after
+// every one of its stores, Y and the status word, is visible to the host):
+// about 2.5 us sooner than a stream synchronisation on this hardware.  Every
+// 1024 polls the stream is queried; an error, an idle stream, or a second
+// without the word ends the polling in a stream synchronisation, which
+// reports the error or waits for the rest.
+void wait_done(DeviceCtx& c) {
+    volatile int* flag = c.done_host;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t i = 1;; ++i) {
+        if (*flag) return;
+        if ((i & 1023u) == 0) {
+            if (cudaStreamQuery(c.stream) != cudaErrorNotReady) break;
+            if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(1)) break;
+        }
+    }
+    check(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+}
+
+// The status word of the work on `stream` (cleared on the device when set).
+// enqueued: the work already copies it into c.status_host; done_flag: and
+// then sets c.done_host, which the host waits on instead of the stream.
+int take_status(DeviceCtx& c, cudaStream_t stream, bool enqueued = false, bool done_flag = false) {
     if (!enqueued)
         check(cudaMemcpyAsync(c.status_host, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream), "read status");
-    check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    if (done_flag && stream == c.stream)
+        wait_done(c);
+    else
+        check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     const int st = *static_cast<volatile int*>(c.status_host);
     if (st) {
         check(cudaMemsetAsync(c.status, 0, sizeof(int), stream), "clear status");
@@ -1509,12 +1544,13 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
             run_problem(p, c.stream);
             if (ymap)
                 check_launch(q4::launch_copy_words(dy, ymap, static_cast<long long>(m) * w->N, c.status,
-                                                   c.status_host_dev, c.stream),
+                                                   c.status_host_dev, c.stream, c.done_host_dev, c.done_count),
                              "copy Y out");
             else
                 d2h(y, dy, yb, c.stream);
         };
         const int variant = decode_variant_init().load();
+        if (ymap) *static_cast<volatile int*>(c.done_host) = 0;  // the copy-out kernel sets it again
         if (xmap && ymap && m <= 8) {
             // decode-sized call with pinned buffers: replay (or capture) its graph
             cudaGraphExec_t exec = nullptr;
@@ -1558,7 +1594,8 @@ int spaceslug_q4_weights_run_host(spaceslug_q4_weights* w, const float* x, float
         } else {
             issue();
         }
-        if (take_status(c, c.stream, ymap != nullptr)) return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
+        if (take_status(c, c.stream, ymap != nullptr, ymap != nullptr))
+            return fail(SPACESLUG_TIMEOUT, "a kernel wait timed out");
         return SPACESLUG_OK;
     });
 }

@@ -82,7 +82,8 @@ def test_asynchronous_call_reports_through_device_status(session, oracle, cuda, 
 
 def test_pinned_host_call_returns_timeout_then_recovers(session, oracle, cuda, stall):
     # spaceslug_q4_weights_run_host with pinned X and Y: the status word rides
-    # to the host with Y (a small copy kernel into a mapped host word)
+    # to the host with Y (a small copy kernel into a mapped host word), and the
+    # host waits on the completion word that kernel's last CTA sets
     import ctypes
 
     import torch
