@@ -639,7 +639,8 @@ def cq4_gpu(args, dist: Dist, torch, session, peaks) -> dict:
 
 
 def sgemm_gpu(args, dist: Dist, torch, session) -> dict:
-    """spaceslug_sgemm_device (cuBLAS fp32 FMA) at the reference bench's 1024^3
+    """spaceslug_sgemm_device (tcgen05 kind::tf32, three TF32 products per term
+    for fp32-level accuracy) at the reference bench's 1024^3 and at 4096^3
     (bench/bench_cq4gemm.cpp:39: 3.21 TFLOP/s fp32 baseline on the RX580)."""
     dev = torch.device("cuda", dist.local)
     stream = torch.cuda.Stream(device=dev)
