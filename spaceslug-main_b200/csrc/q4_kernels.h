@@ -291,6 +291,12 @@ struct SgemmTcArgs {
 };
 int sgemm_tc_bn(int N);
 int launch_sgemm_tc(const SgemmTcArgs& a, cudaStream_t stream);
+// The CTA-pair form for large problems: 256 x 256 tiles of C, the A and B^T
+// planes padded to whole 256-row tiles and mapped with 32 x 128 boxes (each
+// CTA loads 128 rows); at most max_pairs co-resident pairs (persistent).
+int sgemm_pair_tiles(int M, int N);
+int sgemm_pair_max_active();
+int launch_sgemm_pair(const SgemmTcArgs& a, int max_pairs, cudaStream_t stream);
 // Legacy spaceslug_lora_delta: Y[M,64] = X[M,64] A[64,R] B[R,64].
 int launch_lora_delta64(const float* x, const float* a, const float* b, float* y, int M, int rank,
                         cudaStream_t stream);

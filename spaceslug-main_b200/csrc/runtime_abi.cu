@@ -336,13 +336,44 @@ void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
 // with row pitch lda, or with trans_a A given as [k][m]; op(B) is [k x n]: B
 // row-major [k][n] with row pitch ldb, or with trans_b B given as [n][k].  The
 // operands' TF32 hi / lo planes live in stream-ordered scratch.
+// Co-resident clusters of the pair SGEMM on the current device (cached).
+int sgemm_pairs_on_device() {
+    static std::atomic<int> cache[64];
+    static std::atomic<bool> init[64];
+    int dev = 0;
+    check(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return q4::sgemm_pair_max_active();
+    if (!init[dev].load(std::memory_order_acquire)) {
+        cache[dev].store(q4::sgemm_pair_max_active(), std::memory_order_relaxed);
+        init[dev].store(true, std::memory_order_release);
+    }
+    return cache[dev].load(std::memory_order_relaxed);
+}
+
+// Pair tiles (256 x 256, MMA-bound, ~1548 cycles per 32-k stage) or single
+// tiles (128 x bn, shared-memory-bound, ~1250 cycles per stage at bn = 128):
+// the one whose waves of stages take less time.
+bool sgemm_use_pair(int m, int n, int sm_count, int pairs) {
+    if (m < 256 || n < 256 || pairs < 1) return false;
+    const long long single_waves = (static_cast<long long>((m + 127) / 128) * ((n + 127) / 128) + sm_count - 1) / sm_count;
+    const long long pair_waves = (static_cast<long long>(q4::sgemm_pair_tiles(m, n)) + pairs - 1) / pairs;
+    return pair_waves * 1548 < single_waves * 1250;
+}
+
 void run_sgemm(const float* a, long long lda, bool trans_a, const float* b, long long ldb, bool trans_b, float* cm,
                long long ldc, int m, int n, int k, float alpha, int* status, cudaStream_t stream) {
+    int dev = 0, sms = 0;
+    check(cudaGetDevice(&dev), "cudaGetDevice");
+    check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+    const int pairs = m >= 256 && n >= 256 ? sgemm_pairs_on_device() : 0;
+    const bool pair = sgemm_use_pair(m, n, sms, pairs);
     // Planes padded to whole TMA boxes (zeros): k to a multiple of 32, the rows
-    // to whole 128-row (A) and bn-row (B) tiles, so every box lies inside its plane.
+    // to whole tiles (128 rows of A and bn of B, or 256 of both for pairs), so
+    // every box lies inside its plane.
     const int bn = q4::sgemm_tc_bn(n);
     const long long ldk = (static_cast<long long>(k) + 31) / 32 * 32;
-    const int mr = (m + 127) / 128 * 128, nr = (n + bn - 1) / bn * bn;
+    const int mt = pair ? 256 : 128, nt = pair ? 256 : bn;
+    const int mr = (m + mt - 1) / mt * mt, nr = (n + nt - 1) / nt * nt;
     Scratch pa(static_cast<size_t>(2) * mr * ldk * sizeof(float), stream);
     Scratch pb(static_cast<size_t>(2) * nr * ldk * sizeof(float), stream);
     float* ahi = static_cast<float*>(pa.p);
@@ -363,16 +394,18 @@ void run_sgemm(const float* a, long long lda, bool trans_a, const float* b, long
     const uint64_t kk = static_cast<uint64_t>(ldk);
     encode_2d(&g.tm_ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ahi, kk, mr, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     encode_2d(&g.tm_alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, alo, kk, mr, rb, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_2d(&g.tm_bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, bhi, kk, nr, rb, 32, static_cast<uint32_t>(bn),
-              CU_TENSOR_MAP_SWIZZLE_128B);
-    encode_2d(&g.tm_blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, blo, kk, nr, rb, 32, static_cast<uint32_t>(bn),
-              CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint32_t b_box = pair ? 128u : static_cast<uint32_t>(bn);  // a pair CTA loads 128 rows of B
+    encode_2d(&g.tm_bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, bhi, kk, nr, rb, 32, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
+    encode_2d(&g.tm_blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, blo, kk, nr, rb, 32, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
     g.c = cm;
     g.M = m; g.N = n; g.K = k;
     g.ldc = ldc;
     g.alpha = alpha;
     g.status = status;
-    check_launch(q4::launch_sgemm_tc(g, stream), "sgemm (tcgen05) launch");
+    if (pair)
+        check_launch(q4::launch_sgemm_pair(g, pairs, stream), "sgemm (tcgen05 pairs) launch");
+    else
+        check_launch(q4::launch_sgemm_tc(g, stream), "sgemm (tcgen05) launch");
 }
 
 // The LoRA backward takes the tensor-core passes of lora_tc.cu when the

@@ -31,6 +31,10 @@
 // frees it, one per chunk hands the chunk's buffer to the epilogue), warps
 // 4-7 (tensor-memory lane quarters 0-3, one row of C per thread) sum the
 // chunks and store C.
+// Large problems take sgemm_pair_kernel instead: CTA pairs (cta_group::2) on
+// 256 x 256 tiles of C, where each CTA loads half of the A and half of the B
+// rows and the leader's M = 256, N = 256 MMAs read both halves, so that the
+// tensor core rather than shared-memory bandwidth sets the pace (below).
 // Every wait is bounded (status word + abort flag).
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -291,7 +295,265 @@ int launch_sgemm_bn(const SgemmTcArgs& a, cudaStream_t stream) {
     return static_cast<int>(e);
 }
 
+// ---------------------------------------------------------------- pairs --
+// A cluster of two CTAs owns a 256 x 256 tile of C.  CTA c TMA-loads rows
+// m0 + 128 c .. of the A planes and rows n0 + 128 c .. of the B^T planes (hi
+// and lo, 32 k per stage; the loads are counted on the leader's barrier), and
+// the leader issues kind::tf32 MMAs with M = 256, N = 256, K = 8 that read A
+// and B from both CTAs' shared memory at the same offsets.  Each CTA's tensor
+// memory holds its 128 rows x 256 columns of the accumulator, double-buffered
+// for the 32-k chunks (all 512 columns).  Per CTA and stage: 64 KB written by
+// TMA and 96 KB read by twelve MMAs, ~1250 shared-memory cycles, against
+// 12 x ~129 cycles of tensor core; the single-CTA 128 x 128 tile moves the
+// same 160 KB for half the products.  Persistent: pair p takes tiles p,
+// p + pairs, ...; the eight epilogue warps (two per lane quarter, 128 columns
+// each) sum the chunks of a tile in registers and store its rows of C while
+// the MMAs run on into the next tile.
+constexpr int kSpHalf = 128;
+constexpr int kSpTile = 256;
+constexpr int kSpThreads = 320;  // warp 0 TMA, warp 1 MMA (leader CTA), warps 2-9 epilogue
+constexpr int kSpEpiWarp0 = 2;
+constexpr int kSpEpiWarps = 8;
+constexpr int kSpEpiCols = 128;  // accumulator columns per epilogue warp
+
+struct SpCfg {
+    static constexpr int kPlane = kSpHalf * kSBK * 4;  // 16 KB: 128 rows x 32 k of one plane
+    static constexpr int kStageBytes = 4 * kPlane;     // A hi, A lo, B hi, B lo
+    static constexpr int kStages = 3;
+    static constexpr int kBarOff = kStages * kStageBytes;
+    // full[S] (leader), empty[S] (both), chunk_full[2] (both), chunk_empty[2] (leader), done (leader);
+    // then abort flag, TMEM address
+    static constexpr int kNumBars = 2 * kStages + 5;
+    static constexpr int kSmem = kBarOff + kNumBars * 8 + 16;
+    static constexpr int kSmemAlloc = kSmem + 1024;
+    static constexpr int kTmemCols = 2 * kSpTile;
+    static_assert(kSmemAlloc <= 232448, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(kSpThreads, 1)
+    sgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                      const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                      float* __restrict__ c, int M, int N, int K, long long ldc, float alpha, int* __restrict__ status) {
+    using C = SpCfg;
+    constexpr int ST = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;  // 128B-swizzled tiles need a 1024-aligned window
+    uint8_t* smem = smem_raw + (base - raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t crank = cluster_ctarank();
+    const bool leader = crank == 0;
+    const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+    const int MT = (M + kSpTile - 1) / kSpTile, NT = (N + kSpTile - 1) / kSpTile;
+    const int tiles = MT * NT;
+    const int KT = (K + kSBK - 1) / kSBK;
+
+    const uint32_t bar = base + C::kBarOff;
+    auto full = [&](int s) { return bar + 8u * s; };
+    auto empty = [&](int s) { return bar + 8u * (ST + s); };
+    auto chunk_full = [&](int b) { return bar + 8u * (2 * ST + b); };
+    auto chunk_empty = [&](int b) { return bar + 8u * (2 * ST + 2 + b); };
+    const uint32_t done_bar = bar + 8u * (2 * ST + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kBarOff + C::kNumBars * 8);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOff + C::kNumBars * 8 + 8);
+    auto leader_addr = [&](uint32_t a) { return mapa_shared(a, 0); };
+
+    if (tid == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(full(s), 1);   // the leader's expect_tx (both CTAs' bytes)
+            mbar_init(empty(s), 1);  // the leader's multicast commit
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(chunk_full(b), 1);                  // the leader's multicast commit
+            mbar_init(chunk_empty(b), 2 * kSpEpiWarps);   // epilogue warps of both CTAs
+        }
+        mbar_init(done_bar, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before_sync();
+    cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated
+    tc_fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // --------------------------------------------------- producer --
+            tma_prefetch_desc(&tm_ahi);
+            tma_prefetch_desc(&tm_alo);
+            tma_prefetch_desc(&tm_bhi);
+            tma_prefetch_desc(&tm_blo);
+            pdl_wait();  // the planes are written by the previous launches (the split pass)
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                const int m0 = (t % MT) * kSpTile + static_cast<int>(crank) * kSpHalf;
+                const int n0 = (t / MT) * kSpTile + static_cast<int>(crank) * kSpHalf;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST;
+                    const uint32_t ph = (it / ST) & 1u;
+                    if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(full(s), 2u * C::kStageBytes);
+                    const uint32_t f = leader_addr(full(s));
+                    const uint32_t st = base + s * C::kStageBytes;
+                    tma_load_2d_pair(st, &tm_ahi, f, kt * kSBK, m0);
+                    tma_load_2d_pair(st + C::kPlane, &tm_alo, f, kt * kSBK, m0);
+                    tma_load_2d_pair(st + 2 * C::kPlane, &tm_bhi, f, kt * kSBK, n0);
+                    tma_load_2d_pair(st + 3 * C::kPlane, &tm_blo, f, kt * kSBK, n0);
+                }
+            }
+            if (*abort_flag && leader)  // let the copies in flight (both CTAs') land before exit
+                for (int j = (it > ST ? it - ST : 0); j < it; ++j) mbar_drain(full(j % ST), (j / ST) & 1u);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (leader && elect_one()) {
+            // ------------------------------------------- MMA (leader CTA) --
+            constexpr uint32_t idesc = umma_idesc_tf32(kSpTile, kSpTile);
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int b = it & 1;  // one 32-k chunk per stage
+                    if (!mbar_wait(chunk_empty(b), ((it >> 1) & 1u) ^ 1u, abort_flag, status, kStatusTimeoutMma) ||
+                        !mbar_wait(full(it % ST), (it / ST) & 1u, abort_flag, status, kStatusTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t dacc = tmem + static_cast<uint32_t>(b * kSpTile);
+                    const uint32_t st = base + (it % ST) * C::kStageBytes;
+                    const uint32_t ahi = st, alo = st + C::kPlane, bhi = st + 2 * C::kPlane, blo = st + 3 * C::kPlane;
+#pragma unroll
+                    for (int kk = 0; kk < kSBK / 8; ++kk) {
+                        const uint32_t off = kk * 32;
+                        umma_tf32_ss_pair(dacc, umma_desc_k_sw128(alo + off), umma_desc_k_sw128(bhi + off), idesc,
+                                          kk > 0 ? 1u : 0u);
+                        umma_tf32_ss_pair(dacc, umma_desc_k_sw128(ahi + off), umma_desc_k_sw128(blo + off), idesc, 1u);
+                        umma_tf32_ss_pair(dacc, umma_desc_k_sw128(ahi + off), umma_desc_k_sw128(bhi + off), idesc, 1u);
+                    }
+                    umma_commit_pair_both(empty(it % ST), 0x3);  // the stage may be refilled in both CTAs
+                    umma_commit_pair_both(chunk_full(b), 0x3);   // the chunk is complete in both CTAs
+                }
+            }
+            umma_commit_pair(leader_addr(done_bar));  // tracks every MMA issued above
+            mbar_drain(done_bar, 0u);
+        }
+        __syncwarp();
+    } else {
+        // -------------------------------------------------------- epilogue --
+        // Warp w reads lane quarter w % 4 (thread t <-> row 32 (w % 4) + t of
+        // this CTA's 128), columns 128 h .. 128 h + 127 of the tile, h = (w - 2) / 4.
+        const int quarter = warp & 3, h = (warp - kSpEpiWarp0) >> 2;
+        const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        float total[kSpEpiCols];
+#pragma unroll
+        for (int j = 0; j < kSpEpiCols; ++j) total[j] = 0.0f;
+        int it = 0;
+        bool ok = true;
+        for (int t = pair; t < tiles && ok; t += npairs) {
+            for (int kt = 0; kt < KT; ++kt, ++it) {
+                const int b = it & 1;
+                if (!mbar_wait_warp(chunk_full(b), (it >> 1) & 1u, abort_flag, status, kStatusTimeoutEpilogue)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t col = t_lane + static_cast<uint32_t>(b * kSpTile + h * kSpEpiCols);
+#pragma unroll
+                for (int cb = 0; cb < kSpEpiCols; cb += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(col + cb, v);
+                    tmem_ld_wait_regs(v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) total[cb + j] += __uint_as_float(v[j]);  // round to nearest
+                }
+                tc_fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(leader_addr(chunk_empty(b)));  // buffer b may take chunk it + 2
+            }
+            if (!ok) break;
+            const int row = (t % MT) * kSpTile + static_cast<int>(crank) * kSpHalf + quarter * 32 + lane;
+            const int n0 = (t / MT) * kSpTile + h * kSpEpiCols;
+            if (*abort_flag == 0 && row < M && n0 < N) {
+                float* dst = c + static_cast<long long>(row) * ldc + n0;
+#pragma unroll
+                for (int cb = 0; cb < kSpEpiCols; cb += 4) {
+                    if (n0 + cb + 4 <= N && (reinterpret_cast<uintptr_t>(dst + cb) & 15u) == 0) {
+                        *reinterpret_cast<float4*>(dst + cb) = make_float4(
+                            alpha * total[cb], alpha * total[cb + 1], alpha * total[cb + 2], alpha * total[cb + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (n0 + cb + j < N) dst[cb + j] = alpha * total[cb + j];
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kSpEpiCols; ++j) total[j] = 0.0f;
+        }
+    }
+    tc_fence_before_sync();
+    cluster_sync_all();  // no CTA leaves while its peer may still use its shared or tensor memory
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc_pair(tmem, C::kTmemCols);
+    }
+}
+
+cudaLaunchConfig_t sgemm_pair_config(unsigned pairs, cudaLaunchAttribute* attr, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kSpThreads, 1, 1);
+    cfg.dynamicSmemBytes = SpCfg::kSmemAlloc;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cfg;
+}
+
 }  // namespace
+
+int sgemm_pair_tiles(int M, int N) { return ((M + kSpTile - 1) / kSpTile) * ((N + kSpTile - 1) / kSpTile); }
+
+int sgemm_pair_max_active() {
+    if (cudaFuncSetAttribute(sgemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SpCfg::kSmemAlloc) !=
+        cudaSuccess)
+        return 0;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = sgemm_pair_config(1, attr, nullptr);
+    cfg.numAttrs = 1;  // the cluster shape only
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, sgemm_pair_kernel, &cfg) != cudaSuccess) return 0;
+    return n;
+}
+
+int launch_sgemm_pair(const SgemmTcArgs& a, int max_pairs, cudaStream_t stream) {
+    if (a.M < 1 || a.N < 1 || a.K < 1 || max_pairs < 1) return static_cast<int>(cudaErrorInvalidValue);
+    cudaError_t e = cudaFuncSetAttribute(sgemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SpCfg::kSmemAlloc);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const int tiles = sgemm_pair_tiles(a.M, a.N);
+    const unsigned pairs = static_cast<unsigned>(tiles < max_pairs ? tiles : max_pairs);
+    cudaLaunchAttribute attr[2];
+    const cudaLaunchConfig_t cfg = sgemm_pair_config(pairs, attr, stream);
+    e = cudaLaunchKernelEx(&cfg, sgemm_pair_kernel, a.tm_ahi, a.tm_alo, a.tm_bhi, a.tm_blo, a.c, a.M, a.N, a.K, a.ldc,
+                           a.alpha, a.status);
+    return static_cast<int>(e);
+}
 
 int launch_split_planes(const float* src, int rows, int cols, long long ld_src, bool transpose, float* hi, float* lo,
                         int out_rows, long long ld_out, cudaStream_t stream) {

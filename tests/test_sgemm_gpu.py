@@ -60,9 +60,11 @@ def test_reports_zero_error_like_the_reference(session, cuda):
     assert err.value == 0.0 and np.all(c == 32.0)
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (37, 51, 37), (130, 17, 5), (300, 129, 1000), (5, 2000, 64)])
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (37, 51, 37), (130, 17, 5), (300, 129, 1000), (5, 2000, 64),
+                                   (2000, 1800, 700), (2300, 2600, 333)])
 def test_device_entry_ragged(session, cuda, m, n, k):
-    # tiles of 128 rows x 16/32/64/128 columns, ragged in every dimension, K not a multiple of 4
+    # tiles of 128 rows x 16/32/64/128 columns, ragged in every dimension, K not a multiple of 4;
+    # the last two run on CTA pairs (256 x 256 tiles; 2300 x 2600 gives most pairs two tiles)
     import torch
     rng = np.random.default_rng(m * n + k)
     a = (rng.standard_normal((m, k)) * 3).astype(np.float32)
@@ -89,3 +91,19 @@ def test_accuracy_is_fp32_level(session, cuda, k):
     ref = a.astype(np.float64) @ b.astype(np.float64)
     assert np.linalg.norm(c - ref) / np.linalg.norm(ref) < 2e-6
     assert abs(float(np.mean((c - ref) * np.sign(ref)))) < 2e-6 * np.sqrt(k)  # no pull toward zero
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 2048, 8192), (2304, 2560, 992)])
+def test_pair_tiles_accuracy(session, cuda, m, n, k):
+    # problems this large run on CTA pairs (cta_group::2, 256 x 256 tiles of C):
+    # the bars of the single-CTA accuracy test above (normwise near fp32
+    # rounding, no bias growing with K) and the reference's elementwise 1e-3
+    rng = np.random.default_rng(m + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    c = session.sgemm(a, b)
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    err = np.abs(c - ref) / np.maximum(1.0, np.abs(ref))
+    assert float(err.max()) <= 1e-3, float(err.max())
+    assert np.linalg.norm(c - ref) / np.linalg.norm(ref) < 2e-6
+    assert abs(float(np.mean((c - ref) * np.sign(ref)))) < 2e-6 * np.sqrt(k)
