@@ -54,12 +54,14 @@ constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row
 // CTAs share an SM).
 template <int M>
 struct TileCfg {
-    // M >= 5 multiplies on the tensor cores with mma.sync (see below): its
-    // loop costs the same at every M (3.6 us per layer in a 24-layer graph at
+    // M >= 4 multiplies on the tensor cores with mma.sync (see below): its
+    // loop costs the same at every M (3.3 us per layer in a 24-layer graph at
     // K = N = 4096), but every CTA first converts all of X into f16 hi/lo
-    // planes (1.4 us at M = 4, 2.1 us at M = 8), so it ties with the fp32
-    // path (M FMAs per weight: 5.0 us at M = 4) at M = 4 and wins above.
-    static constexpr bool kMma = M >= 5;
+    // planes (1.4 us at M = 4, 2.1 us at M = 8).  Against the fp32 path (M
+    // FMAs per weight: 5.0 us at M = 4) it is ahead from M = 4 on: 8.70
+    // against 8.93 us per layer there, and M = 3 stays on the fp32 path
+    // (8.08 us).
+    static constexpr bool kMma = M >= 4;
     static constexpr int kWarps = 16;
     static constexpr int kThreads = kWarps * 32;
     // X conversion of the mma path: float4 per thread and row (M * kslice <= 32768)
@@ -600,8 +602,8 @@ size_t gemv_tile_smem_bytes(int M, int K, int S) { return static_cast<size_t>(ti
 bool gemv_tile_supported(int M, int K, int S) {
     if (M < 1 || M > 8 || S < 1 || S > 8 || (S & (S - 1)) != 0) return false;
     if (K <= 0 || K % (kTBoxK * S) != 0) return false;
-    // the mma path (M >= 5) holds at most 16 float4 of X per thread while converting it
-    if (M >= 5 && static_cast<long long>(M) * (K / S) > 16LL * 4 * 512) return false;
+    // the mma path (M >= 4) holds at most 16 float4 of X per thread while converting it
+    if (M >= 4 && static_cast<long long>(M) * (K / S) > 16LL * 4 * 512) return false;
     return gemv_tile_smem_bytes(M, K, S) <= 227 * 1024;
 }
 
