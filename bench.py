@@ -2,7 +2,7 @@
 """Benchmark of the int4-dequant GEMM/GEMV (+ fused LoRA) hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill|lora|mlp70b|tiny]
+                    [--workload decode|prefill|lora|mlp70b|tiny|lora_backward|sgemm]
 
 Prints ONE JSON line on rank 0.
 
@@ -19,7 +19,9 @@ Other workloads (secondary figures, also attached to the default line at N=1):
 prefill = configs[2] (2048 x 4096 x 11008), lora = configs[3] (512 x 4096 x
 4096, r=16, alpha=32), tiny = configs[0]; mlp70b = configs[4] N-sharded over
 the ranks with an NCCL all-gather of Y (run it under torchrun; at N > 1 the
-default run attaches it as a secondary figure).
+default run attaches it as a secondary figure); lora_backward = the LoRA
+gradients at configs[3] and configs[4]'s sizes; sgemm = spaceslug_sgemm_device
+(fp32, 3xTF32 on tcgen05) at 1024^3 and 4096^3, the line's value at 4096^3.
 
 --impl reference times the reference's own CPU implementation
 (cpu_reference of vulkan-runtime/tests/test_q4gemm.cpp:102-119, compiled from
@@ -844,7 +846,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "lora", "tiny", "mlp70b", "lora_backward"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "lora", "tiny", "mlp70b", "lora_backward", "sgemm"],
                     default="decode")
     ap.add_argument("--no-secondary", action="store_true", help="skip the prefill/lora figures")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -936,6 +938,14 @@ def main() -> None:
         line.update({"value": big["GB/s"], "unit": "GB/s", "ms_per_step": big["us"] / 1e3, "scaling": "weak",
                      "dtype": "f32 (3xTF32-accurate tcgen05)",
                      "config": {"workload": "LoRA backward (T, G, dB, dA) at configs[4]'s size, rank 16",
+                                "l2": "L2 flushed (256 MB write) before every step", "parallelism": "single GPU"},
+                     "detail": r})
+    elif args.workload == "sgemm":
+        r = sgemm_gpu(args, dist, torch, session)
+        big = r["4096^3"]
+        line.update({"value": big["TFLOP/s"], "unit": "TFLOP/s", "ms_per_step": big["us"] / 1e3, "scaling": "weak",
+                     "dtype": "f32 (3xTF32-accurate tcgen05)",
+                     "config": {"workload": "spaceslug_sgemm_device, M = N = K = 4096 (split passes included)",
                                 "l2": "L2 flushed (256 MB write) before every step", "parallelism": "single GPU"},
                      "detail": r})
     else:
