@@ -16,7 +16,7 @@
 //     signals its dependents at once: the next layer's CTAs can stream their
 //     weights while this layer computes.  X (after the wait) is one TMA box
 //     per row.
-//   * 8 warps take the weight boxes round robin.  Lane (cq = lane/4, j =
+//   * The warps take the weight boxes round robin.  Lane (cq = lane/4, j =
 //     lane%4) handles columns cq, cq+8, cq+16, cq+24 and, in each 32-k scale
 //     group, the 8 k of word j: the weights are unpacked exactly (2^23 magic
 //     number), scaled in fp32 (the reference's single rounding) and multiplied
@@ -50,8 +50,12 @@ constexpr int kTSlot = 32;       // rows (columns of W) per shared-memory box sl
 constexpr int kTBoxK = 256;      // k per weight box: one 128-byte row (32 words) per column
 constexpr int kTScaleBoxG = 32;  // scale groups per scale box: one 128-byte row per column
 
-// 16 warps per CTA (latency hiding; at M <= 2 within 64 registers, so two
-// CTAs share an SM).
+// Warps per CTA: 8 on the fp32 path (M <= 3; each warp takes two or more
+// weight boxes and has up to 128 registers, enough independent work to hide
+// latency: 4.36 / 5.36 / 7.81 us per layer at M = 1 / 2 / 3 against 4.50 /
+// 5.61 / 8.08 with 16 warps and 4.61 / 5.78 with 4), 16 on the mma path (its
+// X conversion spreads each row over 512 threads).  At M <= 2 two CTAs share
+// an SM.
 template <int M>
 struct TileCfg {
     // M >= 4 multiplies on the tensor cores with mma.sync (see below): its
@@ -62,13 +66,13 @@ struct TileCfg {
     // against 8.93 us per layer there, and M = 3 stays on the fp32 path
     // (8.08 us).
     static constexpr bool kMma = M >= 4;
-    static constexpr int kWarps = 16;
+    static constexpr int kWarps = M <= 3 ? 8 : 16;
     static constexpr int kThreads = kWarps * 32;
     // X conversion of the mma path: float4 per thread and row (M * kslice <= 32768)
     static constexpr int kConvPerRow = (16 + M - 1) / M;
 };
 
-__host__ __device__ inline int tile_warps(int) { return 16; }
+__host__ __device__ inline int tile_warps(int M) { return M <= 3 ? 8 : 16; }
 
 // Test hook (gemv_tile_set_wait_test): when set, warp 0 of every CTA also
 // waits for a second phase of its first weight barrier, which nothing arms,
