@@ -127,16 +127,18 @@ import sys, time, pynvml
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
 print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
-i, power = 0, 0
-while True:
+i, power, errors = 0, 0, 0
+while errors < 2000:  # a transient NVML error (another client polling, say) skips one poll
     t = time.time_ns()
     try:
         if i % 8 == 0:
             power = pynvml.nvmlDeviceGetPowerUsage(h)
         print(t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
               pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), power, flush=True)
+        errors = 0
     except pynvml.NVMLError:
-        break
+        errors += 1
+        time.sleep(0.001)
     i += 1
     time.sleep(0.0002)
 """
@@ -205,10 +207,12 @@ class ClockSampler:
         if not samples:
             # a short region can fall between two polls: take the polls that
             # bracket it (the last one before it and the first one after it)
-            before = [e for e in every if e[0] < self.t0 and self.t0 - e[0] < 50_000_000]
-            after = [e for e in every if e[0] > t1 and e[0] - t1 < 50_000_000]
+            before = [e for e in every if e[0] < self.t0 and self.t0 - e[0] < 1_000_000_000]
+            after = [e for e in every if e[0] > t1 and e[0] - t1 < 1_000_000_000]
             samples = [e[1:] for e in before[-1:] + after[:1]]
-            window = f"the polls bracketing the {(t1 - self.t0) / 1e6:.1f} ms timed region (none fell inside)"
+            gap = max([(self.t0 - e[0]) / 1e6 for e in before[-1:]] + [(e[0] - t1) / 1e6 for e in after[:1]] + [0.0])
+            window = (f"the polls bracketing the {(t1 - self.t0) / 1e6:.1f} ms timed region (none fell inside; "
+                      f"the farther one {gap:.1f} ms away)")
         if not samples:
             return {"unavailable": "no NVML samples in or around the timed region"}
         reasons = sorted({name for _, r, _ in samples for name, bit in self.REASONS if r & bit})
