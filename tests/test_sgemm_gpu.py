@@ -93,9 +93,10 @@ def test_accuracy_is_fp32_level(session, cuda, k):
     assert abs(float(np.mean((c - ref) * np.sign(ref)))) < 2e-6 * np.sqrt(k)  # no pull toward zero
 
 
-@pytest.mark.parametrize("m,n,k", [(2048, 2048, 8192), (2304, 2560, 992)])
+@pytest.mark.parametrize("m,n,k", [(2048, 2048, 8192), (2304, 2560, 992), (4096, 4096, 1024)])
 def test_pair_tiles_accuracy(session, cuda, m, n, k):
-    # problems this large run on CTA pairs (cta_group::2, 256 x 256 tiles of C):
+    # problems this large run on CTA pairs (cta_group::2, 256 x 256 tiles of C;
+    # 4096 x 4096 gives most pairs four tiles):
     # the bars of the single-CTA accuracy test above (normwise near fp32
     # rounding, no bias growing with K) and the reference's elementwise 1e-3
     rng = np.random.default_rng(m + k)
