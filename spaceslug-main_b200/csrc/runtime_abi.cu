@@ -331,11 +331,6 @@ void encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
     if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
 }
 
-// fp32 GEMM C[m x n] (row pitch ldc) = alpha * op(A) op(B) on the tcgen05
-// tensor cores (3xTF32, sgemm_tc.cu).  op(A) is [m x k]: A row-major [m][k]
-// with row pitch lda, or with trans_a A given as [k][m]; op(B) is [k x n]: B
-// row-major [k][n] with row pitch ldb, or with trans_b B given as [n][k].  The
-// operands' TF32 hi / lo planes live in stream-ordered scratch.
 // Co-resident clusters of the pair SGEMM on the current device (cached).
 int sgemm_pairs_on_device() {
     static std::atomic<int> cache[64];
@@ -360,6 +355,11 @@ bool sgemm_use_pair(int m, int n, int sm_count, int pairs) {
     return pair_waves * 1548 < single_waves * 1250;
 }
 
+// fp32 GEMM C[m x n] (row pitch ldc) = alpha * op(A) op(B) on the tcgen05
+// tensor cores (3xTF32, sgemm_tc.cu).  op(A) is [m x k]: A row-major [m][k]
+// with row pitch lda, or with trans_a A given as [k][m]; op(B) is [k x n]: B
+// row-major [k][n] with row pitch ldb, or with trans_b B given as [n][k].  The
+// operands' TF32 hi / lo planes live in stream-ordered scratch.
 void run_sgemm(const float* a, long long lda, bool trans_a, const float* b, long long ldb, bool trans_b, float* cm,
                long long ldc, int m, int n, int k, float alpha, int* status, cudaStream_t stream) {
     int dev = 0, sms = 0;
